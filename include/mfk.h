@@ -1,0 +1,154 @@
+/* mfk.h — the C ABI of the B200 (sm_100a) kernels for Mensurflow's dense fp32 contraction path.
+ *
+ * This is the drop-in boundary. The reference's CUDA backend registers a C++ KernelFn per
+ * (op, device, dtype) with its dispatcher (src/core/dispatcher.hpp:199 `KernelFn`, :249
+ * `register_kernel`; src/backends/cuda/backend.cpp:231-238 `register_kernels`). A backend
+ * adapter unpacks `OpArgs` (dispatcher.hpp:164-197) into the plain descriptors below and calls
+ * these functions; nothing here uses C++ or torch types.
+ *
+ * Conventions
+ *   - All pointers are device pointers on the current CUDA device, except where a comment says
+ *     "host". `stream` is a cudaStream_t (NULL = the legacy default stream).
+ *   - Calls are asynchronous on `stream`, like every kernel launch of the reference's CUDA
+ *     backend (include/mensurflow/ops/blas.hpp:1-3).
+ *   - Return value: MFK_OK, or an mfk_status error code (text: mfk_status_string). Argument
+ *     errors are reported before anything is launched. The reference's adapters turn a non-zero
+ *     status into std::runtime_error / std::invalid_argument (src/backends/cuda/backend.cpp:22-34).
+ *   - Faults inside a kernel (a bounded pipeline wait that gave up) are recorded in a per-device
+ *     error word, read with mfk_device_status().
+ */
+#ifndef MFK_H
+#define MFK_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum mfk_status {
+    MFK_OK = 0,
+    MFK_ERR_INVALID_ARGUMENT = 1, /* a shape, stride, pointer or enum value is not valid */
+    MFK_ERR_UNSUPPORTED = 2,      /* valid, but beyond what this build handles */
+    MFK_ERR_CUDA = 3,             /* a CUDA runtime call failed (launch, attribute, copy) */
+    MFK_ERR_OUT_OF_MEMORY = 4,    /* the stream-ordered workspace could not be allocated */
+    MFK_ERR_NO_DEVICE = 5,        /* no sm_100 device is current */
+    MFK_ERR_DEVICE_FAULT = 6      /* a kernel recorded a fault (see mfk_device_status) */
+} mfk_status;
+
+/* Epilogue activation, applied after alpha/beta/bias: relu (elementwise.hpp:56), exact GELU
+ * 0.5*v*erfc(-v/sqrt 2) or its tanh form (elementwise.hpp:62, approximate=true). */
+typedef enum mfk_activation {
+    MFK_ACT_NONE = 0,
+    MFK_ACT_RELU = 1,
+    MFK_ACT_GELU = 2,
+    MFK_ACT_GELU_TANH = 3
+} mfk_activation;
+
+/* Tensor-core arithmetic for the fp32 GEMMs. 3xTF32 splits each operand into tf32 hi + lo and
+ * accumulates three products in fp32 (fp32-faithful: |C - C_ref| <= 1e-5 * (|A||B|)_ij + 1e-6);
+ * 1xTF32 is one tf32 product per term (<= 2e-3 * (|A||B|)_ij). */
+typedef enum mfk_precision {
+    MFK_PRECISION_DEFAULT = -1, /* the process-wide setting (mfk_set_default_precision) */
+    MFK_PRECISION_3XTF32 = 0,
+    MFK_PRECISION_1XTF32 = 1
+} mfk_precision;
+
+/* Bits of the device error word. */
+#define MFK_DEVERR_PRODUCER_TIMEOUT 0x1u
+#define MFK_DEVERR_MMA_TIMEOUT 0x2u
+#define MFK_DEVERR_EPILOGUE_TIMEOUT 0x4u
+
+/* One GEMM: c = act(alpha * op(A) op(B) + beta * c_in + bias).
+ * op(A) is m x k with element (i, p) at a[i*a_rs + p*a_cs]; op(B) is k x n with element (p, j)
+ * at b[p*b_rs + j*b_cs]. A transpose is a swap of the two strides, exactly as the reference's
+ * strided kernels take it (cpu::BatchedGemm rsa/csa/rsb/csb, gemm_batched.hpp:21-37;
+ * matmul_f32_packed_strided, gemm_packed.hpp:138). c_in is read only when beta != 0 (it may be
+ * c itself), with element (i, j) at c_in[i*c_in_rs + j*c_in_cs] (a row broadcast has
+ * c_in_rs = 0). c is row-major with row stride ldc >= n. bias (optional) has n entries. */
+typedef struct mfk_gemm_desc {
+    const float* a;
+    int64_t a_rs, a_cs;
+    const float* b;
+    int64_t b_rs, b_cs;
+    const float* c_in;
+    int64_t c_in_rs, c_in_cs;
+    float* c;
+    int64_t ldc;
+    int64_t m, n, k;
+    float alpha, beta;
+    const float* bias;
+    int32_t activation; /* mfk_activation */
+    int32_t precision;  /* mfk_precision */
+} mfk_gemm_desc;
+
+/* The batch of a strided-batched GEMM. Matrix i of op(A) starts at a + a_offsets[i] and of op(B)
+ * at b + b_offsets[i] (host arrays of `batch` element offsets, the reference's odometer walk in
+ * gemm_batched_kernel, src/backends/cpu/backend.cpp:251-270). When an offsets pointer is NULL the
+ * matrices are evenly spaced by a_stride / b_stride elements (0 = one matrix shared by all).
+ * c_in of matrix i starts at c_in + i*c_in_stride (0 = shared), c of matrix i at c + i*c_stride. */
+typedef struct mfk_batch_desc {
+    int64_t batch;
+    const int64_t* a_offsets; /* host, may be NULL */
+    const int64_t* b_offsets; /* host, may be NULL */
+    int64_t a_stride, b_stride;
+    int64_t c_in_stride;
+    int64_t c_stride;
+} mfk_batch_desc;
+
+/* gemm / matmul on CUDA in one call. Replaces the OpId::Matmul kernel (CPU adapter:
+ * src/backends/cpu/backend.cpp:131-164) and the mul / scal / add / bias_add dispatches that
+ * mensurflow::gemm and bias_add chain after it (src/ops/blas.cpp:234-262,
+ * src/ops/elementwise.cpp:251-284). matmul is alpha = 1, beta = 0, no bias, no activation. */
+int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream);
+
+/* gemm_strided_batched on CUDA. Replaces the OpId::GemmBatched kernel (CPU adapter:
+ * src/backends/cpu/backend.cpp:239-293 -> cpu::gemm_batched_f32_parallel, gemm_batched.cpp:58)
+ * and so both batched GEMMs of attention (src/ops/attention.cpp:69, :97). desc->m/n/k describe
+ * one matrix; desc->a and desc->b are the base pointers the batch offsets apply to. */
+int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc* batch,
+                                 void* stream);
+
+/* gemv: y = alpha * op(A) x + beta * y0 with A row-major [rows, cols] (row stride lda), op(A) = A
+ * or its transpose, sums accumulated in double. Replaces the OpId::Gemv kernel (CPU adapter:
+ * src/backends/cpu/backend.cpp:120-125 -> cpu::gemv_f32, src/backends/cpu/ops/blas/blas.cpp:66).
+ * y0 is read only when beta != 0. incx is x's element stride. */
+int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_t transpose,
+                 const float* x, int64_t incx, float alpha, float beta, const float* y0, float* y,
+                 void* stream);
+
+/* matvec: y = A x, A [m, k] contiguous. Replaces the OpId::Matvec kernel (cpu::matvec_f32,
+ * src/backends/cpu/ops/blas/blas.cpp:55). */
+int mfk_matvec_f32(const float* a, int64_t m, int64_t k, const float* x, float* y, void* stream);
+
+/* out = act(x + bias) over a contiguous [rows, cols] x; bias (cols entries) may be NULL, so this
+ * is also the standalone relu / gelu. Replaces the OpId::BiasAdd, Relu and Gelu kernels (CPU
+ * adapters: src/backends/cpu/backend.cpp:762-767 bias_add_kernel, :658 gelu_kernel). out may be
+ * x. */
+int mfk_bias_act_f32(const float* x, const float* bias, float* out, int64_t rows, int64_t cols,
+                     int32_t activation, void* stream);
+
+/* Process-wide precision used when a descriptor says MFK_PRECISION_DEFAULT. The reference's
+ * public signatures have no precision argument, so its adapters leave the default in place. */
+int mfk_set_default_precision(int32_t precision);
+int32_t mfk_get_default_precision(void);
+
+/* Reads (and clears when `clear` != 0) the error word of the current device after waiting for the
+ * device to finish its work. *bits receives MFK_DEVERR_* bits; returns MFK_OK, or
+ * MFK_ERR_DEVICE_FAULT when bits were set, or MFK_ERR_CUDA. */
+int mfk_device_status(uint32_t* bits, int32_t clear);
+
+/* Human-readable text of a status code (static storage). */
+const char* mfk_status_string(int32_t status);
+
+/* Text of the last CUDA error seen by this thread inside the library ("" when none). */
+const char* mfk_last_cuda_error(void);
+
+/* ABI version: (major << 16) | minor. */
+int32_t mfk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MFK_H */

@@ -1,0 +1,26 @@
+"""mensurflow_b200 — B200 (sm_100a) kernels for Mensurflow's dense fp32 contraction path.
+
+The kernels live in ``lib/libmfkernels.so`` behind the C ABI of ``include/mfk.h``; ``ops``
+mirrors the reference's op API over torch CUDA tensors, ``sharded`` splits a GEMM over ranks.
+"""
+from ._lib import MfkError, build  # noqa: F401
+from .ops import (  # noqa: F401
+    bias_add,
+    device_status,
+    gelu,
+    gemm,
+    gemm_strided_batched,
+    gemv,
+    get_default_precision,
+    linear,
+    matmul,
+    matvec,
+    relu,
+    set_default_precision,
+)
+
+__all__ = [
+    "MfkError", "build", "bias_add", "device_status", "gelu", "gemm", "gemm_strided_batched",
+    "gemv", "get_default_precision", "linear", "matmul", "matvec", "relu",
+    "set_default_precision",
+]

@@ -1,0 +1,373 @@
+// The tcgen05 tensor-core GEMM for fp32 data: C = act(alpha * op(A) op(B) + beta * C_in + bias).
+//
+// Replaces the reference's CPU packed GEMM (src/backends/cpu/ops/gemm/gemm_packed.cpp:1505
+// gemm_parallel, :313 kernel_6x16) plus the alpha/beta/bias/activation passes that follow it
+// (src/ops/blas.cpp:246-260, gemm_batched.cpp:12-28 finish_matrix, elementwise.cpp:128 bias_add).
+//
+// Design (sm_100a):
+//  * persistent: one CTA per SM walks output tiles (BM x BN) in a grouped raster order so the
+//    A and B panels in flight stay in L2;
+//  * warp-specialised, 256 threads: warp 0 issues TMA loads into an mbarrier ring of STAGES
+//    shared-memory stages; warp 1 owns TMEM and one lane issues tcgen05.mma; warps 4-7 are the
+//    epilogue (TMEM -> registers -> alpha/beta/bias/activation -> global);
+//  * operands are K-major fp32 tiles of 32 elements (128 B) per row, SWIZZLE_128B, read by the
+//    MMA through shared-memory descriptors; kind::tf32 with an fp32 accumulator in TMEM;
+//  * 3xTF32 (SPLIT3): each operand arrives as a (hi, lo) pair with hi = tf32(x), lo = tf32(x-hi)
+//    and three MMAs per k-step accumulate lo*hi + hi*lo + hi*hi (Ootomo & Yokota 2022; the
+//    split-precision "3xTF32" scheme); 1xTF32 issues one MMA per k-step;
+//  * two TMEM accumulators, so the epilogue of tile i overlaps the main loop of tile i+1.
+#pragma once
+
+#include "mfk_ptx.cuh"
+
+namespace mfk {
+
+constexpr int kBM = 128;          // rows of a tile = TMEM lanes
+constexpr int kBK = 32;           // fp32 depth per stage: one 128-byte swizzle row
+constexpr int kGemmThreads = 256;
+constexpr int kEpiWarp0 = 4;      // warps 4..7 are the epilogue warpgroup
+
+enum : unsigned int {
+    kErrProducerWait = 1u << 0,
+    kErrMmaWait = 1u << 1,
+    kErrEpilogueWait = 1u << 2,
+};
+
+enum Activation : int { kActNone = 0, kActRelu = 1, kActGelu = 2, kActGeluTanh = 3 };
+
+struct GemmArgs {
+    int m, n, k;
+    int num_kb;        // ceil(k / kBK)
+    int batch;
+    int tiles_m, tiles_n;
+    int group_m;       // M-tiles per raster group
+    long long num_tiles;
+    int a_batch_bcast; // 1: every matrix uses A's matrix 0
+    int b_batch_bcast;
+    float alpha, beta;
+    const float* c_in;
+    long long c_in_rs, c_in_cs, c_in_bs;
+    float* c;
+    long long ldc, c_bs;
+    const float* bias;
+    int act;
+};
+
+template <int BN, bool SPLIT3>
+struct TcConfig {
+    static constexpr int kABytes = kBM * kBK * 4;
+    static constexpr int kBBytes = BN * kBK * 4;
+    static constexpr int kOps = SPLIT3 ? 2 : 1;
+    static constexpr int kStageBytes = kOps * (kABytes + kBBytes);
+    static constexpr int kStages = (200 * 1024) / kStageBytes;
+    static constexpr int kAccStages = 2;
+    static constexpr int kTmemCols = (kAccStages * BN <= 32)    ? 32
+                                     : (kAccStages * BN <= 64)  ? 64
+                                     : (kAccStages * BN <= 128) ? 128
+                                     : (kAccStages * BN <= 256) ? 256
+                                                                : 512;
+    // stages (1024-aligned), then barriers and the TMEM address holder
+    static constexpr int kBarrierBytes = 256;
+    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+    static_assert(kAccStages * BN <= 512, "accumulators exceed TMEM");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be 32..256, multiple of 32");
+    static_assert(kStages >= 2, "need at least two stages");
+};
+
+struct TileCoord {
+    int b, tm, tn;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, long long t) {
+    const long long per_batch = static_cast<long long>(g.tiles_m) * g.tiles_n;
+    TileCoord c;
+    c.b = static_cast<int>(t / per_batch);
+    const int r = static_cast<int>(t - static_cast<long long>(c.b) * per_batch);
+    const int group_size = g.group_m * g.tiles_n;
+    const int grp = r / group_size;
+    const int first_m = grp * g.group_m;
+    const int gm = min(g.tiles_m - first_m, g.group_m);
+    const int in_group = r - grp * group_size;
+    c.tm = first_m + in_group % gm;
+    c.tn = in_group / gm;
+    return c;
+}
+
+__device__ __forceinline__ float gelu_exact(float value) {
+    if (isinf(value)) return value < 0.0f ? -0.0f : value;
+    const double v = value;
+    return static_cast<float>(0.5 * v * erfc(-v * 0.70710678118654752440));
+}
+
+__device__ __forceinline__ float gelu_tanh(float value) {
+    if (isinf(value)) return value < 0.0f ? -0.0f : value;
+    const double v = value;
+    const double u = 0.79788456080286535588 * v * (1.0 + 0.044715 * v * v);
+    const double z = 2.0 * u;
+    const double s = z >= 0.0 ? 1.0 / (1.0 + exp(-z)) : exp(z) / (1.0 + exp(z));
+    return static_cast<float>(v * s);
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+    switch (act) {
+    case kActRelu:
+        return v < 0.0f ? 0.0f : v;
+    case kActGelu:
+        return gelu_exact(v);
+    case kActGeluTanh:
+        return gelu_tanh(v);
+    default:
+        return v;
+    }
+}
+
+// The reference composes alpha*AB (mul), + beta*C (scal then add) and + bias (bias_add) as
+// separate fp32 operations; each rounding step is kept (no contraction into an FMA).
+__device__ __forceinline__ float epilogue_value(float acc, float alpha, float beta, float cin,
+                                                bool has_cin, float bias, bool has_bias,
+                                                int act) {
+    float v = alpha == 1.0f ? acc : __fmul_rn(alpha, acc);
+    if (has_cin) v = __fadd_rn(v, __fmul_rn(beta, cin));
+    if (has_bias) v = __fadd_rn(v, bias);
+    return apply_act(v, act);
+}
+
+template <int BN, bool SPLIT3>
+__device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap* tmA0,
+                                            const CUtensorMap* tmA1, const CUtensorMap* tmB0,
+                                            const CUtensorMap* tmB1, uint8_t* stages,
+                                            uint64_t* full, uint64_t* empty) {
+    using C = TcConfig<BN, SPLIT3>;
+    const uint64_t pol_a = l2_policy_evict_last();
+    const uint64_t pol_b = l2_policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
+        const TileCoord tc = tile_coord(g, t);
+        const int za = g.a_batch_bcast ? 0 : tc.b;
+        const int zb = g.b_batch_bcast ? 0 : tc.b;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, kErrProducerWait)) return;
+            uint8_t* s = stages + stage * C::kStageBytes;
+            mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+            const int kx = kb * kBK;
+            tma_load_3d(s, tmA0, &full[stage], kx, tc.tm * kBM, za, pol_a);
+            tma_load_3d(s + C::kABytes, tmB0, &full[stage], kx, tc.tn * BN, zb, pol_b);
+            if constexpr (SPLIT3) {
+                tma_load_3d(s + C::kABytes + C::kBBytes, tmA1, &full[stage], kx, tc.tm * kBM, za,
+                            pol_a);
+                tma_load_3d(s + 2 * C::kABytes + C::kBBytes, tmB1, &full[stage], kx, tc.tn * BN,
+                            zb, pol_b);
+            }
+            if (++stage == C::kStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+}
+
+template <int BN, bool SPLIT3>
+__device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, uint8_t* stages,
+                                       uint64_t* full, uint64_t* empty, uint64_t* acc_full,
+                                       uint64_t* acc_empty) {
+    using C = TcConfig<BN, SPLIT3>;
+    constexpr uint32_t idesc = idesc_tf32(kBM, BN, false, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t stage0 = smem_u32(stages);
+    for (long long t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kErrMmaWait)) return;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+            if (!mbar_wait(&full[stage], phase, kErrMmaWait)) return;
+            tc_fence_after();
+            const uint32_t a_hi = stage0 + stage * C::kStageBytes;
+            const uint32_t b_hi = a_hi + C::kABytes;
+            const uint32_t a_lo = b_hi + C::kBBytes;
+            const uint32_t b_lo = a_lo + C::kABytes;
+#pragma unroll
+            for (int ks = 0; ks < kBK / 8; ++ks) {
+                const uint32_t koff = ks * 32;  // 8 tf32 = 32 bytes along the swizzled row
+                const uint64_t dah = smem_desc(a_hi + koff, 16, 1024, kSwizzle128B);
+                const uint64_t dbh = smem_desc(b_hi + koff, 16, 1024, kSwizzle128B);
+                const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
+                if constexpr (SPLIT3) {
+                    const uint64_t dal = smem_desc(a_lo + koff, 16, 1024, kSwizzle128B);
+                    const uint64_t dbl = smem_desc(b_lo + koff, 16, 1024, kSwizzle128B);
+                    mma_tf32(d_tmem, dal, dbh, idesc, accumulate);
+                    mma_tf32(d_tmem, dah, dbl, idesc, 1u);
+                    mma_tf32(d_tmem, dah, dbh, idesc, 1u);
+                } else {
+                    mma_tf32(d_tmem, dah, dbh, idesc, accumulate);
+                }
+            }
+            mma_commit(&empty[stage]);
+            if (++stage == C::kStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        mma_commit(&acc_full[acc]);
+        if (++acc == C::kAccStages) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+}
+
+template <int BN, bool SPLIT3>
+__device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_base,
+                                            uint64_t* acc_full, uint64_t* acc_empty) {
+    using C = TcConfig<BN, SPLIT3>;
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int ew = warp - kEpiWarp0;  // TMEM lane quarter this warp may access
+    const bool has_cin = g.c_in != nullptr && g.beta != 0.0f;
+    const bool has_bias = g.bias != nullptr;
+    const bool vec_out = (g.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0) &&
+                         (g.c_bs % 4 == 0);
+    const bool vec_cin = has_cin && g.c_in_cs == 1 && (g.c_in_rs % 4 == 0) &&
+                         (g.c_in_bs % 4 == 0) &&
+                         ((reinterpret_cast<uintptr_t>(g.c_in) & 15) == 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (long long t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
+        const TileCoord tc = tile_coord(g, t);
+        if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) return;
+        tc_fence_after();
+        const int row = tc.tm * kBM + ew * 32 + lane;
+        const bool row_ok = row < g.m;
+        float* crow = g.c + static_cast<long long>(tc.b) * g.c_bs + static_cast<long long>(row) * g.ldc;
+        const float* cin_row =
+            has_cin ? g.c_in + static_cast<long long>(tc.b) * g.c_in_bs +
+                          static_cast<long long>(row) * g.c_in_rs
+                    : nullptr;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + c0);
+            tmem_ld_32x32b_x32(taddr, r);
+            const int col0 = tc.tn * BN + c0;
+            if (!row_ok || col0 >= g.n) continue;
+            if (col0 + 32 <= g.n && vec_out && (!has_cin || vec_cin)) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    float4 cin4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (has_cin) cin4 = *reinterpret_cast<const float4*>(cin_row + col0 + j);
+                    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (has_bias) {
+                        b4.x = g.bias[col0 + j];
+                        b4.y = g.bias[col0 + j + 1];
+                        b4.z = g.bias[col0 + j + 2];
+                        b4.w = g.bias[col0 + j + 3];
+                    }
+                    float4 o;
+                    o.x = epilogue_value(__uint_as_float(r[j]), g.alpha, g.beta, cin4.x, has_cin,
+                                         b4.x, has_bias, g.act);
+                    o.y = epilogue_value(__uint_as_float(r[j + 1]), g.alpha, g.beta, cin4.y,
+                                         has_cin, b4.y, has_bias, g.act);
+                    o.z = epilogue_value(__uint_as_float(r[j + 2]), g.alpha, g.beta, cin4.z,
+                                         has_cin, b4.z, has_bias, g.act);
+                    o.w = epilogue_value(__uint_as_float(r[j + 3]), g.alpha, g.beta, cin4.w,
+                                         has_cin, b4.w, has_bias, g.act);
+                    *reinterpret_cast<float4*>(crow + col0 + j) = o;
+                }
+            } else {
+#pragma unroll 4
+                for (int j = 0; j < 32; ++j) {
+                    const int col = col0 + j;
+                    if (col < g.n) {
+                        const float cin =
+                            has_cin ? cin_row[static_cast<long long>(col) * g.c_in_cs] : 0.0f;
+                        const float bv = has_bias ? g.bias[col] : 0.0f;
+                        crow[col] = epilogue_value(__uint_as_float(r[j]), g.alpha, g.beta, cin,
+                                                   has_cin, bv, has_bias, g.act);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (++acc == C::kAccStages) {
+            acc = 0;
+            acc_phase ^= 1u;
+        }
+    }
+}
+
+template <int BN, bool SPLIT3>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0,
+                   const __grid_constant__ CUtensorMap tmA1,
+                   const __grid_constant__ CUtensorMap tmB0,
+                   const __grid_constant__ CUtensorMap tmB1, const GemmArgs g) {
+    using C = TcConfig<BN, SPLIT3>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* stages = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + C::kStages * C::kStageBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = full + C::kStages;
+    uint64_t* acc_full = empty + C::kStages;
+    uint64_t* acc_empty = acc_full + C::kAccStages;
+    uint64_t* drain = acc_empty + C::kAccStages;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < C::kAccStages; ++s) {
+            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_empty[s], 4);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA0);
+        tma_prefetch_desc(&tmB0);
+        if constexpr (SPLIT3) {
+            tma_prefetch_desc(&tmA1);
+            tma_prefetch_desc(&tmB1);
+        }
+    }
+    if (warp == 1) tmem_alloc(tmem_holder, C::kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) tc_producer<BN, SPLIT3>(g, &tmA0, &tmA1, &tmB0, &tmB1, stages, full, empty);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            tc_mma<BN, SPLIT3>(g, tmem_base, stages, full, empty, acc_full, acc_empty);
+            // Every MMA issued above must finish before TMEM is released, also on an error exit.
+            mma_commit(drain);
+            mbar_wait(drain, 0, kErrMmaWait);
+        }
+        __syncwarp();
+    } else if (warp >= kEpiWarp0) {
+        tc_epilogue<BN, SPLIT3>(g, tmem_base, acc_full, acc_empty);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+}  // namespace mfk

@@ -1,0 +1,496 @@
+// The C ABI declared in include/mfk.h: argument checks, operand staging decisions, TMA tensor
+// maps, the stream-ordered workspace and the kernel launches. One translation unit holds every
+// kernel of the library (the device error word is shared without relocatable device code).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "mfk.h"
+
+#include "gemm_tc.cuh"
+#include "prep.cuh"
+#include "simt.cuh"
+
+namespace {
+
+using mfk::GemmArgs;
+
+thread_local std::string t_cuda_error;
+std::atomic<int> g_default_precision{MFK_PRECISION_3XTF32};
+
+constexpr int kMaxDevices = 64;
+
+int cuda_fail(cudaError_t e, const char* what) {
+    t_cuda_error = std::string(what) + ": " + cudaGetErrorString(e);
+    if (e == cudaErrorMemoryAllocation) return MFK_ERR_OUT_OF_MEMORY;
+    return MFK_ERR_CUDA;
+}
+
+#define MFK_CUDA(call)                                      \
+    do {                                                    \
+        const cudaError_t e_ = (call);                      \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+    } while (0)
+
+struct DeviceInfo {
+    bool ready = false;
+    int sm_count = 0;
+    int major = 0, minor = 0;
+    bool smem_set[8] = {};
+};
+
+std::mutex g_mutex;
+DeviceInfo g_devices[kMaxDevices];
+
+int current_device(int* dev, DeviceInfo** info) {
+    MFK_CUDA(cudaGetDevice(dev));
+    if (*dev < 0 || *dev >= kMaxDevices) return MFK_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    DeviceInfo& d = g_devices[*dev];
+    if (!d.ready) {
+        MFK_CUDA(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, *dev));
+        MFK_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, *dev));
+        MFK_CUDA(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, *dev));
+        // Stream-ordered workspace: keep freed blocks in the pool instead of returning them to
+        // the driver after every call.
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, *dev) == cudaSuccess) {
+            uint64_t threshold = UINT64_MAX;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+        }
+        d.ready = true;
+    }
+    *info = &d;
+    if (d.major != 10) return MFK_ERR_NO_DEVICE;  // sm_100a code only
+    return MFK_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// A K-major operand view for TMA: `rows` rows of `depth` fp32 values, row r of matrix z at
+// base + z*bstride + r*rstride (elements). Box: 32 values (128 B, SWIZZLE_128B) x box_rows.
+bool make_kmajor_map(CUtensorMap* map, const float* base, int64_t depth, int64_t rows,
+                     int64_t nmat, int64_t rstride, int64_t bstride, int box_rows) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    if (nmat == 1) bstride = rstride * std::max<int64_t>(rows, 1);
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(depth), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(nmat)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(rstride) * 4,
+                             static_cast<cuuint64_t>(bstride) * 4};
+    cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                          const_cast<float*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Batch placement of one operand: matrix z starts at shift + z*stride elements, or at
+// offsets[z] when the caller's offsets are not evenly spaced.
+struct BatchLayout {
+    const int64_t* offsets = nullptr;  // host, uneven spacing only
+    int64_t shift = 0;
+    int64_t stride = 0;
+};
+
+BatchLayout batch_layout(const int64_t* offsets, int64_t stride, int64_t batch) {
+    BatchLayout l;
+    if (offsets == nullptr) {
+        l.stride = stride;
+        return l;
+    }
+    l.shift = offsets[0];
+    l.stride = batch > 1 ? offsets[1] - offsets[0] : 0;
+    for (int64_t i = 1; i < batch; ++i) {
+        if (offsets[i] - offsets[i - 1] != l.stride) {
+            l.offsets = offsets;
+            l.shift = 0;
+            l.stride = 0;
+            break;
+        }
+    }
+    return l;
+}
+
+// One GEMM operand as K-major rows: row r (of R), depth p (of K) at
+// ptr + off(z) + r*rs + p*cs.
+struct Operand {
+    const float* ptr;
+    int64_t rs, cs;
+    int64_t rows;
+    BatchLayout bl;
+    bool direct = false;      // TMA straight from the caller's memory
+    bool bcast = false;       // direct with one shared matrix
+    float* hi = nullptr;      // packed copies (workspace)
+    float* lo = nullptr;
+    int64_t* dev_offsets = nullptr;
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Whether TMA can read the operand where it lies (1xTF32 only: 3xTF32 needs the split copy).
+bool can_read_direct(const Operand& o, int64_t k, bool split3) {
+    if (split3 || o.cs != 1 || o.bl.offsets != nullptr) return false;
+    if (!aligned16(o.ptr) || o.rs <= 0 || (o.rs % 4) != 0 || o.rs < k) return false;
+    if (o.bl.stride < 0 || (o.bl.stride % 4) != 0) return false;
+    if (o.rs >= (int64_t(1) << 37) || o.bl.stride >= (int64_t(1) << 37)) return false;
+    return true;
+}
+
+template <int BN, bool SPLIT3>
+int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+              const CUtensorMap& b1, const GemmArgs& g, DeviceInfo* info, int slot,
+              cudaStream_t stream) {
+    using C = mfk::TcConfig<BN, SPLIT3>;
+    auto kernel = mfk::gemm_tc_kernel<BN, SPLIT3>;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if (!info->smem_set[slot]) {
+            MFK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          C::kSmemBytes));
+            info->smem_set[slot] = true;
+        }
+    }
+    const long long grid = std::min<long long>(g.num_tiles, info->sm_count);
+    kernel<<<static_cast<unsigned>(grid), mfk::kGemmThreads, C::kSmemBytes, stream>>>(a0, a1, b0,
+                                                                                    b1, g);
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+int check_desc(const mfk_gemm_desc* d) {
+    if (d == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    if (d->m < 0 || d->n < 0 || d->k < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (d->activation < MFK_ACT_NONE || d->activation > MFK_ACT_GELU_TANH)
+        return MFK_ERR_INVALID_ARGUMENT;
+    if (d->precision < MFK_PRECISION_DEFAULT || d->precision > MFK_PRECISION_1XTF32)
+        return MFK_ERR_INVALID_ARGUMENT;
+    if (d->m > 0 && d->n > 0) {
+        if (d->c == nullptr || d->ldc < d->n) return MFK_ERR_INVALID_ARGUMENT;
+        if (d->k > 0 && (d->a == nullptr || d->b == nullptr)) return MFK_ERR_INVALID_ARGUMENT;
+        if (d->beta != 0.0f && d->c_in == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    }
+    return MFK_OK;
+}
+
+int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream) {
+    int rc = check_desc(d);
+    if (rc != MFK_OK) return rc;
+    const int64_t batch = bd ? bd->batch : 1;
+    if (batch < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (d->m == 0 || d->n == 0 || batch == 0) return MFK_OK;
+    if (d->m > (int64_t(1) << 31) - 256 || d->n > (int64_t(1) << 31) - 256 ||
+        d->k > (int64_t(1) << 31) - 256 || batch > (int64_t(1) << 31) - 1)
+        return MFK_ERR_UNSUPPORTED;
+
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+
+    const int precision = d->precision == MFK_PRECISION_DEFAULT ? g_default_precision.load()
+                                                                 : d->precision;
+    const bool split3 = precision == MFK_PRECISION_3XTF32;
+
+    GemmArgs g{};
+    g.m = static_cast<int>(d->m);
+    g.n = static_cast<int>(d->n);
+    g.k = static_cast<int>(d->k);
+    g.batch = static_cast<int>(batch);
+    g.alpha = d->alpha;
+    g.beta = d->beta;
+    g.c_in = d->beta != 0.0f ? d->c_in : nullptr;
+    g.c_in_rs = d->c_in_rs;
+    g.c_in_cs = d->c_in_cs;
+    g.c_in_bs = bd ? bd->c_in_stride : 0;
+    g.c = d->c;
+    g.ldc = d->ldc;
+    g.c_bs = bd ? bd->c_stride : 0;
+    g.bias = d->bias;
+    g.act = d->activation;
+
+    if (d->k == 0) {
+        const long long total = static_cast<long long>(batch) * d->m * d->n;
+        const long long blocks = std::min<long long>((total + 255) / 256, 65535LL * 8);
+        mfk::epilogue_only_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(g);
+        MFK_CUDA(cudaGetLastError());
+        return MFK_OK;
+    }
+
+    constexpr int BN = 128;
+    const int64_t Kp = (d->k + mfk::kBK - 1) / mfk::kBK * mfk::kBK;
+
+    Operand A{d->a, d->a_rs, d->a_cs, d->m,
+              batch_layout(bd ? bd->a_offsets : nullptr, bd ? bd->a_stride : 0, batch)};
+    // op(B) element (p, j) at p*b_rs + j*b_cs: as K-major rows over j, rs = b_cs, cs = b_rs.
+    Operand B{d->b, d->b_cs, d->b_rs, d->n,
+              batch_layout(bd ? bd->b_offsets : nullptr, bd ? bd->b_stride : 0, batch)};
+    A.ptr += A.bl.shift;
+    B.ptr += B.bl.shift;
+
+    // Direct TMA reads when the layout allows; the maps are encoded now so that a layout the
+    // driver rejects falls back to packing instead of failing.
+    CUtensorMap ma0, ma1, mb0, mb1;
+    auto direct_map = [&](Operand& o, int box_rows, CUtensorMap* m0, CUtensorMap* m1,
+                          int* bcast) {
+        if (!can_read_direct(o, d->k, split3)) return;
+        *bcast = (o.bl.stride == 0 && batch > 1) ? 1 : 0;
+        const int64_t nmat = *bcast ? 1 : batch;
+        if (make_kmajor_map(m0, o.ptr, d->k, o.rows, nmat, o.rs, o.bl.stride, box_rows)) {
+            *m1 = *m0;
+            o.direct = true;
+        } else {
+            *bcast = 0;
+        }
+    };
+    direct_map(A, mfk::kBM, &ma0, &ma1, &g.a_batch_bcast);
+    direct_map(B, BN, &mb0, &mb1, &g.b_batch_bcast);
+
+    // Workspace: packed operands plus device copies of non-arithmetic offset tables.
+    const int nops = split3 ? 2 : 1;
+    auto packed_elems = [&](const Operand& o) { return o.rows * Kp * batch; };
+    size_t bytes = 0;
+    auto reserve = [&](size_t n) {
+        const size_t off = bytes;
+        bytes += (n + 255) / 256 * 256;
+        return off;
+    };
+    size_t a_off = 0, b_off = 0, ao_off = 0, bo_off = 0;
+    if (!A.direct) a_off = reserve(sizeof(float) * packed_elems(A) * nops);
+    if (!B.direct) b_off = reserve(sizeof(float) * packed_elems(B) * nops);
+    if (!A.direct && A.bl.offsets) ao_off = reserve(sizeof(int64_t) * batch);
+    if (!B.direct && B.bl.offsets) bo_off = reserve(sizeof(int64_t) * batch);
+
+    uint8_t* ws = nullptr;
+    if (bytes > 0) MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream));
+    struct Free {
+        uint8_t* p;
+        cudaStream_t s;
+        ~Free() {
+            if (p) cudaFreeAsync(p, s);
+        }
+    } release{ws, stream};
+
+    auto pack = [&](Operand& o, size_t off, size_t offs_off) -> int {
+        o.hi = reinterpret_cast<float*>(ws + off);
+        o.lo = split3 ? o.hi + packed_elems(o) : nullptr;
+        if (o.bl.offsets) {
+            o.dev_offsets = reinterpret_cast<int64_t*>(ws + offs_off);
+            MFK_CUDA(cudaMemcpyAsync(o.dev_offsets, o.bl.offsets, sizeof(int64_t) * batch,
+                                     cudaMemcpyHostToDevice, stream));
+        }
+        const int mode = split3 ? mfk::kPackSplit : mfk::kPackRound;
+        const int p_contig = (o.cs == 1) || (o.rs != 1 && std::llabs(o.cs) <= std::llabs(o.rs));
+        if (o.rows > 65535LL * 32) return MFK_ERR_UNSUPPORTED;
+        for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
+            const int64_t nz = std::min<int64_t>(65535, batch - z0);
+            dim3 grid(static_cast<unsigned>(Kp / 32), static_cast<unsigned>((o.rows + 31) / 32),
+                      static_cast<unsigned>(nz));
+            const long long* offs =
+                o.dev_offsets ? reinterpret_cast<const long long*>(o.dev_offsets) + z0 : nullptr;
+            const float* src = o.dev_offsets ? o.ptr : o.ptr + z0 * o.bl.stride;
+            const int64_t out_shift = z0 * o.rows * Kp;
+            mfk::pack_kmajor_kernel<<<grid, dim3(32, 8), 0, stream>>>(
+                src, offs, o.bl.stride, o.rs, o.cs, static_cast<int>(o.rows),
+                static_cast<int>(d->k), static_cast<int>(Kp), o.hi + out_shift,
+                o.lo ? o.lo + out_shift : nullptr, mode, p_contig);
+            MFK_CUDA(cudaGetLastError());
+        }
+        return MFK_OK;
+    };
+    if (!A.direct && (rc = pack(A, a_off, ao_off)) != MFK_OK) return rc;
+    if (!B.direct && (rc = pack(B, b_off, bo_off)) != MFK_OK) return rc;
+
+    auto packed_maps = [&](const Operand& o, int box_rows, CUtensorMap* m0, CUtensorMap* m1) {
+        bool ok = make_kmajor_map(m0, o.hi, Kp, o.rows, batch, Kp, o.rows * Kp, box_rows);
+        if (split3) {
+            ok = ok && make_kmajor_map(m1, o.lo, Kp, o.rows, batch, Kp, o.rows * Kp, box_rows);
+        } else {
+            *m1 = *m0;
+        }
+        return ok;
+    };
+    if ((!A.direct && !packed_maps(A, mfk::kBM, &ma0, &ma1)) ||
+        (!B.direct && !packed_maps(B, BN, &mb0, &mb1))) {
+        t_cuda_error = "cuTensorMapEncodeTiled rejected a packed operand";
+        return MFK_ERR_UNSUPPORTED;
+    }
+
+    g.num_kb = static_cast<int>(Kp / mfk::kBK);
+    g.tiles_m = static_cast<int>((d->m + mfk::kBM - 1) / mfk::kBM);
+    g.tiles_n = static_cast<int>((d->n + BN - 1) / BN);
+    g.group_m = 16;
+    g.num_tiles = static_cast<long long>(batch) * g.tiles_m * g.tiles_n;
+
+    if (split3) return launch_tc<BN, true>(ma0, ma1, mb0, mb1, g, info, 0, stream);
+    return launch_tc<BN, false>(ma0, ma1, mb0, mb1, g, info, 1, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream) {
+    return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc* batch,
+                                 void* stream) {
+    if (batch == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    return run_gemm(desc, batch, static_cast<cudaStream_t>(stream));
+}
+
+int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_t transpose,
+                 const float* x, int64_t incx, float alpha, float beta, const float* y0, float* y,
+                 void* stream_) {
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (rows < 0 || cols < 0 || lda < cols || incx < 1) return MFK_ERR_INVALID_ARGUMENT;
+    const int64_t n_out = transpose ? cols : rows;
+    const int64_t n_in = transpose ? rows : cols;
+    if (n_out == 0) return MFK_OK;
+    if (y == nullptr || (beta != 0.0f && y0 == nullptr)) return MFK_ERR_INVALID_ARGUMENT;
+    if (n_in > 0 && (a == nullptr || x == nullptr)) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    if (!transpose) {
+        const bool vec = incx == 1 && lda % 4 == 0 && aligned16(a) && aligned16(x);
+        if (vec) {
+            const int64_t warps = (rows + mfk::kGemvRowsPerWarp - 1) / mfk::kGemvRowsPerWarp;
+            const int64_t blocks = (warps * 32 + mfk::kGemvThreads - 1) / mfk::kGemvThreads;
+            if (blocks > INT32_MAX) return MFK_ERR_UNSUPPORTED;
+            mfk::gemv_n_vec4_kernel<<<static_cast<unsigned>(blocks), mfk::kGemvThreads, 0,
+                                      stream>>>(a, rows, cols, lda, x, alpha, beta, y0, y);
+        } else {
+            const int64_t blocks = (rows * 32 + mfk::kGemvThreads - 1) / mfk::kGemvThreads;
+            if (blocks > INT32_MAX) return MFK_ERR_UNSUPPORTED;
+            mfk::gemv_n_scalar_kernel<<<static_cast<unsigned>(blocks), mfk::kGemvThreads, 0,
+                                        stream>>>(a, rows, cols, lda, x, incx, alpha, beta, y0, y);
+        }
+        MFK_CUDA(cudaGetLastError());
+        return MFK_OK;
+    }
+    const int64_t chunks = std::max<int64_t>(1, (rows + mfk::kGemvTRowsPerChunk - 1) /
+                                                    mfk::kGemvTRowsPerChunk);
+    if (chunks > 65535) return MFK_ERR_UNSUPPORTED;
+    double* partial = nullptr;
+    MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&partial),
+                             sizeof(double) * chunks * std::max<int64_t>(cols, 1), stream));
+    const unsigned bx = static_cast<unsigned>((cols + 255) / 256);
+    if (rows > 0) {
+        mfk::gemv_t_partial_kernel<<<dim3(bx, static_cast<unsigned>(chunks)), 256, 0, stream>>>(
+            a, rows, cols, lda, x, incx, partial);
+    } else {
+        cudaMemsetAsync(partial, 0, sizeof(double) * cols, stream);
+    }
+    mfk::gemv_t_finish_kernel<<<bx, 256, 0, stream>>>(partial, static_cast<int>(chunks), cols,
+                                                      alpha, beta, y0, y);
+    const cudaError_t e = cudaGetLastError();
+    cudaFreeAsync(partial, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_t launch");
+    return MFK_OK;
+}
+
+int mfk_matvec_f32(const float* a, int64_t m, int64_t k, const float* x, float* y, void* stream) {
+    return mfk_gemv_f32(a, m, k, k, 0, x, 1, 1.0f, 0.0f, nullptr, y, stream);
+}
+
+int mfk_bias_act_f32(const float* x, const float* bias, float* out, int64_t rows, int64_t cols,
+                     int32_t activation, void* stream_) {
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (rows < 0 || cols < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (activation < MFK_ACT_NONE || activation > MFK_ACT_GELU_TANH) return MFK_ERR_INVALID_ARGUMENT;
+    const int64_t total = rows * cols;
+    if (total == 0) return MFK_OK;
+    if (x == nullptr || out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    const int64_t max_blocks = static_cast<int64_t>(info->sm_count) * 8;
+    if (cols % 4 == 0 && aligned16(x) && aligned16(out)) {
+        const int64_t total4 = total / 4;
+        const int64_t blocks = std::min<int64_t>((total4 + 255) / 256, max_blocks);
+        mfk::bias_act_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            reinterpret_cast<const float4*>(x), bias, reinterpret_cast<float4*>(out), total4,
+            cols, activation);
+    } else {
+        const int64_t blocks = std::min<int64_t>((total + 255) / 256, max_blocks);
+        mfk::bias_act_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            x, bias, out, total, cols, activation);
+    }
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+int mfk_set_default_precision(int32_t precision) {
+    if (precision != MFK_PRECISION_3XTF32 && precision != MFK_PRECISION_1XTF32)
+        return MFK_ERR_INVALID_ARGUMENT;
+    g_default_precision.store(precision);
+    return MFK_OK;
+}
+
+int32_t mfk_get_default_precision(void) { return g_default_precision.load(); }
+
+int mfk_device_status(uint32_t* bits, int32_t clear) {
+    if (bits == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    MFK_CUDA(cudaDeviceSynchronize());
+    unsigned int v = 0;
+    MFK_CUDA(cudaMemcpyFromSymbol(&v, mfk::g_device_error, sizeof(v)));
+    if (clear && v != 0) {
+        const unsigned int zero = 0;
+        MFK_CUDA(cudaMemcpyToSymbol(mfk::g_device_error, &zero, sizeof(zero)));
+    }
+    *bits = v;
+    return v != 0 ? MFK_ERR_DEVICE_FAULT : MFK_OK;
+}
+
+const char* mfk_status_string(int32_t status) {
+    switch (status) {
+    case MFK_OK:
+        return "ok";
+    case MFK_ERR_INVALID_ARGUMENT:
+        return "invalid argument";
+    case MFK_ERR_UNSUPPORTED:
+        return "unsupported shape or layout";
+    case MFK_ERR_CUDA:
+        return "CUDA runtime error";
+    case MFK_ERR_OUT_OF_MEMORY:
+        return "out of device memory";
+    case MFK_ERR_NO_DEVICE:
+        return "no sm_100 device is current";
+    case MFK_ERR_DEVICE_FAULT:
+        return "a kernel recorded a fault";
+    default:
+        return "unknown status";
+    }
+}
+
+const char* mfk_last_cuda_error(void) { return t_cuda_error.c_str(); }
+
+int32_t mfk_version(void) { return (1 << 16) | 0; }
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// Operand staging for the tensor-core GEMM: gathers a strided fp32 operand into the K-major,
+// 16-byte-aligned, K-padded layout that TMA tiles need, and (3xTF32) splits it into a
+// tf32 (hi, lo) pair on the way.
+//
+// The reference reads any strided view in place inside its packing step
+// (src/backends/cpu/ops/gemm/gemm_pack.hpp, pack_a/pack_b); this is the GPU counterpart: one
+// pass over the operand, coalesced on both sides through a 32x32 shared-memory tile, so a
+// transposed view, a sliced view or a broadcast batch never goes through the host.
+#pragma once
+
+#include <cstdint>
+
+namespace mfk {
+
+// Round to the nearest tf32 (ties away from zero), with the documented PTX conversion.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+enum PackMode : int {
+    kPackCopy = 0,   // hi = x
+    kPackRound = 1,  // hi = tf32(x)
+    kPackSplit = 2,  // hi = tf32(x), lo = tf32(x - hi)
+};
+
+// op(X) of matrix b: element (r, p) at x[off(b) + r*rs + p*cs], with off(b) = offsets[b] when
+// offsets is non-null, else b*bstride. Writes hi/lo as [batch, R, Kp] row-major (row stride
+// Kp), zero in the padding columns K..Kp-1.
+__global__ void __launch_bounds__(256) pack_kmajor_kernel(
+    const float* __restrict__ x, const long long* __restrict__ offsets, long long bstride,
+    long long rs, long long cs, int R, int K, int Kp, float* __restrict__ hi,
+    float* __restrict__ lo, int mode, int p_contig) {
+    __shared__ float tile[32][33];
+    const int b = blockIdx.z;
+    const int r0 = blockIdx.y * 32;
+    const int p0 = blockIdx.x * 32;
+    const long long base = offsets ? offsets[b] : static_cast<long long>(b) * bstride;
+    const float* xb = x + base;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    if (p_contig) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = r0 + ty + 8 * i, p = p0 + tx;
+            tile[ty + 8 * i][tx] =
+                (r < R && p < K) ? xb[static_cast<long long>(r) * rs + static_cast<long long>(p) * cs]
+                                 : 0.0f;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int p = p0 + ty + 8 * i, r = r0 + tx;
+            tile[tx][ty + 8 * i] =
+                (r < R && p < K) ? xb[static_cast<long long>(r) * rs + static_cast<long long>(p) * cs]
+                                 : 0.0f;
+        }
+    }
+    __syncthreads();
+    const long long out_base = static_cast<long long>(b) * R * Kp;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = r0 + ty + 8 * i, p = p0 + tx;
+        if (r < R && p < Kp) {
+            const float v = tile[ty + 8 * i][tx];
+            const long long o = out_base + static_cast<long long>(r) * Kp + p;
+            if (mode == kPackCopy) {
+                hi[o] = v;
+            } else {
+                const float h = tf32_rna(v);
+                hi[o] = h;
+                if (mode == kPackSplit) lo[o] = tf32_rna(v - h);
+            }
+        }
+    }
+}
+
+}  // namespace mfk

@@ -1,0 +1,177 @@
+// Bandwidth-bound SIMT kernels of the path: gemv/matvec, the standalone bias_add/activation
+// pass, and the "no products" (k == 0) epilogue.
+#pragma once
+
+#include <cstdint>
+
+#include "gemm_tc.cuh"
+
+namespace mfk {
+
+// ---- gemv ------------------------------------------------------------------------------------
+// y[i] = alpha * sum_j A[i, j] x[j] + beta * y0[i], the sum accumulated in double as the
+// reference's gemv_f32 / matvec_f32 do (src/backends/cpu/ops/blas/blas.cpp:55-80). A is
+// row-major with row stride lda. One warp per row; each lane streams 16-byte chunks of the row,
+// so a warp reads 512 contiguous bytes per load instruction.
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvRowsPerWarp = 2;
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float gemv_finish(double sum, float alpha, float beta,
+                                             const float* y0, long long i) {
+    return static_cast<float>(static_cast<double>(alpha) * sum +
+                              (beta == 0.0f ? 0.0 : static_cast<double>(beta) * y0[i]));
+}
+
+__global__ void __launch_bounds__(kGemvThreads) gemv_n_vec4_kernel(
+    const float* __restrict__ a, long long rows, long long cols, long long lda,
+    const float* __restrict__ x, float alpha, float beta, const float* __restrict__ y0,
+    float* __restrict__ y) {
+    const int lane = threadIdx.x % 32;
+    const long long warp_global =
+        (static_cast<long long>(blockIdx.x) * kGemvThreads + threadIdx.x) / 32;
+    const long long row0 = warp_global * kGemvRowsPerWarp;
+    const long long cols4 = cols / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll
+    for (int rr = 0; rr < kGemvRowsPerWarp; ++rr) {
+        const long long row = row0 + rr;
+        if (row >= rows) return;
+        const float4* a4 = reinterpret_cast<const float4*>(a + row * lda);
+        double s0 = 0.0, s1 = 0.0;
+        long long j = lane;
+        // Four independent 16-byte loads in flight per lane.
+        for (; j + 96 < cols4; j += 128) {
+            const float4 v0 = __ldcs(a4 + j), v1 = __ldcs(a4 + j + 32);
+            const float4 v2 = __ldcs(a4 + j + 64), v3 = __ldcs(a4 + j + 96);
+            const float4 w0 = __ldg(x4 + j), w1 = __ldg(x4 + j + 32);
+            const float4 w2 = __ldg(x4 + j + 64), w3 = __ldg(x4 + j + 96);
+            s0 += (double)v0.x * w0.x + (double)v0.y * w0.y + (double)v0.z * w0.z + (double)v0.w * w0.w;
+            s1 += (double)v1.x * w1.x + (double)v1.y * w1.y + (double)v1.z * w1.z + (double)v1.w * w1.w;
+            s0 += (double)v2.x * w2.x + (double)v2.y * w2.y + (double)v2.z * w2.z + (double)v2.w * w2.w;
+            s1 += (double)v3.x * w3.x + (double)v3.y * w3.y + (double)v3.z * w3.z + (double)v3.w * w3.w;
+        }
+        for (; j < cols4; j += 32) {
+            const float4 v = __ldcs(a4 + j);
+            const float4 w = __ldg(x4 + j);
+            s0 += (double)v.x * w.x + (double)v.y * w.y + (double)v.z * w.z + (double)v.w * w.w;
+        }
+        for (long long t = cols4 * 4 + lane; t < cols; t += 32) {
+            s1 += (double)a[row * lda + t] * (double)x[t];
+        }
+        const double s = warp_sum(s0 + s1);
+        if (lane == 0) y[row] = gemv_finish(s, alpha, beta, y0, row);
+    }
+}
+
+__global__ void __launch_bounds__(kGemvThreads) gemv_n_scalar_kernel(
+    const float* __restrict__ a, long long rows, long long cols, long long lda,
+    const float* __restrict__ x, long long incx, float alpha, float beta,
+    const float* __restrict__ y0, float* __restrict__ y) {
+    const int lane = threadIdx.x % 32;
+    const long long row = (static_cast<long long>(blockIdx.x) * kGemvThreads + threadIdx.x) / 32;
+    if (row >= rows) return;
+    double s = 0.0;
+    for (long long j = lane; j < cols; j += 32) s += (double)a[row * lda + j] * (double)x[j * incx];
+    s = warp_sum(s);
+    if (lane == 0) y[row] = gemv_finish(s, alpha, beta, y0, row);
+}
+
+// Transposed: y[i] = alpha * sum_j A[j, i] x[j] + beta*y0[i] for i < cols. Threads run along
+// i (coalesced rows of A); the j range is split over blockIdx.y into partial double sums,
+// reduced in a fixed order by gemv_t_finish_kernel (deterministic).
+constexpr int kGemvTRowsPerChunk = 512;
+
+__global__ void __launch_bounds__(256) gemv_t_partial_kernel(const float* __restrict__ a,
+                                                             long long rows, long long cols,
+                                                             long long lda,
+                                                             const float* __restrict__ x,
+                                                             long long incx,
+                                                             double* __restrict__ partial) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= cols) return;
+    const long long j0 = static_cast<long long>(blockIdx.y) * kGemvTRowsPerChunk;
+    const long long j1 = min(rows, j0 + kGemvTRowsPerChunk);
+    double s = 0.0;
+    for (long long j = j0; j < j1; ++j) s += (double)a[j * lda + i] * (double)x[j * incx];
+    partial[static_cast<long long>(blockIdx.y) * cols + i] = s;
+}
+
+__global__ void __launch_bounds__(256) gemv_t_finish_kernel(const double* __restrict__ partial,
+                                                            int chunks, long long cols,
+                                                            float alpha, float beta,
+                                                            const float* __restrict__ y0,
+                                                            float* __restrict__ y) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= cols) return;
+    double s = 0.0;
+    for (int c = 0; c < chunks; ++c) s += partial[static_cast<long long>(c) * cols + i];
+    y[i] = gemv_finish(s, alpha, beta, y0, i);
+}
+
+// ---- bias_add + activation -------------------------------------------------------------------
+// out[r, j] = act(x[r, j] + bias[j]) for a contiguous [rows, cols] x (bias optional): the
+// reference's bias_add_f32 (elementwise.cpp:128-137) and relu_f32 / gelu_f32 (:158, :173-192).
+__global__ void __launch_bounds__(256) bias_act_vec4_kernel(const float4* __restrict__ x,
+                                                            const float* __restrict__ bias,
+                                                            float4* __restrict__ out,
+                                                            long long total4, long long cols,
+                                                            int act) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total4;
+         i += stride) {
+        float4 v = x[i];
+        if (bias != nullptr) {
+            const long long j = (i * 4) % cols;  // cols % 4 == 0: all four share the row
+            v.x = __fadd_rn(v.x, bias[j]);
+            v.y = __fadd_rn(v.y, bias[j + 1]);
+            v.z = __fadd_rn(v.z, bias[j + 2]);
+            v.w = __fadd_rn(v.w, bias[j + 3]);
+        }
+        v.x = apply_act(v.x, act);
+        v.y = apply_act(v.y, act);
+        v.z = apply_act(v.z, act);
+        v.w = apply_act(v.w, act);
+        out[i] = v;
+    }
+}
+
+__global__ void __launch_bounds__(256) bias_act_scalar_kernel(const float* __restrict__ x,
+                                                              const float* __restrict__ bias,
+                                                              float* __restrict__ out,
+                                                              long long total, long long cols,
+                                                              int act) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += stride) {
+        float v = x[i];
+        if (bias != nullptr) v = __fadd_rn(v, bias[i % cols]);
+        out[i] = apply_act(v, act);
+    }
+}
+
+// ---- k == 0 ------------------------------------------------------------------------------
+// No products: C = act(alpha*0 + beta*C_in + bias), batched, C row-major (ldc, c_bs).
+__global__ void __launch_bounds__(256) epilogue_only_kernel(GemmArgs g) {
+    const long long total = static_cast<long long>(g.batch) * g.m * g.n;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    const bool has_cin = g.c_in != nullptr && g.beta != 0.0f;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += stride) {
+        const long long b = i / (static_cast<long long>(g.m) * g.n);
+        const long long rem = i - b * g.m * g.n;
+        const long long r = rem / g.n, j = rem - r * g.n;
+        const float cin = has_cin ? g.c_in[b * g.c_in_bs + r * g.c_in_rs + j * g.c_in_cs] : 0.0f;
+        const float bv = g.bias != nullptr ? g.bias[j] : 0.0f;
+        g.c[b * g.c_bs + r * g.ldc + j] =
+            epilogue_value(0.0f, g.alpha, g.beta, cin, has_cin, bv, g.bias != nullptr, g.act);
+    }
+}
+
+}  // namespace mfk

@@ -1,0 +1,301 @@
+"""The reference's op API for the dense fp32 contraction path, on B200 tensors.
+
+Same names, argument meaning and error behaviour as bakir004/mensurflow's public API
+(include/mensurflow/ops/blas.hpp, elementwise.hpp): ``gemm``, ``matmul``,
+``gemm_strided_batched``, ``gemv``, ``matvec``, ``bias_add``, ``relu``, ``gelu``, plus the fused
+``linear`` (gemm + bias + activation in one kernel). The reference throws
+``std::invalid_argument`` for bad arguments; here that is ``ValueError``.
+
+Tensors are torch CUDA float32 tensors (torch provides device memory and streams only); every
+op runs on the current stream through the C ABI in ``include/mfk.h``. Strided views (transposed,
+sliced, expanded) go to the kernels as they are, with their strides — nothing is staged through
+the host, unlike the reference's non-CPU path (src/core/tensor.cpp:224-229).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import BatchDesc, GemmDesc, check
+
+_ACTS = {None: _lib.ACT_NONE, "none": _lib.ACT_NONE, "relu": _lib.ACT_RELU,
+         "gelu": _lib.ACT_GELU, "gelu_tanh": _lib.ACT_GELU_TANH}
+_PRECISIONS = {None: _lib.PRECISION_DEFAULT, "default": _lib.PRECISION_DEFAULT,
+               "3xtf32": _lib.PRECISION_3XTF32, "1xtf32": _lib.PRECISION_1XTF32}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require(t, op: str, name: str, dims: Optional[int] = None, at_least: bool = False):
+    if t is None or not isinstance(t, torch.Tensor):
+        raise ValueError(f"{op}: {name} is an undefined tensor")
+    if dims is not None:
+        bad = t.dim() < dims if at_least else t.dim() != dims
+        if bad:
+            what = f"at least {dims}-D" if at_least else f"{dims}-D"
+            raise ValueError(f"{op}: {name} must be {what}, got shape {tuple(t.shape)}")
+
+
+def _same(op: str, *ts):
+    ts = [t for t in ts if t is not None]
+    if any(t.dtype != ts[0].dtype for t in ts):
+        raise ValueError(f"{op}: dtypes differ")
+    if any(t.device != ts[0].device for t in ts):
+        raise ValueError(f"{op}: tensors are on different devices; move one with Tensor::to()")
+    if ts[0].dtype != torch.float32:
+        raise NotImplementedError(f"{op}: no kernel for dtype {ts[0].dtype} on {ts[0].device}")
+    if ts[0].device.type != "cuda":
+        raise NotImplementedError(f"{op}: these kernels run on CUDA devices only")
+
+
+def set_default_precision(precision: str) -> None:
+    """Process-wide GEMM precision ("3xtf32", the default, or "1xtf32")."""
+    check(_lib.lib().mfk_set_default_precision(_PRECISIONS[precision]), "set_default_precision")
+
+
+def get_default_precision() -> str:
+    return {0: "3xtf32", 1: "1xtf32"}[_lib.lib().mfk_get_default_precision()]
+
+
+def _gemm_desc(a_op, b_op, out, alpha, c_in, beta, bias, act, precision) -> GemmDesc:
+    """a_op: op(A) [m,k] view, b_op: op(B) [k,n] view, out: [m,n] with unit column stride."""
+    d = GemmDesc()
+    d.a, d.a_rs, d.a_cs = _ptr(a_op), a_op.stride(0), a_op.stride(1)
+    d.b, d.b_rs, d.b_cs = _ptr(b_op), b_op.stride(0), b_op.stride(1)
+    if c_in is not None:
+        d.c_in, d.c_in_rs, d.c_in_cs = _ptr(c_in), c_in.stride(0), c_in.stride(1)
+    d.c, d.ldc = _ptr(out), out.stride(0)
+    d.m, d.n, d.k = out.shape[0], out.shape[1], a_op.shape[1]
+    d.alpha, d.beta = float(alpha), float(beta)
+    d.bias = _ptr(bias)
+    d.activation = _ACTS[act]
+    d.precision = _PRECISIONS[precision]
+    return d
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch.Tensor] = None,
+         beta: float = 0.0, transpose_a: bool = False, transpose_b: bool = False, *,
+         bias: Optional[torch.Tensor] = None, activation: Optional[str] = None,
+         precision: Optional[str] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """alpha * op(a) @ op(b) + beta * c, as mensurflow::gemm (blas.hpp:59, blas.cpp:234-262),
+    in ONE kernel; `bias` and `activation` fuse the following bias_add/relu/gelu."""
+    _require(a, "gemm", "a", 2)
+    _require(b, "gemm", "b", 2)
+    if c is not None:
+        _require(c, "gemm", "c")
+    _same("gemm", a, b, c, bias)
+    left = a.t() if transpose_a else a
+    right = b.t() if transpose_b else b
+    m, k = left.shape
+    if right.shape[0] != k:
+        raise ValueError(f"gemm: inner dimensions differ ({tuple(left.shape)} times "
+                         f"{tuple(right.shape)})")
+    n = right.shape[1]
+    if c is not None and tuple(c.shape) != (m, n):
+        raise ValueError("gemm: c shape does not match result")
+    if c is None and beta != 0.0:
+        raise ValueError("gemm: beta requires c")
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != n):
+        raise ValueError(f"gemm: bias must be [{n}], got {tuple(bias.shape)}")
+    if activation not in _ACTS:
+        raise ValueError(f"gemm: unknown activation {activation!r}")
+    if bias is not None:
+        bias = bias.contiguous()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    elif tuple(out.shape) != (m, n) or out.stride(1) != 1:
+        raise ValueError("gemm: out must be [m, n] with unit column stride")
+    desc = _gemm_desc(left, right, out, alpha, c if beta != 0.0 else None, beta, bias,
+                      activation, precision)
+    check(_lib.lib().mfk_gemm_f32(ctypes.byref(desc), _stream()), "gemm")
+    return out
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, *, precision: Optional[str] = None) -> torch.Tensor:
+    """[M,K] @ [K,N] as mensurflow::matmul (blas.hpp:55, blas.cpp:186-232)."""
+    _require(a, "matmul", "a", 2)
+    _require(b, "matmul", "b", 2)
+    _same("matmul", a, b)
+    if b.shape[0] != a.shape[1]:
+        raise ValueError(f"matmul: inner dimensions differ ({tuple(a.shape)} times "
+                         f"{tuple(b.shape)})")
+    return gemm(a, b, precision=precision)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           activation: Optional[str] = None, *, transpose_w: bool = False,
+           precision: Optional[str] = None) -> torch.Tensor:
+    """act(x @ op(w) + bias) in one kernel: the fused form of matmul + bias_add (+ relu/gelu)."""
+    return gemm(x, w, transpose_b=transpose_w, bias=bias, activation=activation,
+                precision=precision)
+
+
+def _broadcast_shapes(op: str, x: Sequence[int], y: Sequence[int]):
+    try:
+        return tuple(torch.broadcast_shapes(tuple(x), tuple(y)))
+    except RuntimeError:
+        raise ValueError(f"{op}: batch shapes {tuple(x)} and {tuple(y)} do not broadcast")
+
+
+def _odometer_offsets(t: torch.Tensor, batch_shape) -> np.ndarray:
+    """Element offset of each matrix of an expanded view, last batch dim fastest — the walk of
+    the reference's gemm_batched_kernel (src/backends/cpu/backend.cpp:251-270)."""
+    nd = len(batch_shape)
+    if nd == 0:
+        return np.zeros(1, np.int64)
+    idx = np.indices(batch_shape).reshape(nd, -1).T  # row-major order = last dim fastest
+    strides = np.array(t.stride()[:nd], np.int64)
+    return (idx.astype(np.int64) * strides).sum(axis=1).astype(np.int64)
+
+
+def gemm_strided_batched(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0,
+                         c: Optional[torch.Tensor] = None, beta: float = 0.0,
+                         transpose_a: bool = False, transpose_b: bool = False, *,
+                         precision: Optional[str] = None) -> torch.Tensor:
+    """Batched gemm with NumPy batch broadcasting, as mensurflow::gemm_strided_batched
+    (blas.hpp:75, blas.cpp:297-394)."""
+    op = "gemm_strided_batched"
+    for t, name in ((a, "a"), (b, "b")):
+        _require(t, op, name, 2, at_least=True)
+    _same(op, a, b, c)
+    if c is None and beta != 0.0:
+        raise ValueError(f"{op}: beta requires c")
+    left = a.transpose(-2, -1) if transpose_a else a
+    right = b.transpose(-2, -1) if transpose_b else b
+    m, k, n = left.shape[-2], left.shape[-1], right.shape[-1]
+    if right.shape[-2] != k:
+        raise ValueError(f"{op}: inner dimensions differ ({tuple(left.shape)} times "
+                         f"{tuple(right.shape)})")
+    batch_shape = _broadcast_shapes(op, left.shape[:-2], right.shape[:-2])
+    out_shape = batch_shape + (m, n)
+    initial = None
+    if c is not None:
+        ok = c.dim() <= len(out_shape)
+        if ok:
+            try:
+                ok = tuple(torch.broadcast_shapes(tuple(c.shape), out_shape)) == out_shape
+            except RuntimeError:
+                ok = False
+        if not ok:
+            raise ValueError(f"{op}: c has shape {tuple(c.shape)}, which does not broadcast to "
+                             f"{out_shape}")
+        if beta != 0.0:
+            initial = c.expand(out_shape)
+    out = torch.empty(out_shape, dtype=torch.float32, device=a.device)
+    batch = int(np.prod(batch_shape)) if batch_shape else 1
+    if out.numel() == 0:
+        return out
+    lv = left.expand(batch_shape + (m, k))
+    rv = right.expand(batch_shape + (k, n))
+    a_off = _odometer_offsets(lv, batch_shape)
+    b_off = _odometer_offsets(rv, batch_shape)
+    bd = BatchDesc()
+    bd.batch = batch
+    bd.a_offsets = a_off.ctypes.data
+    bd.b_offsets = b_off.ctypes.data
+    bd.c_stride = m * n
+    zero = (0,) * len(batch_shape)
+    desc = _gemm_desc(lv[zero], rv[zero], out.view(-1, m, n)[0], alpha, None, 0.0, None, None,
+                      precision)
+    # Base pointers are the expanded views' first elements; the offsets are relative to them.
+    desc.a = lv.data_ptr()
+    desc.b = rv.data_ptr()
+    if initial is not None:
+        c_off = _odometer_offsets(initial, batch_shape)
+        even = batch <= 1 or bool(np.all(np.diff(c_off) == c_off[1] - c_off[0]))
+        if not even:
+            initial = initial.contiguous()  # the reference packs c the same way (blas.cpp:361)
+            c_off = _odometer_offsets(initial, batch_shape)
+        desc.c_in = initial.data_ptr()
+        desc.c_in_rs, desc.c_in_cs = initial.stride(-2), initial.stride(-1)
+        desc.beta = float(beta)
+        bd.c_in_stride = int(c_off[1] - c_off[0]) if batch > 1 else 0
+    check(_lib.lib().mfk_gemm_strided_batched_f32(ctypes.byref(desc), ctypes.byref(bd), _stream()),
+          op)
+    return out
+
+
+def gemv(a: torch.Tensor, x: torch.Tensor, alpha: float = 1.0, y: Optional[torch.Tensor] = None,
+         beta: float = 0.0, transpose_a: bool = False) -> torch.Tensor:
+    """alpha * op(a) x + beta * y, sums in double, as mensurflow::gemv (blas.hpp:40)."""
+    _require(a, "gemv", "a", 2)
+    _require(x, "gemv", "x", 1)
+    if y is None and beta != 0.0:
+        raise ValueError("gemv: beta requires an output vector")
+    _same("gemv", a, x, y)
+    rows, cols = a.shape
+    n_in, n_out = (rows, cols) if transpose_a else (cols, rows)
+    if x.shape[0] != n_in:
+        raise ValueError("gemv: input length does not match matrix dimensions")
+    if y is not None and y.shape[0] != n_out:
+        raise ValueError("gemv: output length does not match matrix dimensions")
+    if a.stride(1) != 1 or (rows > 1 and a.stride(0) < cols):
+        a = a.contiguous()
+    out = torch.empty(n_out, dtype=torch.float32, device=a.device)
+    y0 = y.contiguous() if y is not None else None
+    check(_lib.lib().mfk_gemv_f32(a.data_ptr(), rows, cols, max(a.stride(0), cols),
+                                  1 if transpose_a else 0, x.data_ptr(), x.stride(0) or 1,
+                                  float(alpha), float(beta), _ptr(y0), out.data_ptr(), _stream()),
+          "gemv")
+    return out
+
+
+def matvec(a: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """[M,K] @ [K] as mensurflow::matvec (blas.hpp:35)."""
+    _require(a, "matvec", "a", 2)
+    _require(x, "matvec", "x", 1)
+    _same("matvec", a, x)
+    if x.shape[0] != a.shape[1]:
+        raise ValueError(f"matvec: inner dimensions differ ({tuple(a.shape)} times "
+                         f"{tuple(x.shape)})")
+    return gemv(a, x)
+
+
+def _bias_act(x: torch.Tensor, bias: Optional[torch.Tensor], act: int, op: str) -> torch.Tensor:
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    cols = x.shape[-1] if x.dim() > 0 else 1
+    rows = x.numel() // cols if cols else 0
+    check(_lib.lib().mfk_bias_act_f32(x.data_ptr(), _ptr(bias), out.data_ptr(), rows, cols, act,
+                                      _stream()), op)
+    return out
+
+
+def bias_add(x: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """x [batch, features] + bias [features], as mensurflow::bias_add (elementwise.hpp:43,
+    elementwise.cpp:251-284)."""
+    _require(x, "bias_add", "x")
+    _require(bias, "bias_add", "bias")
+    if x.dim() != 2 or bias.dim() != 1 or bias.shape[0] != x.shape[1]:
+        raise ValueError(f"bias_add: expected x [batch, features] and bias [features], got "
+                         f"{tuple(x.shape)} and {tuple(bias.shape)}")
+    _same("bias_add", x, bias)
+    return _bias_act(x, bias.contiguous(), _lib.ACT_NONE, "bias_add")
+
+
+def relu(x: torch.Tensor) -> torch.Tensor:
+    _require(x, "relu", "x")
+    _same("relu", x)
+    return _bias_act(x, None, _lib.ACT_RELU, "relu")
+
+
+def gelu(x: torch.Tensor, approximate: bool = False) -> torch.Tensor:
+    """Exact 0.5*v*erfc(-v/sqrt 2) (or the tanh form), as mensurflow::gelu (elementwise.hpp:62)."""
+    _require(x, "gelu", "x")
+    _same("gelu", x)
+    return _bias_act(x, None, _lib.ACT_GELU_TANH if approximate else _lib.ACT_GELU, "gelu")
+
+
+def device_status() -> int:
+    """Kernel error bits of the current device (0 = none); clears them."""
+    return _lib.device_status(True)

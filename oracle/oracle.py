@@ -1,0 +1,313 @@
+"""TEST INFRASTRUCTURE ONLY — Python access to the parity oracle.
+
+Two libraries, both built by ``oracle/Makefile``:
+
+* ``oracle/_build/libmforacle.so`` — the C restatement (``oracle/mf_oracle.c``) of the
+  reference's CPU algorithms. Always available: built here or, on a machine without the
+  prebuilt file, compiled on first use with the system gcc.
+* ``oracle/_ref/libmfref.so`` — the unmodified reference library compiled from its own
+  sources plus ``oracle/ref_shim.cpp``. Present only where it was built (it travels with the
+  repository snapshot); ``reference()`` returns None without it.
+
+Only tests, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline/reference legs may use this
+module. The product path never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_ORACLE_SO = os.path.join(HERE, "_build", "libmforacle.so")
+_REF_SO = os.path.join(HERE, "_ref", "libmfref.so")
+
+_lock = threading.Lock()
+_oracle = None
+_ref = None
+_ref_loaded = False
+
+_i64 = ctypes.c_int64
+_u64 = ctypes.c_uint64
+_f32 = ctypes.c_float
+_ptr = ctypes.c_void_p
+
+
+def _p(arr):
+    return None if arr is None else ctypes.c_void_p(arr.ctypes.data)
+
+
+def build_oracle() -> str:
+    if not os.path.exists(_ORACLE_SO) or os.path.getmtime(_ORACLE_SO) < os.path.getmtime(
+        os.path.join(HERE, "mf_oracle.c")
+    ):
+        subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
+    return _ORACLE_SO
+
+
+def lib():
+    """The C restatement, built on first use."""
+    global _oracle
+    with _lock:
+        if _oracle is None:
+            so = ctypes.CDLL(build_oracle())
+            so.mfo_uniform.argtypes = [_ptr, _i64, _f32, _f32, _u64, _u64]
+            so.mfo_normal.argtypes = [_ptr, _i64, _f32, _f32, _u64, _u64]
+            so.mfo_philox_word.argtypes = [_u64, _u64, ctypes.c_int]
+            so.mfo_philox_word.restype = ctypes.c_uint32
+            so.mfo_gemm_batched.argtypes = [
+                _ptr, _ptr, _i64, _i64, _ptr, _ptr, _i64, _i64, _ptr, _i64, _i64,
+                _ptr, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32, _i64,
+            ]
+            so.mfo_abs_product.argtypes = [
+                _ptr, _ptr, _i64, _i64, _ptr, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
+            ]
+            so.mfo_bias_add.argtypes = [_ptr, _ptr, _ptr, _i64, _i64]
+            so.mfo_relu.argtypes = [_ptr, _ptr, _i64]
+            so.mfo_gelu.argtypes = [_ptr, _ptr, _i64, ctypes.c_int]
+            so.mfo_gemv.argtypes = [_ptr, _i64, _i64, _i64, _ptr, _f32, _f32, _ptr, _ptr, ctypes.c_int]
+            _oracle = so
+    return _oracle
+
+
+def reference():
+    """The unmodified reference library (CPU), or None where it was not built."""
+    global _ref, _ref_loaded
+    with _lock:
+        if not _ref_loaded:
+            _ref_loaded = True
+            if os.path.exists(_REF_SO):
+                so = ctypes.CDLL(_REF_SO)
+                so.mfref_last_error.restype = ctypes.c_char_p
+                so.mfref_uniform.argtypes = [_ptr, _i64, _f32, _f32, _u64, _u64]
+                so.mfref_normal.argtypes = [_ptr, _i64, _f32, _f32, _u64, _u64]
+                so.mfref_gemm.argtypes = [_ptr, _i64, _i64, _ptr, _i64, _i64, _ptr, _f32, _f32,
+                                          ctypes.c_int, ctypes.c_int, _ptr]
+                so.mfref_matmul.argtypes = [_ptr, _i64, _i64, _ptr, _i64, _ptr]
+                so.mfref_gemm_strided_batched.argtypes = [
+                    _ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int,
+                    _f32, _f32, ctypes.c_int, ctypes.c_int, _ptr, _ptr, _ptr,
+                ]
+                so.mfref_bias_add.argtypes = [_ptr, _i64, _i64, _ptr, _ptr]
+                so.mfref_gelu.argtypes = [_ptr, _i64, ctypes.c_int, _ptr]
+                so.mfref_relu.argtypes = [_ptr, _i64, _ptr]
+                so.mfref_gemv.argtypes = [_ptr, _i64, _i64, _ptr, _f32, _ptr, _f32, ctypes.c_int, _ptr]
+                so.mfref_matvec.argtypes = [_ptr, _i64, _i64, _ptr, _ptr]
+                so.mfref_time_gemm.argtypes = [_i64, _i64, _i64, _f32, _f32, ctypes.c_int,
+                                               ctypes.c_int, _u64, ctypes.c_int, ctypes.c_int, _ptr]
+                so.mfref_time_gemv.argtypes = [_i64, _i64, _u64, ctypes.c_int, ctypes.c_int, _ptr]
+                so.mfref_set_threads.argtypes = [ctypes.c_int]
+                _ref = so
+    return _ref
+
+
+def _check_ref(rc):
+    if rc != 0:
+        raise RuntimeError(reference().mfref_last_error().decode())
+
+
+# ---- the C restatement -------------------------------------------------------------------
+
+def uniform(n, low, high, seed, offset=0):
+    out = np.empty(n, np.float32)
+    lib().mfo_uniform(_p(out), n, low, high, seed, offset)
+    return out
+
+
+def normal(n, mean, std, seed, offset=0):
+    out = np.empty(n, np.float32)
+    lib().mfo_normal(_p(out), n, mean, std, seed, offset)
+    return out
+
+
+def _as_strided_args(x, transpose):
+    """Row/col element strides of op(x) for a 2-D C-contiguous float32 array."""
+    rs, cs = x.strides[0] // 4, x.strides[1] // 4
+    return (cs, rs) if transpose else (rs, cs)
+
+
+def gemm(a, b, alpha=1.0, c=None, beta=0.0, transpose_a=False, transpose_b=False,
+         bias=None, act=None, kc=256):
+    """alpha*op(a)@op(b) + beta*c (+ bias, then act) with the restated CPU algorithm."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = (a.shape[1], a.shape[0]) if transpose_a else a.shape
+    n = b.shape[0] if transpose_b else b.shape[1]
+    rsa, csa = _as_strided_args(a, transpose_a)
+    rsb, csb = _as_strided_args(b, transpose_b)
+    out = np.empty((m, n), np.float32)
+    c0 = None
+    if c is not None and beta != 0.0:
+        c0 = np.ascontiguousarray(np.broadcast_to(c, (m, n)), np.float32)
+    lib().mfo_gemm_batched(_p(a), None, rsa, csa, _p(b), None, rsb, csb, _p(out), n, m * n,
+                           _p(c0), n, 1, m * n, 1, m, n, k, alpha, beta if c0 is not None else 0.0,
+                           kc)
+    if bias is not None:
+        out = bias_add(out, bias)
+    if act is not None:
+        out = activation(out, act)
+    return out
+
+
+def abs_product(a, b, transpose_a=False, transpose_b=False):
+    """(|op(a)|·|op(b)|) in float64."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = (a.shape[1], a.shape[0]) if transpose_a else a.shape
+    n = b.shape[0] if transpose_b else b.shape[1]
+    rsa, csa = _as_strided_args(a, transpose_a)
+    rsb, csb = _as_strided_args(b, transpose_b)
+    out = np.empty((m, n), np.float64)
+    lib().mfo_abs_product(_p(a), None, rsa, csa, _p(b), None, rsb, csb, _p(out), 1, m, n, k)
+    return out
+
+
+def gemm_batched_raw(a, a_off, rsa, csa, b, b_off, rsb, csb, batch, m, n, k, alpha=1.0,
+                     c0=None, c0_strides=(0, 0, 0), beta=0.0, kc=256):
+    """The restated cpu::BatchedGemm on flat float32 buffers with explicit offsets/strides."""
+    out = np.empty((batch, m, n), np.float32)
+    ao = np.ascontiguousarray(a_off, np.int64)
+    bo = np.ascontiguousarray(b_off, np.int64)
+    lib().mfo_gemm_batched(_p(a), _p(ao), rsa, csa, _p(b), _p(bo), rsb, csb, _p(out), n, m * n,
+                           _p(c0), c0_strides[0], c0_strides[1], c0_strides[2], batch, m, n, k,
+                           alpha, beta if c0 is not None else 0.0, kc)
+    return out
+
+
+def abs_product_batched_raw(a, a_off, rsa, csa, b, b_off, rsb, csb, batch, m, n, k):
+    out = np.empty((batch, m, n), np.float64)
+    ao = np.ascontiguousarray(a_off, np.int64)
+    bo = np.ascontiguousarray(b_off, np.int64)
+    lib().mfo_abs_product(_p(a), _p(ao), rsa, csa, _p(b), _p(bo), rsb, csb, _p(out), batch, m, n, k)
+    return out
+
+
+def bias_add(x, bias):
+    x = np.ascontiguousarray(x, np.float32)
+    bias = np.ascontiguousarray(bias, np.float32)
+    out = np.empty_like(x)
+    lib().mfo_bias_add(_p(x), _p(bias), _p(out), x.shape[0], x.shape[1])
+    return out
+
+
+def activation(x, act):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    if act == "relu":
+        lib().mfo_relu(_p(x), _p(out), x.size)
+    elif act in ("gelu", "gelu_tanh"):
+        lib().mfo_gelu(_p(x), _p(out), x.size, 1 if act == "gelu_tanh" else 0)
+    else:
+        raise ValueError(f"unknown activation {act!r}")
+    return out
+
+
+def gemv(a, x, alpha=1.0, y=None, beta=0.0, transpose_a=False):
+    a = np.ascontiguousarray(a, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = a.shape
+    n_out = cols if transpose_a else rows
+    out = np.empty(n_out, np.float32)
+    y0 = None if y is None else np.ascontiguousarray(y, np.float32)
+    lib().mfo_gemv(_p(a), rows, cols, cols, _p(x), alpha, beta, _p(y0), _p(out),
+                   1 if transpose_a else 0)
+    return out
+
+
+# ---- the reference itself (where built) --------------------------------------------------
+
+def ref_uniform(n, low, high, seed, offset=0):
+    out = np.empty(n, np.float32)
+    _check_ref(reference().mfref_uniform(_p(out), n, low, high, seed, offset))
+    return out
+
+
+def ref_normal(n, mean, std, seed, offset=0):
+    out = np.empty(n, np.float32)
+    _check_ref(reference().mfref_normal(_p(out), n, mean, std, seed, offset))
+    return out
+
+
+def ref_gemm(a, b, alpha=1.0, c=None, beta=0.0, transpose_a=False, transpose_b=False):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m = a.shape[1] if transpose_a else a.shape[0]
+    n = b.shape[0] if transpose_b else b.shape[1]
+    out = np.empty((m, n), np.float32)
+    cc = None if c is None else np.ascontiguousarray(c, np.float32)
+    _check_ref(reference().mfref_gemm(_p(a), a.shape[0], a.shape[1], _p(b), b.shape[0],
+                                      b.shape[1], _p(cc), alpha, beta, int(transpose_a),
+                                      int(transpose_b), _p(out)))
+    return out
+
+
+def ref_gemm_strided_batched(a, b, alpha=1.0, c=None, beta=0.0, transpose_a=False,
+                             transpose_b=False):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    cc = None if c is None else np.ascontiguousarray(c, np.float32)
+    ash = np.array(a.shape, np.int64)
+    bsh = np.array(b.shape, np.int64)
+    csh = None if cc is None else np.array(cc.shape if cc.ndim else [1], np.int64)
+    oshape = np.zeros(8, np.int64)
+    ond = ctypes.c_int(0)
+    lib_ = reference()
+    _check_ref(lib_.mfref_gemm_strided_batched(
+        _p(a), _p(ash), a.ndim, _p(b), _p(bsh), b.ndim, _p(cc), _p(csh),
+        0 if cc is None else cc.ndim, alpha, beta, int(transpose_a), int(transpose_b), None,
+        _p(oshape), ctypes.byref(ond)))
+    shape = tuple(int(v) for v in oshape[: ond.value])
+    out = np.empty(shape, np.float32)
+    _check_ref(lib_.mfref_gemm_strided_batched(
+        _p(a), _p(ash), a.ndim, _p(b), _p(bsh), b.ndim, _p(cc), _p(csh),
+        0 if cc is None else cc.ndim, alpha, beta, int(transpose_a), int(transpose_b), _p(out),
+        _p(oshape), ctypes.byref(ond)))
+    return out
+
+
+def ref_bias_add(x, bias):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    _check_ref(reference().mfref_bias_add(_p(x), x.shape[0], x.shape[1],
+                                          _p(np.ascontiguousarray(bias, np.float32)), _p(out)))
+    return out
+
+
+def ref_gelu(x, approximate=False):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    _check_ref(reference().mfref_gelu(_p(x), x.size, int(approximate), _p(out)))
+    return out
+
+
+def ref_relu(x):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    _check_ref(reference().mfref_relu(_p(x), x.size, _p(out)))
+    return out
+
+
+def ref_gemv(a, x, alpha=1.0, y=None, beta=0.0, transpose_a=False):
+    a = np.ascontiguousarray(a, np.float32)
+    rows, cols = a.shape
+    out = np.empty(cols if transpose_a else rows, np.float32)
+    yy = None if y is None else np.ascontiguousarray(y, np.float32)
+    _check_ref(reference().mfref_gemv(_p(a), rows, cols, _p(np.ascontiguousarray(x, np.float32)),
+                                      alpha, _p(yy), beta, int(transpose_a), _p(out)))
+    return out
+
+
+def ref_time_gemm(m, n, k, alpha, beta, transpose_b, with_bias, seed, warmup, reps):
+    secs = np.zeros(reps, np.float64)
+    _check_ref(reference().mfref_time_gemm(m, n, k, alpha, beta, int(transpose_b), int(with_bias),
+                                           seed, warmup, reps, _p(secs)))
+    return secs
+
+
+def ref_time_gemv(rows, cols, seed, warmup, reps):
+    secs = np.zeros(reps, np.float64)
+    _check_ref(reference().mfref_time_gemv(rows, cols, seed, warmup, reps, _p(secs)))
+    return secs

@@ -1,0 +1,229 @@
+// TEST INFRASTRUCTURE ONLY — never part of the product path.
+//
+// A C-ABI over the unmodified reference library (bakir004/mensurflow, built from its own
+// sources by oracle/Makefile into oracle/_ref/). Everything here calls the reference's PUBLIC
+// API with Execution::CPU, so the numbers it returns are the reference's own CPU results:
+//   gemm                  include/mensurflow/ops/blas.hpp:59   (src/ops/blas.cpp:234-262)
+//   matmul                include/mensurflow/ops/blas.hpp:55   (src/ops/blas.cpp:186-232)
+//   gemm_strided_batched  include/mensurflow/ops/blas.hpp:75   (src/ops/blas.cpp:297-394)
+//   gemv / matvec         include/mensurflow/ops/blas.hpp:35,40 (src/ops/blas.cpp:119-183)
+//   bias_add / relu/gelu  include/mensurflow/ops/elementwise.hpp:43,56,62
+//   uniform / normal      include/mensurflow/ops/random.hpp:20,25
+// Used by tests/golden/make_golden.py (fixtures), by tests that pin the C restatement in
+// oracle/mf_oracle.c against the reference, and by bench.py's CPU-baseline and reference arms.
+// Every entry returns 0 on success and -1 on a C++ exception (text in mfref_last_error()).
+#include "backends/cpu/threads.hpp"
+#include "mensurflow/mensurflow.hpp"
+
+#include <algorithm>
+#include <chrono>
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+using namespace mensurflow;
+
+namespace {
+
+thread_local std::string g_error;
+
+template <typename F> int guarded(F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return -1;
+    }
+}
+
+Shape make_shape(const std::int64_t* dims, int nd) { return Shape(dims, dims + nd); }
+
+Tensor host_tensor(const float* data, const Shape& shape) {
+    return Tensor::from_host(data, shape, DType::F32, Device{});
+}
+
+void copy_out(const Tensor& t, float* out) {
+    if (t.numel() > 0) {
+        t.copy_to_host(out);
+    }
+}
+
+double now() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+} // namespace
+
+extern "C" {
+
+const char* mfref_last_error() { return g_error.c_str(); }
+
+int mfref_openmp() { return cpu::has_openmp() ? 1 : 0; }
+
+int mfref_max_threads() { return cpu::max_threads(); }
+
+void mfref_set_threads(int threads) { cpu::set_max_threads(threads); }
+
+int mfref_uniform(float* out, std::int64_t n, float low, float high, std::uint64_t seed,
+                  std::uint64_t offset) {
+    return guarded([&] { copy_out(uniform({n}, low, high, seed, offset, Execution::CPU), out); });
+}
+
+int mfref_normal(float* out, std::int64_t n, float mean, float stddev, std::uint64_t seed,
+                 std::uint64_t offset) {
+    return guarded(
+        [&] { copy_out(normal({n}, mean, stddev, seed, offset, Execution::CPU), out); });
+}
+
+// a is stored [ar, ac], b is stored [br, bc], c (optional) is the [m, n] result shape.
+int mfref_gemm(const float* a, std::int64_t ar, std::int64_t ac, const float* b, std::int64_t br,
+               std::int64_t bc, const float* c, float alpha, float beta, int transpose_a,
+               int transpose_b, float* out) {
+    return guarded([&] {
+        const Tensor ta = host_tensor(a, {ar, ac});
+        const Tensor tb = host_tensor(b, {br, bc});
+        const std::int64_t m = transpose_a ? ac : ar;
+        const std::int64_t n = transpose_b ? br : bc;
+        Tensor tc;
+        if (c != nullptr) {
+            tc = host_tensor(c, {m, n});
+        }
+        copy_out(gemm(ta, tb, alpha, c ? &tc : nullptr, beta, transpose_a != 0, transpose_b != 0,
+                      Execution::CPU),
+                 out);
+    });
+}
+
+int mfref_matmul(const float* a, std::int64_t m, std::int64_t k, const float* b, std::int64_t n,
+                 float* out) {
+    return guarded([&] {
+        copy_out(matmul(host_tensor(a, {m, k}), host_tensor(b, {k, n}), Execution::CPU), out);
+    });
+}
+
+// Shapes as stored (before the transpose flags). out_shape receives the result's shape
+// (up to 8 dims) and out_nd its rank; out must hold numel(result) floats.
+int mfref_gemm_strided_batched(const float* a, const std::int64_t* a_shape, int a_nd,
+                               const float* b, const std::int64_t* b_shape, int b_nd,
+                               const float* c, const std::int64_t* c_shape, int c_nd, float alpha,
+                               float beta, int transpose_a, int transpose_b, float* out,
+                               std::int64_t* out_shape, int* out_nd) {
+    return guarded([&] {
+        const Tensor ta = host_tensor(a, make_shape(a_shape, a_nd));
+        const Tensor tb = host_tensor(b, make_shape(b_shape, b_nd));
+        Tensor tc;
+        if (c != nullptr) {
+            tc = host_tensor(c, make_shape(c_shape, c_nd));
+        }
+        const Tensor r = gemm_strided_batched(ta, tb, alpha, c ? &tc : nullptr, beta,
+                                              transpose_a != 0, transpose_b != 0, Execution::CPU);
+        *out_nd = r.dim();
+        for (int d = 0; d < r.dim(); ++d) {
+            out_shape[d] = r.size(d);
+        }
+        if (out != nullptr) {
+            copy_out(r, out);
+        }
+    });
+}
+
+int mfref_bias_add(const float* x, std::int64_t rows, std::int64_t cols, const float* bias,
+                   float* out) {
+    return guarded([&] {
+        copy_out(bias_add(host_tensor(x, {rows, cols}), host_tensor(bias, {cols}), Execution::CPU),
+                 out);
+    });
+}
+
+int mfref_gelu(const float* x, std::int64_t n, int approximate, float* out) {
+    return guarded(
+        [&] { copy_out(gelu(host_tensor(x, {n}), approximate != 0, Execution::CPU), out); });
+}
+
+int mfref_relu(const float* x, std::int64_t n, float* out) {
+    return guarded([&] { copy_out(relu(host_tensor(x, {n}), Execution::CPU), out); });
+}
+
+// a stored [rows, cols]; y (optional) has op(a)'s row count.
+int mfref_gemv(const float* a, std::int64_t rows, std::int64_t cols, const float* x, float alpha,
+               const float* y, float beta, int transpose_a, float* out) {
+    return guarded([&] {
+        const Tensor ta = host_tensor(a, {rows, cols});
+        const std::int64_t in = transpose_a ? rows : cols;
+        const std::int64_t outn = transpose_a ? cols : rows;
+        Tensor ty;
+        if (y != nullptr) {
+            ty = host_tensor(y, {outn});
+        }
+        copy_out(gemv(ta, host_tensor(x, {in}), alpha, y ? &ty : nullptr, beta, transpose_a != 0,
+                      Execution::CPU),
+                 out);
+    });
+}
+
+int mfref_matvec(const float* a, std::int64_t m, std::int64_t k, const float* x, float* out) {
+    return guarded(
+        [&] { copy_out(matvec(host_tensor(a, {m, k}), host_tensor(x, {k}), Execution::CPU), out); });
+}
+
+// Times the reference's public gemm (+ bias_add when with_bias) on CPU-resident inputs made by
+// its own normal() factory: A [m,k], B [n,k] read transposed when transpose_b (else [k,n]),
+// C_in [m,n]. Runs `warmup` untimed calls, then `reps` timed calls; writes each call's seconds
+// into seconds[0..reps). Inputs are created outside the timed region.
+int mfref_time_gemm(std::int64_t m, std::int64_t n, std::int64_t k, float alpha, float beta,
+                    int transpose_b, int with_bias, std::uint64_t seed, int warmup, int reps,
+                    double* seconds) {
+    return guarded([&] {
+        const Tensor a = normal({m, k}, 0.0f, 1.0f, seed, 0, Execution::CPU);
+        const Tensor b = transpose_b ? normal({n, k}, 0.0f, 1.0f, seed, std::uint64_t(m * k),
+                                              Execution::CPU)
+                                     : normal({k, n}, 0.0f, 1.0f, seed, std::uint64_t(m * k),
+                                              Execution::CPU);
+        const Tensor c = normal({m, n}, 0.0f, 1.0f, seed, std::uint64_t(m * k + n * k),
+                                Execution::CPU);
+        const Tensor bias = uniform({n}, -0.1f, 0.1f, seed,
+                                    std::uint64_t(m * k + n * k + m * n), Execution::CPU);
+        auto once = [&] {
+            Tensor r = gemm(a, b, alpha, beta != 0.0f ? &c : nullptr, beta, false,
+                            transpose_b != 0, Execution::CPU);
+            if (with_bias) {
+                r = bias_add(r, bias, Execution::CPU);
+            }
+            return r;
+        };
+        for (int i = 0; i < warmup; ++i) {
+            once();
+        }
+        for (int i = 0; i < reps; ++i) {
+            const double t0 = now();
+            const Tensor r = once();
+            seconds[i] = now() - t0;
+            (void)r;
+        }
+    });
+}
+
+// Times the reference's public gemv on A [rows, cols] and x [cols] from uniform(-1,1).
+int mfref_time_gemv(std::int64_t rows, std::int64_t cols, std::uint64_t seed, int warmup, int reps,
+                    double* seconds) {
+    return guarded([&] {
+        const Tensor a = uniform({rows, cols}, -1.0f, 1.0f, seed, 0, Execution::CPU);
+        const Tensor x = uniform({cols}, -1.0f, 1.0f, seed, std::uint64_t(rows * cols),
+                                 Execution::CPU);
+        for (int i = 0; i < warmup; ++i) {
+            gemv(a, x, 1.0f, nullptr, 0.0f, false, Execution::CPU);
+        }
+        for (int i = 0; i < reps; ++i) {
+            const double t0 = now();
+            const Tensor r = gemv(a, x, 1.0f, nullptr, 0.0f, false, Execution::CPU);
+            seconds[i] = now() - t0;
+            (void)r;
+        }
+    });
+}
+
+} // extern "C"

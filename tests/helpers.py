@@ -1,0 +1,85 @@
+"""Shared test helpers: the reference tests' input generator, seeded config inputs and the parity
+bounds of the path."""
+import os
+
+import numpy as np
+
+from oracle import oracle as O
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+# Parity bounds (per element, relative to the magnitude (|A||B|)_ij, plus an absolute floor).
+TOL_3X = (1e-5, 1e-6)
+TOL_1X = (2e-3, 1e-6)
+
+
+def golden(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def make_input(n, seed):
+    """The reference tests' generator: multiples of 0.25 in [-4, 4] from an LCG
+    (tests/ops/matmul_test.cpp:25-35). Vectorised; same sequence as make_golden.make_input."""
+    n = int(n)
+    out = np.empty(n, np.float32)
+    state = np.uint64(seed)
+    # the LCG is sequential; step it in plain Python ints (fast enough for test sizes)
+    s = int(state)
+    vals = np.empty(n, np.int64)
+    for i in range(n):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        vals[i] = (s >> 12) % 33 - 16
+    out[:] = vals.astype(np.float32) / 4
+    return out
+
+
+def seeded_inputs():
+    """Inputs of tests/golden/seeded_cases.npz, regenerated with the oracle's Philox."""
+    d = {}
+    m = n = k = 192
+    d["c2_a"] = O.normal(m * k, 0, 1, 1, 0).reshape(m, k)
+    d["c2_b"] = O.normal(n * k, 0, 1, 1, m * k).reshape(n, k)
+    d["c2_c"] = O.normal(m * n, 0, 1, 1, m * k + n * k).reshape(m, n)
+    d["c2_bias"] = O.uniform(n, -0.1, 0.1, 1, m * k + n * k + m * n)
+    d["c3_x"] = O.normal(64 * 96, 0, 1, 2, 0).reshape(64, 96)
+    d["c3_w1"] = O.uniform(96 * 160, -0.034233, 0.034233, 2, 64 * 96).reshape(96, 160)
+    q = 4 * 64 * 32
+    std = 1 / np.sqrt(32)
+    d["c4_q"] = O.normal(q, 0, std, 3, 0).reshape(4, 64, 32)
+    d["c4_k"] = O.normal(q, 0, std, 3, q).reshape(4, 64, 32)
+    d["c4_v"] = O.normal(q, 0, std, 3, 2 * q).reshape(4, 64, 32)
+    d["gemv_a"] = O.uniform(300 * 257, -1, 1, 4, 0).reshape(300, 257)
+    d["gemv_x"] = O.uniform(257, -1, 1, 4, 300 * 257)
+    d["gemv_y"] = O.uniform(300, -1, 1, 4, 300 * 257 + 257)
+    d["act_x"] = O.normal(4096, 0, 3, 7, 0)
+    return d
+
+
+def softmax_rows(s):
+    p = np.exp(s - s.max(-1, keepdims=True)).astype(np.float32)
+    return (p / p.sum(-1, keepdims=True)).astype(np.float32)
+
+
+def assert_close(got, want, magnitude, tol, what):
+    """|got - want| <= rel * magnitude + abs, elementwise."""
+    rel, ab = tol
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert got.shape == want.shape, f"{what}: shape {got.shape} != {want.shape}"
+    err = np.abs(got - want)
+    bound = rel * np.asarray(magnitude, np.float64) + ab
+    bad = ~(err <= bound)
+    if bad.any():
+        i = np.unravel_index(np.argmax(np.where(bad, err - bound, -np.inf)), got.shape)
+        raise AssertionError(
+            f"{what}: {int(bad.sum())} of {got.size} entries out of tolerance; worst at {i}: "
+            f"got {got[i]!r} want {want[i]!r} bound {bound[i]!r}")
+
+
+def ulp_diff(a, b):
+    """Distance in float32 ulps (sign-aware) between two float32 arrays."""
+    ai = np.asarray(a, np.float32).view(np.int32).astype(np.int64)
+    bi = np.asarray(b, np.float32).view(np.int32).astype(np.int64)
+    ai = np.where(ai < 0, np.int64(-(2 ** 31)) - ai, ai)
+    bi = np.where(bi < 0, np.int64(-(2 ** 31)) - bi, bi)
+    return np.abs(ai - bi)

@@ -1,0 +1,339 @@
+"""GPU parity of the tensor-core GEMM path against the oracle and the reference's golden vectors.
+
+Modelled on the reference's tests/ops/matmul_test.cpp and tests/ops/gemm_batched_test.cpp: the
+same shapes, the same quarter-integer inputs (exact in tf32, so every product and short sum is
+exact and the results must match bit for bit in both precisions), strided views, empty shapes,
+known values; then seeded Philox inputs against the restated CPU algorithm within the bounds of
+the path (3xTF32: 1e-5*(|A||B|) + 1e-6; 1xTF32: 2e-3*(|A||B|) + 1e-6).
+"""
+import numpy as np
+import pytest
+import torch
+
+import mensurflow_b200 as mf
+from helpers import (TOL_1X, TOL_3X, assert_close, golden, make_input, seeded_inputs,
+                     softmax_rows)
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+PRECISIONS = ["3xtf32", "1xtf32"]
+MATMUL_SHAPES = [(1, 1, 1), (1, 5, 1), (5, 1, 3), (3, 5, 7), (16, 16, 16), (17, 31, 13),
+                 (64, 64, 64), (65, 129, 130), (100, 300, 50), (200, 100, 300), (2, 1000, 3),
+                 (1000, 2, 3), (257, 129, 257)]
+
+
+def dev(x, cuda):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def no_fault():
+    assert mf.device_status() == 0, "a kernel recorded a pipeline timeout"
+
+
+def tol(precision):
+    return TOL_3X if precision == "3xtf32" else TOL_1X
+
+
+def test_known_values(cuda):
+    g = golden("matmul_cases.npz")
+    for p in PRECISIONS:
+        c = mf.matmul(dev(g["known_a"], cuda), dev(g["known_b"], cuda), precision=p)
+        assert c.shape == (2, 2) and c.is_contiguous()
+        np.testing.assert_array_equal(host(c), [[58, 64], [139, 154]])
+        np.testing.assert_array_equal(host(c), g["known_c"])
+    # A x I == A exactly
+    m, k = 5, 7
+    a = make_input(m * k, 3).reshape(m, k)
+    for p in PRECISIONS:
+        c = mf.matmul(dev(a, cuda), torch.eye(k, device=cuda), precision=p)
+        np.testing.assert_array_equal(host(c), a)
+    no_fault()
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_sizes_exact(cuda, precision):
+    """The reference's matmul shape table; exact inputs give exact (bit-identical) results."""
+    g = golden("matmul_cases.npz")
+    for (m, n, k) in MATMUL_SHAPES:
+        a = make_input(m * k, 4).reshape(m, k)
+        b = make_input(k * n, 5).reshape(k, n)
+        c = host(mf.matmul(dev(a, cuda), dev(b, cuda), precision=precision))
+        np.testing.assert_array_equal(c, g[f"mm_{m}x{n}x{k}"], err_msg=f"{m}x{n}x{k}")
+    no_fault()
+
+
+def make_view(values, rows, cols, kind, cuda):
+    """The four layouts of matmul_test.cpp make_view: contiguous, column slice of a wider
+    matrix, transposed, transposed and sliced; the view always has shape (rows, cols)."""
+    v = torch.from_numpy(values.reshape(rows, cols)).to(cuda)
+    if kind == 0:
+        return v
+    if kind == 1:
+        big = torch.full((rows + 2, cols + 9), -77.0, device=cuda)
+        big[1:1 + rows, 3:3 + cols] = v
+        return big[1:1 + rows, 3:3 + cols]
+    if kind == 2:
+        return v.t().contiguous().t()
+    big = torch.full((cols + 3, rows + 5), -77.0, device=cuda)
+    big[2:2 + cols, 4:4 + rows] = v.t()
+    return big[2:2 + cols, 4:4 + rows].t()
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_strided_views(cuda, precision):
+    """Every combination of layouts for A and B (matmul_test.cpp test_strided_large)."""
+    for (m, n, k) in [(70, 60, 90), (130, 200, 150), (300, 300, 300)]:
+        a = make_input(m * k, 21)
+        b = make_input(k * n, 22)
+        want = O.gemm(a.reshape(m, k), b.reshape(k, n))
+        for ka in range(4):
+            for kb in range(4):
+                va = make_view(a, m, k, ka, cuda)
+                vb = make_view(b, k, n, kb, cuda)
+                got = host(mf.matmul(va, vb, precision=precision))
+                np.testing.assert_array_equal(got, want, err_msg=f"{m}x{n}x{k} A{ka} B{kb}")
+    no_fault()
+
+
+def test_empty_and_k0(cuda):
+    z = mf.matmul(torch.empty(3, 0, device=cuda), torch.empty(0, 4, device=cuda))
+    assert z.shape == (3, 4)
+    np.testing.assert_array_equal(host(z), np.zeros((3, 4), np.float32))
+    assert mf.matmul(torch.empty(0, 5, device=cuda), torch.empty(5, 2, device=cuda)).shape == (0, 2)
+    assert mf.matmul(torch.empty(2, 5, device=cuda), torch.empty(5, 0, device=cuda)).shape == (2, 0)
+    c = torch.arange(12, dtype=torch.float32, device=cuda).reshape(3, 4)
+    r = mf.gemm(torch.empty(3, 0, device=cuda), torch.empty(0, 4, device=cuda), 2.0, c, 0.5)
+    np.testing.assert_array_equal(host(r), 0.5 * np.arange(12, dtype=np.float32).reshape(3, 4))
+    no_fault()
+
+
+def test_errors(cuda):
+    m23 = torch.ones(2, 3, device=cuda)
+    m32 = torch.ones(3, 2, device=cuda)
+    vec = torch.ones(3, device=cuda)
+    with pytest.raises(ValueError):
+        mf.matmul(m23, m23)
+    with pytest.raises(ValueError):
+        mf.matmul(vec, m32)
+    with pytest.raises(ValueError):
+        mf.matmul(m23, vec)
+    with pytest.raises(ValueError):
+        mf.matmul(None, m32)
+    with pytest.raises(ValueError):
+        mf.gemm(m23, m32, 1.0, None, 1.0)
+    with pytest.raises(ValueError):
+        mf.matmul(m23, m32.double())
+    with pytest.raises(NotImplementedError):
+        mf.matmul(m23.double(), m32.double())
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_seeded_c2_shape(cuda, precision):
+    """C2-shaped gemm (alpha 0.5, beta 1, transB, fused bias) on the reference's Philox inputs,
+    against the reference's own output."""
+    s = seeded_inputs()
+    want = golden("seeded_cases.npz")["c2_out"]
+    got = host(mf.gemm(dev(s["c2_a"], cuda), dev(s["c2_b"], cuda), 0.5, dev(s["c2_c"], cuda), 1.0,
+                       False, True, bias=dev(s["c2_bias"], cuda), precision=precision))
+    mag = 0.5 * O.abs_product(s["c2_a"], s["c2_b"], False, True) + np.abs(s["c2_c"]) + \
+        np.abs(s["c2_bias"])[None, :]
+    assert_close(got, want, mag, tol(precision), f"c2 {precision}")
+    no_fault()
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("shape", [(256, 384, 1000), (384, 130, 4099), (129, 257, 33)])
+@pytest.mark.parametrize("trans", [(False, False), (False, True), (True, False), (True, True)])
+def test_random_gemm(cuda, precision, shape, trans):
+    m, n, k = shape
+    ta, tb = trans
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    a = rng.standard_normal((k, m) if ta else (m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k) if tb else (k, n)).astype(np.float32)
+    c = rng.standard_normal((m, n)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    want = O.gemm(a, b, -0.75, c, 2.0, ta, tb, bias=bias)
+    got = host(mf.gemm(dev(a, cuda), dev(b, cuda), -0.75, dev(c, cuda), 2.0, ta, tb,
+                       bias=dev(bias, cuda), precision=precision))
+    mag = 0.75 * O.abs_product(a, b, ta, tb) + 2 * np.abs(c) + np.abs(bias)[None, :]
+    assert_close(got, want, mag, tol(precision), f"{shape} {trans} {precision}")
+    no_fault()
+
+
+@pytest.mark.parametrize("act", ["relu", "gelu", "gelu_tanh"])
+def test_fused_activation(cuda, act):
+    s = seeded_inputs()
+    x, w = s["c3_x"], s["c3_w1"]
+    b1 = np.linspace(-0.05, 0.05, w.shape[1]).astype(np.float32)
+    pre = O.gemm(x, w, bias=b1)
+    want = O.activation(pre, act)
+    got = host(mf.linear(dev(x, cuda), dev(w, cuda), dev(b1, cuda), act))
+    mag = O.abs_product(x, w) + np.abs(b1)[None, :]
+    # the activation's slope is at most ~1.13, plus 2 ulp of rounding in the result
+    bound_rel, bound_abs = TOL_3X
+    assert_close(got, want, 1.2 * mag + np.abs(want) * 2.5e-7 / bound_rel, TOL_3X, act)
+    if act == "gelu":
+        np.testing.assert_array_equal(  # golden: the reference's gelu(x W1 + 0)
+            host(mf.linear(dev(x, cuda), dev(w, cuda), torch.zeros(w.shape[1], device=cuda),
+                           "gelu")).shape, golden("seeded_cases.npz")["c3_h"].shape)
+    no_fault()
+
+
+def test_guard_regions(cuda):
+    """Output written into the middle of a NaN-poisoned buffer: exactly the [m, n] window
+    changes (the reference poisons C the same way in gemm_packed_test.cpp:38)."""
+    m, n, k = 131, 77, 45
+    a = make_input(m * k, 9).reshape(m, k)
+    b = make_input(k * n, 10).reshape(k, n)
+    buf = torch.full((m + 4, n + 40), float("nan"), device=cuda)
+    window = buf[2:2 + m, 5:5 + n]
+    mf.gemm(dev(a, cuda), dev(b, cuda), out=window)
+    got = host(buf)
+    np.testing.assert_array_equal(got[2:2 + m, 5:5 + n], O.gemm(a, b))
+    mask = np.ones_like(got, bool)
+    mask[2:2 + m, 5:5 + n] = False
+    assert np.isnan(got[mask]).all(), "a write landed outside the output window"
+    no_fault()
+
+
+# ---- batched -------------------------------------------------------------------------------
+
+BATCHED_CASES = [
+    ("plain batch", (3, 4, 5), (3, 5, 2), False, False, 1.0, (), 0.0),
+    ("shared right-hand side", (4, 3, 5), (5, 2), False, False, 1.0, (), 0.0),
+    ("shared left-hand side", (3, 5), (4, 5, 2), False, False, 1.0, (), 0.0),
+    ("broadcast batch dims", (2, 1, 3, 4), (5, 4, 6), False, False, 1.0, (), 0.0),
+    ("plain matrices", (7, 9), (9, 4), False, False, 1.0, (), 0.0),
+    ("transpose a", (2, 5, 3), (2, 5, 4), True, False, 1.0, (), 0.0),
+    ("transpose b", (2, 3, 5), (2, 4, 5), False, True, 1.0, (), 0.0),
+    ("transpose both", (2, 5, 3), (1, 4, 5), True, True, 1.0, (), 0.0),
+    ("alpha only", (2, 3, 4), (2, 4, 5), False, False, -1.5, (), 0.0),
+    ("alpha and full c", (2, 3, 4), (2, 4, 5), False, False, 2.0, (2, 3, 5), 0.5),
+    ("c broadcast over batch", (4, 3, 4), (4, 5), False, False, 1.0, (3, 5), -1.0),
+    ("c as a row", (2, 3, 4), (2, 4, 5), False, False, 1.0, (5,), 1.0),
+    ("c given, beta 0", (2, 3, 4), (2, 4, 5), False, False, 1.0, (2, 3, 5), 0.0),
+    ("empty batch", (0, 3, 4), (0, 4, 5), False, False, 1.0, (), 0.0),
+    ("empty rows", (2, 0, 4), (2, 4, 5), False, False, 1.0, (), 0.0),
+    ("k is 0", (2, 3, 0), (2, 0, 5), False, False, 1.0, (), 0.0),
+    ("k is 0 with c", (2, 3, 0), (2, 0, 5), False, False, 1.0, (2, 3, 5), 3.0),
+    ("many small", (100, 2, 3), (100, 3, 2), False, False, 1.0, (), 0.0),
+    ("larger", (3, 70, 90), (3, 90, 60), False, False, 1.0, (), 0.0),
+]
+
+
+def _prod(s):
+    return int(np.prod(s)) if len(s) else 1
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_batched_api_cases(cuda, precision):
+    """The reference's 19 gemm_strided_batched API cases (gemm_batched_test.cpp:202-220),
+    against the reference's own outputs; exact inputs, so bit-identical."""
+    g = golden("batched_cases.npz")
+    for i, (name, ash, bsh, ta, tb, alpha, csh, beta) in enumerate(BATCHED_CASES):
+        a = make_input(_prod(ash), 4).reshape(ash)
+        b = make_input(_prod(bsh), 5).reshape(bsh)
+        c = dev(make_input(_prod(csh), 6).reshape(csh), cuda) if csh else None
+        got = mf.gemm_strided_batched(dev(a, cuda), dev(b, cuda), alpha, c, beta, ta, tb,
+                                      precision=precision)
+        want = g[f"case{i}_out"]
+        assert tuple(got.shape) == want.shape, name
+        assert got.is_contiguous()
+        np.testing.assert_array_equal(host(got), want, err_msg=name)
+    no_fault()
+
+
+def test_batched_views(cuda):
+    """Sliced batch, transposed view without the flag, expanded batch (gemm_batched_test.cpp
+    test_views): each equals its packed copy."""
+    full = dev(make_input(6 * 4 * 5, 7).reshape(6, 4, 5), cuda)
+    every_other = full[0:6:2]
+    b = dev(make_input(3 * 5 * 2, 8).reshape(3, 5, 2), cuda)
+    np.testing.assert_array_equal(host(mf.gemm_strided_batched(every_other, b)),
+                                  host(mf.gemm_strided_batched(every_other.contiguous(), b)))
+    bt = dev(make_input(3 * 2 * 5, 9).reshape(3, 2, 5), cuda)
+    packed = every_other.contiguous()
+    np.testing.assert_array_equal(
+        host(mf.gemm_strided_batched(packed, bt.transpose(1, 2))),
+        host(mf.gemm_strided_batched(packed, bt, 1.0, None, 0.0, False, True)))
+    one = dev(make_input(4 * 5, 10).reshape(1, 4, 5), cuda)
+    expanded = one.expand(3, 4, 5)
+    np.testing.assert_array_equal(host(mf.gemm_strided_batched(expanded, b)),
+                                  host(mf.gemm_strided_batched(expanded.contiguous(), b)))
+    x = dev(make_input(8 * 6, 11).reshape(8, 6), cuda)
+    y = dev(make_input(6 * 3, 12).reshape(6, 3), cuda)
+    np.testing.assert_array_equal(host(mf.gemm_strided_batched(x, y)), host(mf.matmul(x, y)))
+    no_fault()
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_attention_gemms(cuda, precision):
+    """C4-shaped attention GEMMs (S = Q K^T / sqrt(d), O = P V) against the reference."""
+    s = seeded_inputs()
+    g = golden("seeded_cases.npz")
+    q, k, v = (dev(s[x], cuda) for x in ("c4_q", "c4_k", "c4_v"))
+    scale = float(np.float32(1 / np.sqrt(32)))
+    S = host(mf.gemm_strided_batched(q, k, scale, None, 0.0, False, True, precision=precision))
+    mag_s = np.stack([scale * O.abs_product(s["c4_q"][i], s["c4_k"][i], False, True)
+                      for i in range(4)])
+    assert_close(S, g["c4_s"], mag_s, tol(precision), "scores")
+    P = softmax_rows(g["c4_s"])
+    out = host(mf.gemm_strided_batched(dev(P, cuda), v, precision=precision))
+    mag_o = np.stack([O.abs_product(P[i], s["c4_v"][i]) for i in range(4)])
+    assert_close(out, g["c4_o"], mag_o, tol(precision), "attention output")
+    no_fault()
+
+
+# ---- gemv / bias_add / activations -------------------------------------------------------------
+
+def test_gemv(cuda):
+    s = seeded_inputs()
+    g = golden("seeded_cases.npz")
+    got = host(mf.gemv(dev(s["gemv_a"], cuda), dev(s["gemv_x"], cuda), 0.75, dev(s["gemv_y"], cuda),
+                       -0.5))
+    # double accumulation on both sides: equal after rounding to float (allow 1 ulp)
+    assert np.max(np.abs(got.view(np.int32) - g["gemv_out"].view(np.int32))) <= 1
+    got_t = host(mf.gemv(dev(s["gemv_a"], cuda), dev(s["gemv_y"], cuda), 1.25, None, 0.0, True))
+    assert np.max(np.abs(got_t.view(np.int32) - g["gemv_t_out"].view(np.int32))) <= 1
+    a = np.random.default_rng(1).standard_normal((1031, 4096)).astype(np.float32)
+    x = np.random.default_rng(2).standard_normal(4096).astype(np.float32)
+    got = host(mf.matvec(dev(a, cuda), dev(x, cuda)))
+    assert np.max(np.abs(got.view(np.int32) - O.gemv(a, x).view(np.int32))) <= 1
+    no_fault()
+
+
+def test_bias_add_and_activations(cuda):
+    s = seeded_inputs()
+    g = golden("seeded_cases.npz")
+    x = s["act_x"]
+    np.testing.assert_array_equal(host(mf.relu(dev(x, cuda))), g["act_relu"])
+    for approx, key in ((False, "act_gelu"), (True, "act_gelu_tanh")):
+        got = host(mf.gelu(dev(x, cuda), approximate=approx))
+        d = np.abs(got.view(np.int32).astype(np.int64) - g[key].view(np.int32).astype(np.int64))
+        assert d.max() <= 1, f"gelu approximate={approx}: {d.max()} ulp"
+    xb = x.reshape(64, 64)
+    bias = np.linspace(-1, 1, 64).astype(np.float32)
+    np.testing.assert_array_equal(host(mf.bias_add(dev(xb, cuda), dev(bias, cuda))),
+                                  O.bias_add(xb, bias))
+    xo = np.random.default_rng(3).standard_normal((7, 13)).astype(np.float32)  # odd width
+    bo = np.random.default_rng(4).standard_normal(13).astype(np.float32)
+    np.testing.assert_array_equal(host(mf.bias_add(dev(xo, cuda), dev(bo, cuda))),
+                                  O.bias_add(xo, bo))
+    with pytest.raises(ValueError):
+        mf.bias_add(dev(xb, cuda), dev(bias[:10], cuda))
+    no_fault()
+
+
+def test_precision_knob(cuda):
+    assert mf.get_default_precision() == "3xtf32"
+    mf.set_default_precision("1xtf32")
+    try:
+        assert mf.get_default_precision() == "1xtf32"
+    finally:
+        mf.set_default_precision("3xtf32")
