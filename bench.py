@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 fp32 GEMM path (the reference's `gemm` + `bias_add` on CUDA).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--precision 3xtf32|1xtf32]
+                    [--impl mine|reference] [--workload c2|c5|gemv]
+
+Workload ("C2"): per rank, C = 0.5 * A @ B^T + 1.0 * C_in + bias with
+A, B, C_in [8192, 8192] ~ N(0, 1) and bias [8192] ~ U(-0.1, 0.1), fp32 in HBM, one fused call
+per step (3xTF32 by default). Under torchrun every rank owns one 8192-row block of an
+M = 8192*N problem with B and bias replicated, so per-GPU work is fixed ("scaling": "weak") and
+there is no collective on the data path. `value` is the whole-job TFLOP/s (2*M*N*K per step
+summed over ranks, divided by the max-over-ranks device time). The other workloads: `c5`
+(32768 x 32768 x 8192, row blocks split over the ranks: strong scaling) and `gemv`
+(65536 x 8192, HBM-bound).
+
+`--impl reference` times the reference's own CPU implementation (the unmodified library built
+from its sources into oracle/_ref) on a bounded row sample of the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fp32 GEMM TFLOP/s (3xTF32) at 1/2/4/8 B200 and % of TF32 tensor roofline"
+FALLBACK_BF16_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--precision", choices=["3xtf32", "1xtf32"], default="3xtf32")
+    p.add_argument("--impl", choices=["mine", "reference"], default="mine")
+    p.add_argument("--workload", choices=["c2", "c5", "gemv"], default="c2")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--size", type=int, default=8192,
+                   help="c2 only: M = N = K per rank (profiling captures use a smaller case)")
+    return p.parse_args()
+
+
+# ---- peaks ------------------------------------------------------------------------------------
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"bf16_burst": float(d["bf16_tflops"]),
+                "bf16_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"bf16_burst": FALLBACK_BF16_TFLOPS, "bf16_sustained": FALLBACK_BF16_TFLOPS,
+                "hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
+
+
+def profiled_traffic(workload: str, precision: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any
+    (a line `traffic_bytes_per_launch[<workload>/<precision>]: <bytes>`)."""
+    pat = re.compile(r"traffic_bytes_per_launch\[(\w+)/(\w+)\]:\s*([0-9.eE+]+)")
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for name in sorted(os.listdir(pdir)):
+        if not name.endswith((".md", ".txt")):
+            continue
+        with open(os.path.join(pdir, name)) as f:
+            for line in f:
+                m = pat.search(line)
+                if m and m.group(1) == workload and m.group(2) == precision:
+                    return float(m.group(3))
+    return None
+
+
+# ---- clocks -----------------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi sampled every 100 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)], stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) == 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---- distributed plumbing -------------------------------------------------------------------
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def emit(obj):
+    print(json.dumps(obj), flush=True)
+
+
+# ---- the reference arm / CPU baseline ----------------------------------------------------------
+
+def cpu_gemm_sample(m_full, n, k, target_s, reps, warmup=1):
+    """Times the reference's own public gemm (+ bias_add) on a row sample of the C2 workload.
+    Returns (seconds per call list, sample rows, kind, cores)."""
+    from oracle import oracle as O
+
+    ref = O.reference()
+    if ref is None:
+        return None
+    cores = int(ref.mfref_max_threads())
+    rows = 64
+    bench = O.RefGemmBench(rows, n, k, True, 1)
+    t = float(min(bench.run(0.5, 1.0, True, 2)))
+    bench.close()
+    rows = int(max(64, min(m_full, (target_s / max(t, 1e-6)) * rows)) // 64 * 64)
+    bench = O.RefGemmBench(rows, n, k, True, 1)
+    if warmup:
+        bench.run(0.5, 1.0, True, warmup)
+    secs = list(bench.run(0.5, 1.0, True, reps))
+    bench.close()
+    return secs, rows, "reference", cores
+
+
+def run_reference_arm(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    if args.workload != "c2":
+        emit({"impl": "reference", "unavailable": f"reference arm is implemented for the c2 "
+              f"workload (the headline); {args.workload} was asked"})
+        return 0
+    from oracle import oracle as O
+
+    if O.reference() is None:
+        emit({"impl": "reference", "unavailable": "oracle/_ref/libmfref.so (the reference built "
+              "from its sources) is not present on this machine"})
+        return 0
+    n = k = 8192
+    # each step is a bounded row sample sized to ~0.3 s so K steps end within minutes
+    res = cpu_gemm_sample(8192, n, k, target_s=0.3, reps=args.steps, warmup=args.warmup)
+    secs, rows, kind, cores = res
+    per = statistics.median(secs)
+    flops = 2.0 * rows * n * k
+    value = flops / per / 1e12
+    emit({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (the reference's Philox normal/uniform)",
+        "config": {"workload": "C2 gemm 8192^3 alpha=0.5 beta=1 transB + bias_add, CPU row sample",
+                   "sample_rows": rows, "n": n, "k": k},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": kind,
+                         "sample": f"{rows} of 8192 rows of A/C_in (B, bias full), "
+                                   f"median of {len(secs)} timed calls"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    })
+    return 0
+
+
+# ---- my arm -----------------------------------------------------------------------------------
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import mensurflow_b200 as mf
+    from mensurflow_b200 import _lib
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peaks = load_peaks()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    warm = max(3, args.warmup)
+
+    if args.workload in ("c2", "c5"):
+        if args.workload == "c2":
+            m = n = k = args.size               # per rank: weak scaling
+            scaling = "weak"
+            alpha, beta, use_bias, trans_b = 0.5, 1.0, True, True
+            wl = (f"C2: fused gemm C = 0.5*A@B^T + 1.0*C_in + bias, M=N=K={m} per rank "
+                  f"(row block of an M={m}*N problem, B replicated)")
+        else:
+            m_total, n, k = 32768, 32768, 8192  # strong scaling: rows split over ranks
+            if m_total % world:
+                raise SystemExit("c5: world size must divide 32768")
+            m = m_total // world
+            scaling = "strong"
+            alpha, beta, use_bias, trans_b = 1.0, 0.0, False, False
+            wl = "C5: gemm 32768x32768x8192, alpha=1 beta=0, rows split over ranks"
+        A = torch.randn(m, k, device=device, generator=gen)
+        B = torch.randn(n, k, device=device, generator=gen) if trans_b else \
+            torch.rand(k, n, device=device, generator=gen) * 2 - 1
+        if args.workload == "c5":
+            A.uniform_(-1, 1, generator=gen)
+        C_in = torch.randn(m, n, device=device, generator=gen) if beta != 0 else None
+        bias = (torch.rand(n, device=device, generator=gen) * 0.2 - 0.1) if use_bias else None
+        out = torch.empty(m, n, device=device)
+        flops_rank = 2.0 * m * n * k
+
+        def step():
+            mf.gemm(A, B, alpha, C_in, beta, False, trans_b, bias=bias, out=out,
+                    precision=args.precision)
+
+        unit = "TFLOP/s"
+        h2d_bytes = 4 * (A.numel() + B.numel() + (C_in.numel() if C_in is not None else 0) +
+                         (n if use_bias else 0))
+        d2h_bytes = 4 * out.numel()
+    else:
+        m, k = 65536, 8192
+        n = 1
+        scaling = "weak"
+        wl = "gemv: y = A x, A [65536, 8192] per rank, x [8192], double accumulation"
+        A = torch.rand(m, k, device=device, generator=gen) * 2 - 1
+        x = torch.rand(k, device=device, generator=gen) * 2 - 1
+        yout = torch.empty(m, device=device)
+        flops_rank = 2.0 * m * k
+        unit = "GB/s"
+        h2d_bytes = 4 * (A.numel() + k)
+        d2h_bytes = 4 * m
+
+        def step():
+            mf.matvec(A, x)
+
+    # warm-up
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    assert mf.device_status() == 0, "a kernel recorded a fault during warm-up"
+
+    # timed region (device time, max over ranks)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.25)
+    _lib.kernel_timer(True)
+    _lib.kernel_timer_read()
+    launches0 = _lib.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches = _lib.launch_count() - launches0
+    kern_ms, kern_n = _lib.kernel_timer_read()
+    _lib.kernel_timer(False)
+    clk = clocks.stop()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms_local)
+    kern_avg_ms = max_over_ranks(kern_ms / max(kern_n, 1))
+    assert mf.device_status() == 0, "a kernel recorded a fault during the timed region"
+
+    if args.workload == "gemv":
+        bytes_rank = 4.0 * (m * k + k + m)
+        value = world * bytes_rank / (ms * 1e-3) / 1e9
+        achieved = bytes_rank / (kern_avg_ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": profiled_traffic("gemv", "f64acc"),
+                    "peak_source": f"{peaks['source']} hbm_gbs (STREAM-style copy)",
+                    "algorithmic_bytes_per_launch": bytes_rank}
+    else:
+        value = world * flops_rank / (ms * 1e-3) / 1e12
+        achieved = flops_rank / (kern_avg_ms * 1e-3) / 1e12
+        per_product = 3.0 if args.precision == "3xtf32" else 1.0
+        # tcgen05 kind::tf32 runs at half the kind::f16 rate; 3xTF32 issues three MMAs per term.
+        # The kernel is timed in a sub-second burst at full clocks, so the burst figure is the
+        # denominator; the sustained (power-capped) one is reported beside it.
+        peak = peaks["bf16_burst"] / 2.0 / per_product
+        peak_sustained = peaks["bf16_sustained"] / 2.0 / per_product
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "frac_of_sustained_peak": achieved / peak_sustained,
+                    "traffic": profiled_traffic(args.workload, args.precision),
+                    "peak_source": (f"{peaks['source']} bf16 burst {peaks['bf16_burst']} "
+                                    f"TFLOP/s / 2 (TF32) / {int(per_product)} "
+                                    f"({args.precision})"),
+                    "kernel": "gemm_tc_kernel", "kernel_ms": kern_avg_ms,
+                    "algorithmic_flops_per_launch": flops_rank}
+
+    # end to end through the public API with host buffers (pinned), copies inside the timing
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e_steps = min(args.e2e_steps, args.steps)
+        if args.workload in ("c2", "c5"):
+            hA = A.cpu().pin_memory()
+            hB = B.cpu().pin_memory()
+            hC = C_in.cpu().pin_memory() if C_in is not None else None
+            hbias = bias.cpu().pin_memory() if bias is not None else None
+            hout = torch.empty(m, n, pin_memory=True)
+            dA, dB = torch.empty_like(A), torch.empty_like(B)
+            dC = torch.empty_like(C_in) if C_in is not None else None
+            dbias = torch.empty_like(bias) if bias is not None else None
+
+            def e2e_step():
+                dA.copy_(hA, non_blocking=True)
+                dB.copy_(hB, non_blocking=True)
+                if dC is not None:
+                    dC.copy_(hC, non_blocking=True)
+                if dbias is not None:
+                    dbias.copy_(hbias, non_blocking=True)
+                mf.gemm(dA, dB, alpha, dC, beta, False, trans_b, bias=dbias, out=out,
+                        precision=args.precision)
+                hout.copy_(out, non_blocking=True)
+        else:
+            hA = A.cpu().pin_memory()
+            hx = x.cpu().pin_memory()
+            hy = torch.empty(m, pin_memory=True)
+            dA, dx = torch.empty_like(A), torch.empty_like(x)
+
+            def e2e_step():
+                dA.copy_(hA, non_blocking=True)
+                dx.copy_(hx, non_blocking=True)
+                hy.copy_(mf.matvec(dA, dx), non_blocking=True)
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps)
+        barrier()
+        if args.workload == "gemv":
+            e_val = world * bytes_rank / (e_ms * 1e-3) / 1e9
+        else:
+            e_val = world * flops_rank / (e_ms * 1e-3) / 1e12
+        e2e = {"value": e_val, "unit": unit, "h2d_bytes_per_step": h2d_bytes,
+               "d2h_bytes_per_step": d2h_bytes, "ms_per_step": e_ms, "steps": e2e_steps,
+               "path": "pinned host -> device copies, mensurflow_b200 op (C ABI), device -> "
+                       "pinned host copy of the result, all inside the timed region"}
+
+    cpu_baseline = None
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "c2"
+            and args.size == 8192):
+        res = cpu_gemm_sample(8192, 8192, 8192, target_s=4.0, reps=3)
+        if res is not None:
+            secs, rows, kind, cores = res
+            per = statistics.median(secs)
+            cpu_baseline = {"value": 2.0 * rows * 8192 * 8192 / per / 1e12, "unit": "TFLOP/s",
+                            "cores": cores, "kind": kind,
+                            "sample": f"reference public gemm(+bias_add) on {rows} of 8192 rows "
+                                      f"(B full), median of 3 timed calls, {per:.2f} s each"}
+
+    if rank == 0:
+        emit({
+            "metric": METRIC if args.workload != "gemv" else "gemv HBM GB/s (65536x8192 fp32)",
+            "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded torch randn / uniform with the configs' distributions)",
+            "config": {"workload": wl, "precision": args.precision, "m_per_rank": m, "n": n,
+                       "k": k, "parallelism": f"dp{world} row-block shards, no collective",
+                       "l2": "inputs larger than L2 (each operand >= 256 MiB)"},
+            "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu_baseline,
+            "e2e": e2e, "clocks": clk,
+        })
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -138,6 +138,18 @@ int32_t mfk_get_default_precision(void);
  * MFK_ERR_DEVICE_FAULT when bits were set, or MFK_ERR_CUDA. */
 int mfk_device_status(uint32_t* bits, int32_t clear);
 
+/* Instrumentation (no counterpart in the reference's kernels; the reference times ops with
+ * host-side trace spans in run_on, src/core/dispatcher.cpp:298-317, which cannot see device time).
+ * mfk_kernel_timer(1) makes every later call record a CUDA event pair around its main kernel
+ * launch (the tensor-core GEMM, or the gemv kernel) on the caller's stream; mfk_kernel_timer_read
+ * waits for those events, returns the summed device time in ms and the number of timed launches,
+ * and forgets them. mfk_kernel_timer(0) stops recording. */
+int mfk_kernel_timer(int32_t enable);
+int mfk_kernel_timer_read(double* total_ms, int64_t* launches);
+
+/* Number of kernels this library has launched in this process (all entry points). */
+int64_t mfk_launch_count(void);
+
 /* Human-readable text of a status code (static storage). */
 const char* mfk_status_string(int32_t status);
 

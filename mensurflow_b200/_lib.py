@@ -37,6 +37,9 @@ EXPORTED = (
     "mfk_status_string",
     "mfk_last_cuda_error",
     "mfk_version",
+    "mfk_kernel_timer",
+    "mfk_kernel_timer_read",
+    "mfk_launch_count",
 )
 
 
@@ -106,6 +109,10 @@ def lib() -> ctypes.CDLL:
             so.mfk_status_string.restype = ctypes.c_char_p
             so.mfk_last_cuda_error.restype = ctypes.c_char_p
             so.mfk_version.restype = i32
+            so.mfk_kernel_timer.argtypes = [i32]
+            so.mfk_kernel_timer_read.argtypes = [ctypes.POINTER(ctypes.c_double),
+                                                 ctypes.POINTER(ctypes.c_int64)]
+            so.mfk_launch_count.restype = ctypes.c_int64
             _lib = so
     return _lib
 
@@ -129,3 +136,19 @@ def device_status(clear: bool = True) -> int:
     if rc not in (MFK_OK, MFK_ERR_DEVICE_FAULT):
         check(rc, "mfk_device_status")
     return int(bits.value)
+
+
+def kernel_timer(enable: bool) -> None:
+    check(lib().mfk_kernel_timer(1 if enable else 0), "mfk_kernel_timer")
+
+
+def kernel_timer_read():
+    """(summed device ms, number of timed launches) since the last read."""
+    ms = ctypes.c_double(0.0)
+    n = ctypes.c_int64(0)
+    check(lib().mfk_kernel_timer_read(ctypes.byref(ms), ctypes.byref(n)), "mfk_kernel_timer_read")
+    return ms.value, n.value
+
+
+def launch_count() -> int:
+    return int(lib().mfk_launch_count())

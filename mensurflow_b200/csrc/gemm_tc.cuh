@@ -5,13 +5,19 @@
 // (src/ops/blas.cpp:246-260, gemm_batched.cpp:12-28 finish_matrix, elementwise.cpp:128 bias_add).
 //
 // Design (sm_100a):
-//  * persistent: one CTA per SM walks output tiles (BM x BN) in a grouped raster order so the
-//    A and B panels in flight stay in L2;
-//  * warp-specialised, 256 threads: warp 0 issues TMA loads into an mbarrier ring of STAGES
-//    shared-memory stages; warp 1 owns TMEM and one lane issues tcgen05.mma; warps 4-7 are the
-//    epilogue (TMEM -> registers -> alpha/beta/bias/activation -> global);
+//  * persistent: one CTA (CG = 1) or one CTA pair (CG = 2, a 2-CTA cluster on neighbouring SMs)
+//    per output tile of (128*CG) x BN, walking tiles in a grouped raster order so the A and B
+//    panels in flight stay in L2;
+//  * warp-specialised, 256 threads per CTA: warp 0 issues TMA loads into an mbarrier ring of
+//    STAGES shared-memory stages; warp 1 owns TMEM and one lane of the pair's first CTA issues
+//    tcgen05.mma; warps 4-7 are the epilogue (TMEM -> registers -> alpha/beta/bias/activation ->
+//    global memory);
 //  * operands are K-major fp32 tiles of 32 elements (128 B) per row, SWIZZLE_128B, read by the
 //    MMA through shared-memory descriptors; kind::tf32 with an fp32 accumulator in TMEM;
+//  * CG = 2 (cta_group::2): each CTA of the pair loads its 128 rows of A and its BN/2 rows of B
+//    into its own shared memory (plain TMA loads, completion counted on the first CTA's
+//    barrier); one MMA of M = 256 reads both halves, so a CTA reads half the operand bytes per
+//    flop from shared memory and from L2 that a 1-CTA MMA would;
 //  * 3xTF32 (SPLIT3): each operand arrives as a (hi, lo) pair with hi = tf32(x), lo = tf32(x-hi)
 //    and three MMAs per k-step accumulate lo*hi + hi*lo + hi*hi (Ootomo & Yokota 2022; the
 //    split-precision "3xTF32" scheme); 1xTF32 issues one MMA per k-step;
@@ -22,7 +28,7 @@
 
 namespace mfk {
 
-constexpr int kBM = 128;          // rows of a tile = TMEM lanes
+constexpr int kBM = 128;          // rows of A per CTA = TMEM lanes
 constexpr int kBK = 32;           // fp32 depth per stage: one 128-byte swizzle row
 constexpr int kGemmThreads = 256;
 constexpr int kEpiWarp0 = 4;      // warps 4..7 are the epilogue warpgroup
@@ -53,12 +59,16 @@ struct GemmArgs {
     int act;
 };
 
-template <int BN, bool SPLIT3>
+// CG: CTAs per MMA (1 or 2). BN: N of one MMA (columns of the tile). Per CTA: kBM rows of A,
+// BN/CG rows of B, a kBM x BN accumulator in TMEM.
+template <int CG, int BN, bool SPLIT3>
 struct TcConfig {
+    static constexpr int kBRows = BN / CG;
+    static constexpr int kTileM = kBM * CG;
     static constexpr int kABytes = kBM * kBK * 4;
-    static constexpr int kBBytes = BN * kBK * 4;
+    static constexpr int kBBytes = kBRows * kBK * 4;
     static constexpr int kOps = SPLIT3 ? 2 : 1;
-    static constexpr int kStageBytes = kOps * (kABytes + kBBytes);
+    static constexpr int kStageBytes = kOps * (kABytes + kBBytes);  // per CTA
     static constexpr int kStages = (200 * 1024) / kStageBytes;
     static constexpr int kAccStages = 2;
     static constexpr int kTmemCols = (kAccStages * BN <= 32)    ? 32
@@ -66,11 +76,12 @@ struct TcConfig {
                                      : (kAccStages * BN <= 128) ? 128
                                      : (kAccStages * BN <= 256) ? 256
                                                                 : 512;
-    // stages (1024-aligned), then barriers and the TMEM address holder
     static constexpr int kBarrierBytes = 256;
     static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+    static_assert(CG == 1 || CG == 2, "one or two CTAs per MMA");
     static_assert(kAccStages * BN <= 512, "accumulators exceed TMEM");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be 32..256, multiple of 32");
+    static_assert(kBRows % 8 == 0, "B rows per CTA must be a multiple of 8");
     static_assert(kStages >= 2, "need at least two stages");
 };
 
@@ -132,32 +143,54 @@ __device__ __forceinline__ float epilogue_value(float acc, float alpha, float be
     return apply_act(v, act);
 }
 
-template <int BN, bool SPLIT3>
+template <int CG>
+__device__ __forceinline__ long long first_tile() {
+    return blockIdx.x / CG;
+}
+
+template <int CG>
+__device__ __forceinline__ long long tile_step() {
+    return gridDim.x / CG;
+}
+
+template <int CG, int BN, bool SPLIT3>
 __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap* tmA0,
                                             const CUtensorMap* tmA1, const CUtensorMap* tmB0,
                                             const CUtensorMap* tmB1, uint8_t* stages,
-                                            uint64_t* full, uint64_t* empty) {
-    using C = TcConfig<BN, SPLIT3>;
-    const uint64_t pol_a = l2_policy_evict_last();
-    const uint64_t pol_b = l2_policy_evict_last();
+                                            uint64_t* full, uint64_t* empty, uint32_t rank) {
+    using C = TcConfig<CG, BN, SPLIT3>;
+    const uint64_t pol = l2_policy_evict_last();
     int stage = 0;
     uint32_t phase = 0;
-    for (long long t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
+    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
         const TileCoord tc = tile_coord(g, t);
         const int za = g.a_batch_bcast ? 0 : tc.b;
         const int zb = g.b_batch_bcast ? 0 : tc.b;
+        const int ya = tc.tm * C::kTileM + static_cast<int>(rank) * kBM;
+        const int yb = tc.tn * BN + static_cast<int>(rank) * C::kBRows;
         for (int kb = 0; kb < g.num_kb; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, kErrProducerWait)) return;
             uint8_t* s = stages + stage * C::kStageBytes;
-            mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
             const int kx = kb * kBK;
-            tma_load_3d(s, tmA0, &full[stage], kx, tc.tm * kBM, za, pol_a);
-            tma_load_3d(s + C::kABytes, tmB0, &full[stage], kx, tc.tn * BN, zb, pol_b);
-            if constexpr (SPLIT3) {
-                tma_load_3d(s + C::kABytes + C::kBBytes, tmA1, &full[stage], kx, tc.tm * kBM, za,
-                            pol_a);
-                tma_load_3d(s + 2 * C::kABytes + C::kBBytes, tmB1, &full[stage], kx, tc.tn * BN,
-                            zb, pol_b);
+            if constexpr (CG == 1) {
+                mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+                tma_load_3d(s, tmA0, &full[stage], kx, ya, za, pol);
+                tma_load_3d(s + C::kABytes, tmB0, &full[stage], kx, yb, zb, pol);
+                if constexpr (SPLIT3) {
+                    tma_load_3d(s + C::kABytes + C::kBBytes, tmA1, &full[stage], kx, ya, za, pol);
+                    tma_load_3d(s + 2 * C::kABytes + C::kBBytes, tmB1, &full[stage], kx, yb, zb,
+                                pol);
+                }
+            } else {
+                // Both CTAs' bytes complete on the first CTA's barrier, which expects them all.
+                if (rank == 0) mbar_arrive_expect_tx(&full[stage], CG * C::kStageBytes);
+                const uint32_t bar = mapa_shared(&full[stage], 0);
+                tma_load_3d_cg2(s, tmA0, bar, kx, ya, za, pol);
+                tma_load_3d_cg2(s + C::kABytes, tmB0, bar, kx, yb, zb, pol);
+                if constexpr (SPLIT3) {
+                    tma_load_3d_cg2(s + C::kABytes + C::kBBytes, tmA1, bar, kx, ya, za, pol);
+                    tma_load_3d_cg2(s + 2 * C::kABytes + C::kBBytes, tmB1, bar, kx, yb, zb, pol);
+                }
             }
             if (++stage == C::kStages) {
                 stage = 0;
@@ -167,18 +200,20 @@ __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap
     }
 }
 
-template <int BN, bool SPLIT3>
+// Runs on one lane of the pair's first CTA (or of the single CTA).
+template <int CG, int BN, bool SPLIT3>
 __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, uint8_t* stages,
                                        uint64_t* full, uint64_t* empty, uint64_t* acc_full,
                                        uint64_t* acc_empty) {
-    using C = TcConfig<BN, SPLIT3>;
-    constexpr uint32_t idesc = idesc_tf32(kBM, BN, false, false);
+    using C = TcConfig<CG, BN, SPLIT3>;
+    constexpr uint32_t idesc = idesc_tf32(C::kTileM, BN, false, false);
+    constexpr uint16_t kPair = (1u << CG) - 1u;
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t stage0 = smem_u32(stages);
-    for (long long t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
+    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kErrMmaWait)) return;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -198,20 +233,38 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
                 if constexpr (SPLIT3) {
                     const uint64_t dal = smem_desc(a_lo + koff, 16, 1024, kSwizzle128B);
                     const uint64_t dbl = smem_desc(b_lo + koff, 16, 1024, kSwizzle128B);
-                    mma_tf32(d_tmem, dal, dbh, idesc, accumulate);
-                    mma_tf32(d_tmem, dah, dbl, idesc, 1u);
-                    mma_tf32(d_tmem, dah, dbh, idesc, 1u);
+                    if constexpr (CG == 1) {
+                        mma_tf32(d_tmem, dal, dbh, idesc, accumulate);
+                        mma_tf32(d_tmem, dah, dbl, idesc, 1u);
+                        mma_tf32(d_tmem, dah, dbh, idesc, 1u);
+                    } else {
+                        mma_tf32_cg2(d_tmem, dal, dbh, idesc, accumulate);
+                        mma_tf32_cg2(d_tmem, dah, dbl, idesc, 1u);
+                        mma_tf32_cg2(d_tmem, dah, dbh, idesc, 1u);
+                    }
                 } else {
-                    mma_tf32(d_tmem, dah, dbh, idesc, accumulate);
+                    if constexpr (CG == 1) {
+                        mma_tf32(d_tmem, dah, dbh, idesc, accumulate);
+                    } else {
+                        mma_tf32_cg2(d_tmem, dah, dbh, idesc, accumulate);
+                    }
                 }
             }
-            mma_commit(&empty[stage]);
+            if constexpr (CG == 1) {
+                mma_commit(&empty[stage]);
+            } else {
+                mma_commit_cg2_mc(&empty[stage], kPair);  // frees the stage in both CTAs
+            }
             if (++stage == C::kStages) {
                 stage = 0;
                 phase ^= 1u;
             }
         }
-        mma_commit(&acc_full[acc]);
+        if constexpr (CG == 1) {
+            mma_commit(&acc_full[acc]);
+        } else {
+            mma_commit_cg2_mc(&acc_full[acc], kPair);
+        }
         if (++acc == C::kAccStages) {
             acc = 0;
             acc_phase ^= 1u;
@@ -219,10 +272,11 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
     }
 }
 
-template <int BN, bool SPLIT3>
+template <int CG, int BN, bool SPLIT3>
 __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_base,
-                                            uint64_t* acc_full, uint64_t* acc_empty) {
-    using C = TcConfig<BN, SPLIT3>;
+                                            uint64_t* acc_full, uint64_t* acc_empty,
+                                            uint32_t rank) {
+    using C = TcConfig<CG, BN, SPLIT3>;
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int ew = warp - kEpiWarp0;  // TMEM lane quarter this warp may access
@@ -235,11 +289,11 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_bas
                          ((reinterpret_cast<uintptr_t>(g.c_in) & 15) == 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (long long t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
+    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
         const TileCoord tc = tile_coord(g, t);
         if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) return;
         tc_fence_after();
-        const int row = tc.tm * kBM + ew * 32 + lane;
+        const int row = tc.tm * C::kTileM + static_cast<int>(rank) * kBM + ew * 32 + lane;
         const bool row_ok = row < g.m;
         float* crow = g.c + static_cast<long long>(tc.b) * g.c_bs + static_cast<long long>(row) * g.ldc;
         const float* cin_row =
@@ -278,7 +332,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_bas
                     *reinterpret_cast<float4*>(crow + col0 + j) = o;
                 }
             } else {
-#pragma unroll 4
+#pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int col = col0 + j;
                     if (col < g.n) {
@@ -293,7 +347,13 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_bas
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (lane == 0) {
+            if constexpr (CG == 1) {
+                mbar_arrive(&acc_empty[acc]);
+            } else {
+                mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));  // the MMA issuer's CTA
+            }
+        }
         if (++acc == C::kAccStages) {
             acc = 0;
             acc_phase ^= 1u;
@@ -301,13 +361,13 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_bas
     }
 }
 
-template <int BN, bool SPLIT3>
+template <int CG, int BN, bool SPLIT3>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0,
                    const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmB1, const GemmArgs g) {
-    using C = TcConfig<BN, SPLIT3>;
+    using C = TcConfig<CG, BN, SPLIT3>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* stages = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -321,6 +381,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
+    const uint32_t rank = CG == 1 ? 0u : cluster_ctarank();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
@@ -329,7 +390,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int s = 0; s < C::kAccStages; ++s) {
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], 4);
+            mbar_init(&acc_empty[s], 4 * CG);  // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -342,31 +403,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_prefetch_desc(&tmB1);
         }
     }
-    if (warp == 1) tmem_alloc(tmem_holder, C::kTmemCols);
+    if (warp == 1) {
+        if constexpr (CG == 1) {
+            tmem_alloc(tmem_holder, C::kTmemCols);
+        } else {
+            tmem_alloc_cg2(tmem_holder, C::kTmemCols);
+        }
+    }
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // peer barriers initialised before any remote use
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
-        if (lane == 0) tc_producer<BN, SPLIT3>(g, &tmA0, &tmA1, &tmB0, &tmB1, stages, full, empty);
+        if (lane == 0)
+            tc_producer<CG, BN, SPLIT3>(g, &tmA0, &tmA1, &tmB0, &tmB1, stages, full, empty, rank);
     } else if (warp == 1) {
-        if (lane == 0) {
-            tc_mma<BN, SPLIT3>(g, tmem_base, stages, full, empty, acc_full, acc_empty);
+        if (lane == 0 && rank == 0) {
+            tc_mma<CG, BN, SPLIT3>(g, tmem_base, stages, full, empty, acc_full, acc_empty);
             // Every MMA issued above must finish before TMEM is released, also on an error exit.
-            mma_commit(drain);
+            if constexpr (CG == 1) {
+                mma_commit(drain);
+            } else {
+                mma_commit_cg2(drain);
+            }
             mbar_wait(drain, 0, kErrMmaWait);
         }
         __syncwarp();
     } else if (warp >= kEpiWarp0) {
-        tc_epilogue<BN, SPLIT3>(g, tmem_base, acc_full, acc_empty);
+        tc_epilogue<CG, BN, SPLIT3>(g, tmem_base, acc_full, acc_empty, rank);
     }
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // no CTA leaves while its peer may still signal it
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::kTmemCols);
+        if constexpr (CG == 1) {
+            tmem_dealloc(tmem_base, C::kTmemCols);
+        } else {
+            tmem_dealloc_cg2(tmem_base, C::kTmemCols);
+        }
     }
 }
 

@@ -28,6 +28,39 @@ std::atomic<int> g_default_precision{MFK_PRECISION_3XTF32};
 
 constexpr int kMaxDevices = 64;
 
+std::atomic<int64_t> g_launches{0};
+
+// Optional CUDA-event pairs around the main kernel launch of each call (mfk_kernel_timer).
+struct KernelTimer {
+    std::mutex mu;
+    bool enabled = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> spare;
+} g_timer;
+
+struct TimedLaunch {
+    cudaEvent_t stop = nullptr;
+    cudaStream_t stream;
+    explicit TimedLaunch(cudaStream_t s) : stream(s) {
+        std::lock_guard<std::mutex> lock(g_timer.mu);
+        if (!g_timer.enabled) return;
+        std::pair<cudaEvent_t, cudaEvent_t> ev{nullptr, nullptr};
+        if (!g_timer.spare.empty()) {
+            ev = g_timer.spare.back();
+            g_timer.spare.pop_back();
+        } else if (cudaEventCreate(&ev.first) != cudaSuccess ||
+                   cudaEventCreate(&ev.second) != cudaSuccess) {
+            return;
+        }
+        cudaEventRecord(ev.first, stream);
+        g_timer.pending.push_back(ev);
+        stop = ev.second;
+    }
+    ~TimedLaunch() {
+        if (stop != nullptr) cudaEventRecord(stop, stream);
+    }
+};
+
 int cuda_fail(cudaError_t e, const char* what) {
     t_cuda_error = std::string(what) + ": " + cudaGetErrorString(e);
     if (e == cudaErrorMemoryAllocation) return MFK_ERR_OUT_OF_MEMORY;
@@ -44,7 +77,8 @@ struct DeviceInfo {
     bool ready = false;
     int sm_count = 0;
     int major = 0, minor = 0;
-    bool smem_set[8] = {};
+    bool smem_set[16] = {};
+    int resident_units[16] = {};  // CTAs (CG = 1) or clusters (CG = 2) resident at once
 };
 
 std::mutex g_mutex;
@@ -159,24 +193,52 @@ bool can_read_direct(const Operand& o, int64_t k, bool split3) {
     return true;
 }
 
-template <int BN, bool SPLIT3>
+// One kernel instantiation per (CG, BN, SPLIT3); `slot` indexes its per-device set-up flags.
+template <int CG, int BN, bool SPLIT3>
 int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
               const CUtensorMap& b1, const GemmArgs& g, DeviceInfo* info, int slot,
               cudaStream_t stream) {
-    using C = mfk::TcConfig<BN, SPLIT3>;
-    auto kernel = mfk::gemm_tc_kernel<BN, SPLIT3>;
+    using C = mfk::TcConfig<CG, BN, SPLIT3>;
+    auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3>;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.blockDim = dim3(mfk::kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    if (CG > 1) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = CG;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
     {
         std::lock_guard<std::mutex> lock(g_mutex);
         if (!info->smem_set[slot]) {
             MFK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           C::kSmemBytes));
+            int units = info->sm_count / CG;
+            if (CG > 1) {
+                cfg.gridDim = dim3(static_cast<unsigned>(info->sm_count / CG * CG), 1, 1);
+                int clusters = 0;
+                if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess &&
+                    clusters > 0) {
+                    units = clusters;
+                }
+                cudaGetLastError();
+            }
+            info->resident_units[slot] = units;
             info->smem_set[slot] = true;
         }
     }
-    const long long grid = std::min<long long>(g.num_tiles, info->sm_count);
-    kernel<<<static_cast<unsigned>(grid), mfk::kGemmThreads, C::kSmemBytes, stream>>>(a0, a1, b0,
-                                                                                    b1, g);
-    MFK_CUDA(cudaGetLastError());
+    const long long units = std::min<long long>(g.num_tiles, info->resident_units[slot]);
+    cfg.gridDim = dim3(static_cast<unsigned>(units * CG), 1, 1);
+    {
+        TimedLaunch timed(stream);
+        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, a0, a1, b0, b1, g));
+    }
+    g_launches.fetch_add(1);
     return MFK_OK;
 }
 
@@ -235,11 +297,16 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         const long long total = static_cast<long long>(batch) * d->m * d->n;
         const long long blocks = std::min<long long>((total + 255) / 256, 65535LL * 8);
         mfk::epilogue_only_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(g);
+        g_launches.fetch_add(1);
         MFK_CUDA(cudaGetLastError());
         return MFK_OK;
     }
 
-    constexpr int BN = 128;
+    // Tile shape: a CTA pair (M = 256 per MMA) unless the problem has a single 128-row tile;
+    // N = 256 per MMA unless the output is at most 128 wide.
+    const int cg = d->m > mfk::kBM ? 2 : 1;
+    const int BN = (cg == 2 && d->n > 128) ? 256 : 128;
+    const int b_box_rows = BN / cg;
     const int64_t Kp = (d->k + mfk::kBK - 1) / mfk::kBK * mfk::kBK;
 
     Operand A{d->a, d->a_rs, d->a_cs, d->m,
@@ -266,7 +333,7 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         }
     };
     direct_map(A, mfk::kBM, &ma0, &ma1, &g.a_batch_bcast);
-    direct_map(B, BN, &mb0, &mb1, &g.b_batch_bcast);
+    direct_map(B, b_box_rows, &mb0, &mb1, &g.b_batch_bcast);
 
     // Workspace: packed operands plus device copies of non-arithmetic offset tables.
     const int nops = split3 ? 2 : 1;
@@ -316,6 +383,7 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
                 src, offs, o.bl.stride, o.rs, o.cs, static_cast<int>(o.rows),
                 static_cast<int>(d->k), static_cast<int>(Kp), o.hi + out_shift,
                 o.lo ? o.lo + out_shift : nullptr, mode, p_contig);
+            g_launches.fetch_add(1);
             MFK_CUDA(cudaGetLastError());
         }
         return MFK_OK;
@@ -333,19 +401,29 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         return ok;
     };
     if ((!A.direct && !packed_maps(A, mfk::kBM, &ma0, &ma1)) ||
-        (!B.direct && !packed_maps(B, BN, &mb0, &mb1))) {
+        (!B.direct && !packed_maps(B, b_box_rows, &mb0, &mb1))) {
         t_cuda_error = "cuTensorMapEncodeTiled rejected a packed operand";
         return MFK_ERR_UNSUPPORTED;
     }
 
     g.num_kb = static_cast<int>(Kp / mfk::kBK);
-    g.tiles_m = static_cast<int>((d->m + mfk::kBM - 1) / mfk::kBM);
+    g.tiles_m = static_cast<int>((d->m + mfk::kBM * cg - 1) / (mfk::kBM * cg));
     g.tiles_n = static_cast<int>((d->n + BN - 1) / BN);
-    g.group_m = 16;
+    // Tiles in flight form a group_m x (units / group_m) block; a square block keeps the fewest
+    // distinct A and B panels live in L2.
+    g.group_m = cg == 2 ? 8 : 12;
     g.num_tiles = static_cast<long long>(batch) * g.tiles_m * g.tiles_n;
 
-    if (split3) return launch_tc<BN, true>(ma0, ma1, mb0, mb1, g, info, 0, stream);
-    return launch_tc<BN, false>(ma0, ma1, mb0, mb1, g, info, 1, stream);
+    if (cg == 2 && BN == 256) {
+        return split3 ? launch_tc<2, 256, true>(ma0, ma1, mb0, mb1, g, info, 0, stream)
+                      : launch_tc<2, 256, false>(ma0, ma1, mb0, mb1, g, info, 1, stream);
+    }
+    if (cg == 2) {
+        return split3 ? launch_tc<2, 128, true>(ma0, ma1, mb0, mb1, g, info, 2, stream)
+                      : launch_tc<2, 128, false>(ma0, ma1, mb0, mb1, g, info, 3, stream);
+    }
+    return split3 ? launch_tc<1, 128, true>(ma0, ma1, mb0, mb1, g, info, 4, stream)
+                  : launch_tc<1, 128, false>(ma0, ma1, mb0, mb1, g, info, 5, stream);
 }
 
 }  // namespace
@@ -378,6 +456,8 @@ int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_
     if (rc != MFK_OK) return rc;
     if (!transpose) {
         const bool vec = incx == 1 && lda % 4 == 0 && aligned16(a) && aligned16(x);
+        TimedLaunch timed(stream);
+        g_launches.fetch_add(1);
         if (vec) {
             const int64_t warps = (rows + mfk::kGemvRowsPerWarp - 1) / mfk::kGemvRowsPerWarp;
             const int64_t blocks = (warps * 32 + mfk::kGemvThreads - 1) / mfk::kGemvThreads;
@@ -400,7 +480,9 @@ int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_
     MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&partial),
                              sizeof(double) * chunks * std::max<int64_t>(cols, 1), stream));
     const unsigned bx = static_cast<unsigned>((cols + 255) / 256);
+    g_launches.fetch_add(2);
     if (rows > 0) {
+        TimedLaunch timed(stream);
         mfk::gemv_t_partial_kernel<<<dim3(bx, static_cast<unsigned>(chunks)), 256, 0, stream>>>(
             a, rows, cols, lda, x, incx, partial);
     } else {
@@ -431,6 +513,7 @@ int mfk_bias_act_f32(const float* x, const float* bias, float* out, int64_t rows
     int rc = current_device(&dev, &info);
     if (rc != MFK_OK) return rc;
     const int64_t max_blocks = static_cast<int64_t>(info->sm_count) * 8;
+    g_launches.fetch_add(1);
     if (cols % 4 == 0 && aligned16(x) && aligned16(out)) {
         const int64_t total4 = total / 4;
         const int64_t blocks = std::min<int64_t>((total4 + 255) / 256, max_blocks);
@@ -467,6 +550,31 @@ int mfk_device_status(uint32_t* bits, int32_t clear) {
     *bits = v;
     return v != 0 ? MFK_ERR_DEVICE_FAULT : MFK_OK;
 }
+
+int mfk_kernel_timer(int32_t enable) {
+    std::lock_guard<std::mutex> lock(g_timer.mu);
+    g_timer.enabled = enable != 0;
+    return MFK_OK;
+}
+
+int mfk_kernel_timer_read(double* total_ms, int64_t* launches) {
+    if (total_ms == nullptr || launches == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> lock(g_timer.mu);
+    double sum = 0.0;
+    for (auto& ev : g_timer.pending) {
+        MFK_CUDA(cudaEventSynchronize(ev.second));
+        float ms = 0.0f;
+        MFK_CUDA(cudaEventElapsedTime(&ms, ev.first, ev.second));
+        sum += ms;
+        g_timer.spare.push_back(ev);
+    }
+    *total_ms = sum;
+    *launches = static_cast<int64_t>(g_timer.pending.size());
+    g_timer.pending.clear();
+    return MFK_OK;
+}
+
+int64_t mfk_launch_count(void) { return g_launches.load(); }
 
 const char* mfk_status_string(int32_t status) {
     switch (status) {

@@ -52,9 +52,13 @@ def _same(op: str, *ts):
         raise ValueError(f"{op}: dtypes differ")
     if any(t.device != ts[0].device for t in ts):
         raise ValueError(f"{op}: tensors are on different devices; move one with Tensor::to()")
-    if ts[0].dtype != torch.float32:
-        raise NotImplementedError(f"{op}: no kernel for dtype {ts[0].dtype} on {ts[0].device}")
-    if ts[0].device.type != "cuda":
+
+
+def _kernel_for(op: str, t: torch.Tensor):
+    """The reference's NotImplemented (dispatcher.cpp:263-268): no kernel for this dtype/device."""
+    if t.dtype != torch.float32:
+        raise NotImplementedError(f"{op}: no kernel for dtype {t.dtype} on {t.device}")
+    if t.device.type != "cuda":
         raise NotImplementedError(f"{op}: these kernels run on CUDA devices only")
 
 
@@ -109,6 +113,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch
         raise ValueError(f"gemm: bias must be [{n}], got {tuple(bias.shape)}")
     if activation not in _ACTS:
         raise ValueError(f"gemm: unknown activation {activation!r}")
+    _kernel_for("gemm", a)
     if bias is not None:
         bias = bias.contiguous()
     if out is None:
@@ -191,6 +196,7 @@ def gemm_strided_batched(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0,
                              f"{out_shape}")
         if beta != 0.0:
             initial = c.expand(out_shape)
+    _kernel_for(op, a)
     out = torch.empty(out_shape, dtype=torch.float32, device=a.device)
     batch = int(np.prod(batch_shape)) if batch_shape else 1
     if out.numel() == 0:
@@ -239,6 +245,7 @@ def gemv(a: torch.Tensor, x: torch.Tensor, alpha: float = 1.0, y: Optional[torch
         raise ValueError("gemv: input length does not match matrix dimensions")
     if y is not None and y.shape[0] != n_out:
         raise ValueError("gemv: output length does not match matrix dimensions")
+    _kernel_for("gemv", a)
     if a.stride(1) != 1 or (rows > 1 and a.stride(0) < cols):
         a = a.contiguous()
     out = torch.empty(n_out, dtype=torch.float32, device=a.device)
@@ -262,6 +269,7 @@ def matvec(a: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
 
 
 def _bias_act(x: torch.Tensor, bias: Optional[torch.Tensor], act: int, op: str) -> torch.Tensor:
+    _kernel_for(op, x)
     x = x.contiguous()
     out = torch.empty_like(x)
     cols = x.shape[-1] if x.dim() > 0 else 1

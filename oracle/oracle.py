@@ -96,8 +96,13 @@ def reference():
                 so.mfref_relu.argtypes = [_ptr, _i64, _ptr]
                 so.mfref_gemv.argtypes = [_ptr, _i64, _i64, _ptr, _f32, _ptr, _f32, ctypes.c_int, _ptr]
                 so.mfref_matvec.argtypes = [_ptr, _i64, _i64, _ptr, _ptr]
-                so.mfref_time_gemm.argtypes = [_i64, _i64, _i64, _f32, _f32, ctypes.c_int,
-                                               ctypes.c_int, _u64, ctypes.c_int, ctypes.c_int, _ptr]
+                so.mfref_gemm_bench_new.argtypes = [_i64, _i64, _i64, ctypes.c_int, _u64]
+                so.mfref_gemm_bench_new.restype = ctypes.c_void_p
+                so.mfref_gemm_bench_run.argtypes = [_ptr, _f32, _f32, ctypes.c_int, ctypes.c_int,
+                                                    _ptr]
+                so.mfref_gemm_bench_free.argtypes = [_ptr]
+                so.mfref_max_threads.restype = ctypes.c_int
+                so.mfref_openmp.restype = ctypes.c_int
                 so.mfref_time_gemv.argtypes = [_i64, _i64, _u64, ctypes.c_int, ctypes.c_int, _ptr]
                 so.mfref_set_threads.argtypes = [ctypes.c_int]
                 _ref = so
@@ -300,11 +305,24 @@ def ref_gemv(a, x, alpha=1.0, y=None, beta=0.0, transpose_a=False):
     return out
 
 
-def ref_time_gemm(m, n, k, alpha, beta, transpose_b, with_bias, seed, warmup, reps):
-    secs = np.zeros(reps, np.float64)
-    _check_ref(reference().mfref_time_gemm(m, n, k, alpha, beta, int(transpose_b), int(with_bias),
-                                           seed, warmup, reps, _p(secs)))
-    return secs
+class RefGemmBench:
+    """The reference's public gemm (+ bias_add) on CPU inputs made once by its own factories."""
+
+    def __init__(self, m, n, k, transpose_b, seed):
+        self.h = reference().mfref_gemm_bench_new(m, n, k, int(transpose_b), seed)
+        if not self.h:
+            raise RuntimeError(reference().mfref_last_error().decode())
+
+    def run(self, alpha, beta, with_bias, reps):
+        secs = np.zeros(reps, np.float64)
+        _check_ref(reference().mfref_gemm_bench_run(self.h, alpha, beta, int(with_bias), reps,
+                                                     _p(secs)))
+        return secs
+
+    def close(self):
+        if self.h:
+            reference().mfref_gemm_bench_free(self.h)
+            self.h = None
 
 
 def ref_time_gemv(rows, cols, seed, warmup, reps):

@@ -170,44 +170,51 @@ int mfref_matvec(const float* a, std::int64_t m, std::int64_t k, const float* x,
         [&] { copy_out(matvec(host_tensor(a, {m, k}), host_tensor(x, {k}), Execution::CPU), out); });
 }
 
-// Times the reference's public gemm (+ bias_add when with_bias) on CPU-resident inputs made by
-// its own normal() factory: A [m,k], B [n,k] read transposed when transpose_b (else [k,n]),
-// C_in [m,n]. Runs `warmup` untimed calls, then `reps` timed calls; writes each call's seconds
-// into seconds[0..reps). Inputs are created outside the timed region.
-int mfref_time_gemm(std::int64_t m, std::int64_t n, std::int64_t k, float alpha, float beta,
-                    int transpose_b, int with_bias, std::uint64_t seed, int warmup, int reps,
-                    double* seconds) {
+// Timing harness for the CPU baselines: inputs are made once by the reference's own normal() /
+// uniform() factories (outside any timed region), then each run times `reps` calls of the
+// reference's public gemm (+ bias_add) exactly as a user would make them.
+struct GemmBench {
+    Tensor a, b, c, bias;
+    bool transpose_b = false;
+};
+
+void* mfref_gemm_bench_new(std::int64_t m, std::int64_t n, std::int64_t k, int transpose_b,
+                           std::uint64_t seed) {
+    GemmBench* h = nullptr;
+    const int rc = guarded([&] {
+        auto* g = new GemmBench;
+        g->transpose_b = transpose_b != 0;
+        g->a = normal({m, k}, 0.0f, 1.0f, seed, 0, Execution::CPU);
+        g->b = g->transpose_b
+                   ? normal({n, k}, 0.0f, 1.0f, seed, std::uint64_t(m * k), Execution::CPU)
+                   : normal({k, n}, 0.0f, 1.0f, seed, std::uint64_t(m * k), Execution::CPU);
+        g->c = normal({m, n}, 0.0f, 1.0f, seed, std::uint64_t(m * k + n * k), Execution::CPU);
+        g->bias = uniform({n}, -0.1f, 0.1f, seed, std::uint64_t(m * k + n * k + m * n),
+                          Execution::CPU);
+        h = g;
+    });
+    return rc == 0 ? h : nullptr;
+}
+
+int mfref_gemm_bench_run(void* handle, float alpha, float beta, int with_bias, int reps,
+                         double* seconds) {
     return guarded([&] {
-        const Tensor a = normal({m, k}, 0.0f, 1.0f, seed, 0, Execution::CPU);
-        const Tensor b = transpose_b ? normal({n, k}, 0.0f, 1.0f, seed, std::uint64_t(m * k),
-                                              Execution::CPU)
-                                     : normal({k, n}, 0.0f, 1.0f, seed, std::uint64_t(m * k),
-                                              Execution::CPU);
-        const Tensor c = normal({m, n}, 0.0f, 1.0f, seed, std::uint64_t(m * k + n * k),
-                                Execution::CPU);
-        const Tensor bias = uniform({n}, -0.1f, 0.1f, seed,
-                                    std::uint64_t(m * k + n * k + m * n), Execution::CPU);
-        auto once = [&] {
-            Tensor r = gemm(a, b, alpha, beta != 0.0f ? &c : nullptr, beta, false,
-                            transpose_b != 0, Execution::CPU);
-            if (with_bias) {
-                r = bias_add(r, bias, Execution::CPU);
-            }
-            return r;
-        };
-        for (int i = 0; i < warmup; ++i) {
-            once();
-        }
+        auto* g = static_cast<GemmBench*>(handle);
         for (int i = 0; i < reps; ++i) {
             const double t0 = now();
-            const Tensor r = once();
+            Tensor r = gemm(g->a, g->b, alpha, beta != 0.0f ? &g->c : nullptr, beta, false,
+                            g->transpose_b, Execution::CPU);
+            if (with_bias) {
+                r = bias_add(r, g->bias, Execution::CPU);
+            }
             seconds[i] = now() - t0;
-            (void)r;
         }
     });
 }
 
-// Times the reference's public gemv on A [rows, cols] and x [cols] from uniform(-1,1).
+void mfref_gemm_bench_free(void* handle) { delete static_cast<GemmBench*>(handle); }
+
+// Times the reference's public gemv on A [rows, cols] and x [cols] from uniform(-1, 1).
 int mfref_time_gemv(std::int64_t rows, std::int64_t cols, std::uint64_t seed, int warmup, int reps,
                     double* seconds) {
     return guarded([&] {
