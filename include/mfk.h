@@ -33,7 +33,8 @@ typedef enum mfk_status {
     MFK_ERR_CUDA = 3,             /* a CUDA runtime call failed (launch, attribute, copy) */
     MFK_ERR_OUT_OF_MEMORY = 4,    /* the stream-ordered workspace could not be allocated */
     MFK_ERR_NO_DEVICE = 5,        /* no sm_100 device is current */
-    MFK_ERR_DEVICE_FAULT = 6      /* a kernel recorded a fault (see mfk_device_status) */
+    MFK_ERR_DEVICE_FAULT = 6,     /* a kernel recorded a fault (see mfk_device_status) */
+    MFK_ERR_SCRATCH_LIMIT = 7     /* needs more than MFK_NOALLOC_SCRATCH_BYTES (no-alloc entry) */
 } mfk_status;
 
 /* Epilogue activation, applied after alpha/beta/bias: relu (elementwise.hpp:56), exact GELU
@@ -101,6 +102,30 @@ typedef struct mfk_batch_desc {
  * mensurflow::gemm and bias_add chain after it (src/ops/blas.cpp:234-262,
  * src/ops/elementwise.cpp:251-284). matmul is alpha = 1, beta = 0, no bias, no activation. */
 int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream);
+
+/* mfk_gemm_f32 for callers that cannot allocate device memory. No counterpart in the reference.
+ *
+ * Some hosts must not allocate on the device while they run: a serving process that reserves
+ * its whole memory plan at start-up, a framework whose own caching allocator owns every byte of
+ * the device, or a latency-critical loop where an allocation may synchronise with the device.
+ * mfk_gemm_f32 asks the stream-ordered allocator for the tf32 (hi, lo) operand copies; this entry
+ * point instead uses one fixed scratch array of MFK_NOALLOC_SCRATCH_BYTES that the library keeps
+ * in device memory (a static __device__ array: every GPU that loads the library holds it until
+ * the process exits). It calls no cudaMalloc/cudaFree or other allocating routine.
+ *
+ * Same descriptor, same arithmetic and same results as mfk_gemm_f32; the caller still provides
+ * every input and the output. The operand copies must fit: 4 bytes x (number of copies) x
+ * (rows of each packed operand) x k rounded up to 32, where 3xTF32 packs both A (m rows) and
+ * B (n rows) twice, and 1xTF32 packs only an operand TMA cannot read where it lies. Larger
+ * problems return MFK_ERR_SCRATCH_LIMIT before anything is launched.
+ *
+ * The first call on a device looks up the scratch array's device address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture. All calls share the
+ * one array and it keeps the previous call's contents (every byte a call reads is written by the
+ * same call first), so calls whose kernels overlap on the GPU — on different streams, or from
+ * different host threads — race on it; order them on one stream. */
+#define MFK_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream);
 
 /* gemm_strided_batched on CUDA. Replaces the OpId::GemmBatched kernel (CPU adapter:
  * src/backends/cpu/backend.cpp:239-293 -> cpu::gemm_batched_f32_parallel, gemm_batched.cpp:58)

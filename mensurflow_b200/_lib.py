@@ -20,6 +20,8 @@ MFK_ERR_CUDA = 3
 MFK_ERR_OUT_OF_MEMORY = 4
 MFK_ERR_NO_DEVICE = 5
 MFK_ERR_DEVICE_FAULT = 6
+MFK_ERR_SCRATCH_LIMIT = 7
+NOALLOC_SCRATCH_BYTES = 64 * 1024 * 1024
 
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_GELU_TANH = 0, 1, 2, 3
 PRECISION_DEFAULT, PRECISION_3XTF32, PRECISION_1XTF32 = -1, 0, 1
@@ -27,6 +29,7 @@ PRECISION_DEFAULT, PRECISION_3XTF32, PRECISION_1XTF32 = -1, 0, 1
 # Every symbol include/mfk.h declares.
 EXPORTED = (
     "mfk_gemm_f32",
+    "mfk_gemm_f32_noalloc",
     "mfk_gemm_strided_batched_f32",
     "mfk_gemv_f32",
     "mfk_matvec_f32",
@@ -97,6 +100,7 @@ def lib() -> ctypes.CDLL:
             so = ctypes.CDLL(LIB_PATH)
             vp, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
             so.mfk_gemm_f32.argtypes = [ctypes.POINTER(GemmDesc), vp]
+            so.mfk_gemm_f32_noalloc.argtypes = [ctypes.POINTER(GemmDesc), vp]
             so.mfk_gemm_strided_batched_f32.argtypes = [ctypes.POINTER(GemmDesc),
                                                         ctypes.POINTER(BatchDesc), vp]
             so.mfk_gemv_f32.argtypes = [vp, i64, i64, i64, i32, vp, i64, f32, f32, vp, vp, vp]

@@ -23,6 +23,17 @@ namespace {
 
 using mfk::GemmArgs;
 
+// Scratch of mfk_gemm_f32_noalloc: one fixed array per device, held for the life of the process.
+// Host code must not take its address directly (that is a host-side stand-in); the device
+// address comes from cudaGetSymbolAddress, once per device (DeviceInfo::noalloc_scratch).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MFK_NOALLOC_SCRATCH_BYTES];
+
+// A caller-fixed workspace used instead of the stream-ordered allocator.
+struct FixedScratch {
+    uint8_t* ptr;
+    size_t bytes;
+};
+
 thread_local std::string t_cuda_error;
 std::atomic<int> g_default_precision{MFK_PRECISION_3XTF32};
 
@@ -79,6 +90,7 @@ struct DeviceInfo {
     int major = 0, minor = 0;
     bool smem_set[16] = {};
     int resident_units[16] = {};  // CTAs (CG = 1) or clusters (CG = 2) resident at once
+    void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch on this device
 };
 
 std::mutex g_mutex;
@@ -257,7 +269,8 @@ int check_desc(const mfk_gemm_desc* d) {
     return MFK_OK;
 }
 
-int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream) {
+int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream,
+             const FixedScratch* fixed = nullptr) {
     int rc = check_desc(d);
     if (rc != MFK_OK) return rc;
     const int64_t batch = bd ? bd->batch : 1;
@@ -351,14 +364,19 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     if (!B.direct && B.bl.offsets) bo_off = reserve(sizeof(int64_t) * batch);
 
     uint8_t* ws = nullptr;
-    if (bytes > 0) MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream));
+    if (bytes > 0 && fixed != nullptr) {
+        if (bytes > fixed->bytes) return MFK_ERR_SCRATCH_LIMIT;
+        ws = fixed->ptr;
+    } else if (bytes > 0) {
+        MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream));
+    }
     struct Free {
         uint8_t* p;
         cudaStream_t s;
         ~Free() {
             if (p) cudaFreeAsync(p, s);
         }
-    } release{ws, stream};
+    } release{fixed != nullptr ? nullptr : ws, stream};
 
     auto pack = [&](Operand& o, size_t off, size_t offs_off) -> int {
         o.hi = reinterpret_cast<float*>(ws + off);
@@ -432,6 +450,25 @@ extern "C" {
 
 int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream) {
     return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream) {
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    FixedScratch scratch{nullptr, MFK_NOALLOC_SCRATCH_BYTES};
+    {
+        // Set-up, once per device with that device current: the array's device address.
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if (info->noalloc_scratch == nullptr) {
+            void* p = nullptr;
+            MFK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            info->noalloc_scratch = p;
+        }
+        scratch.ptr = static_cast<uint8_t*>(info->noalloc_scratch);
+    }
+    return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream), &scratch);
 }
 
 int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc* batch,
@@ -592,6 +629,8 @@ const char* mfk_status_string(int32_t status) {
         return "no sm_100 device is current";
     case MFK_ERR_DEVICE_FAULT:
         return "a kernel recorded a fault";
+    case MFK_ERR_SCRATCH_LIMIT:
+        return "the operand copies need more than the no-allocation entry point's fixed scratch";
     default:
         return "unknown status";
     }
