@@ -44,11 +44,13 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--precision", choices=["3xtf32", "1xtf32"], default="3xtf32")
     p.add_argument("--impl", choices=["mine", "reference"], default="mine")
-    p.add_argument("--workload", choices=["c2", "c5", "gemv"], default="c2")
+    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "gemv"], default="c2")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--size", type=int, default=8192,
                    help="c2 only: M = N = K per rank (profiling captures use a smaller case)")
+    p.add_argument("--mnk", type=str, default=None,
+                   help="c2 only: 'M,N,K' per rank instead of --size (profiling other shapes)")
     return p.parse_args()
 
 
@@ -247,12 +249,16 @@ def main():
     gen.manual_seed(1000 + rank)
     warm = max(3, args.warmup)
 
+    e2e_factory = None
+    gather_step = None
     if args.workload in ("c2", "c5"):
         if args.workload == "c2":
             m = n = k = args.size               # per rank: weak scaling
+            if args.mnk:
+                m, n, k = (int(v) for v in args.mnk.split(","))
             scaling = "weak"
             alpha, beta, use_bias, trans_b = 0.5, 1.0, True, True
-            wl = (f"C2: fused gemm C = 0.5*A@B^T + 1.0*C_in + bias, M=N=K={m} per rank "
+            wl = (f"C2: fused gemm C = 0.5*A@B^T + 1.0*C_in + bias, M={m} N={n} K={k} per rank "
                   f"(row block of an M={m}*N problem, B replicated)")
         else:
             m_total, n, k = 32768, 32768, 8192  # strong scaling: rows split over ranks
@@ -276,10 +282,80 @@ def main():
             mf.gemm(A, B, alpha, C_in, beta, False, trans_b, bias=bias, out=out,
                     precision=args.precision)
 
+        if args.workload == "c5" and world > 1:
+            from mensurflow_b200 import sharded
+
+            def gather_step():
+                return sharded.gather_rows(out, m * world)
+
         unit = "TFLOP/s"
         h2d_bytes = 4 * (A.numel() + B.numel() + (C_in.numel() if C_in is not None else 0) +
                          (n if use_bias else 0))
         d2h_bytes = 4 * out.numel()
+
+        def e2e_factory():
+            hA = A.cpu().pin_memory()
+            hB = B.cpu().pin_memory()
+            hC = C_in.cpu().pin_memory() if C_in is not None else None
+            hbias = bias.cpu().pin_memory() if bias is not None else None
+            hout = torch.empty(m, n, pin_memory=True)
+            dA, dB = torch.empty_like(A), torch.empty_like(B)
+            dC = torch.empty_like(C_in) if C_in is not None else None
+            dbias = torch.empty_like(bias) if bias is not None else None
+
+            def e2e_step():
+                dA.copy_(hA, non_blocking=True)
+                dB.copy_(hB, non_blocking=True)
+                if dC is not None:
+                    dC.copy_(hC, non_blocking=True)
+                if dbias is not None:
+                    dbias.copy_(hbias, non_blocking=True)
+                mf.gemm(dA, dB, alpha, dC, beta, False, trans_b, bias=dbias, out=out,
+                        precision=args.precision)
+                hout.copy_(out, non_blocking=True)
+            return e2e_step
+    elif args.workload == "c3":
+        rows, d_in, d_hid = 4096, 1024, 4096    # per rank: weak scaling
+        m, n, k = rows, d_in, d_hid
+        scaling = "weak"
+        wl = ("C3: MLP forward Y = gelu(X@W1 + b1)@W2 + b2, X [4096,1024], W1 [1024,4096], "
+              "W2 [4096,1024], two fused gemm calls (bias + exact GELU in the epilogue)")
+        X = torch.randn(rows, d_in, device=device, generator=gen)
+        lim = (6.0 / (d_in + d_hid)) ** 0.5
+        W1 = (torch.rand(d_in, d_hid, device=device, generator=gen) * 2 - 1) * lim
+        W2 = (torch.rand(d_hid, d_in, device=device, generator=gen) * 2 - 1) * lim
+        b1 = torch.zeros(d_hid, device=device)
+        b2 = torch.zeros(d_in, device=device)
+        flops_rank = 2.0 * rows * d_in * d_hid * 2
+        unit = "TFLOP/s"
+        h2d_bytes = d2h_bytes = 0
+
+        def step():
+            h = mf.linear(X, W1, b1, "gelu", precision=args.precision)
+            mf.linear(h, W2, b2, precision=args.precision)
+    elif args.workload == "c4":
+        heads_total, seq, dh = 32 * 16, 2048, 128
+        if heads_total % world:
+            raise SystemExit("c4: world size must divide 512")
+        bh = heads_total // world                # batch x heads split over ranks
+        m, n, k = seq, seq, dh
+        scaling = "strong"
+        scale = float(1.0 / dh ** 0.5)
+        wl = (f"C4: attention GEMMs S = Q@K^T/sqrt(128) and O = P@V, batch*heads=512 split "
+              f"over ranks ({bh} per rank), seq 2048, head_dim 128; P is a stand-in of S's shape "
+              f"(softmax is not on the timed path)")
+        std = 1.0 / dh ** 0.5
+        Q = torch.randn(bh, seq, dh, device=device, generator=gen) * std
+        K = torch.randn(bh, seq, dh, device=device, generator=gen) * std
+        V = torch.randn(bh, seq, dh, device=device, generator=gen) * std
+        P = torch.softmax(torch.randn(bh, seq, seq, device=device, generator=gen), -1)
+        flops_rank = 2.0 * (2.0 * bh * seq * seq * dh)
+        unit = "TFLOP/s"
+        h2d_bytes = d2h_bytes = 0
+
+        def step():
+            mf.gemm_strided_batched(Q, K, scale, None, 0.0, False, True, precision=args.precision)
+            mf.gemm_strided_batched(P, V, precision=args.precision)
     else:
         m, k = 65536, 8192
         n = 1
@@ -287,7 +363,6 @@ def main():
         wl = "gemv: y = A x, A [65536, 8192] per rank, x [8192], double accumulation"
         A = torch.rand(m, k, device=device, generator=gen) * 2 - 1
         x = torch.rand(k, device=device, generator=gen) * 2 - 1
-        yout = torch.empty(m, device=device)
         flops_rank = 2.0 * m * k
         unit = "GB/s"
         h2d_bytes = 4 * (A.numel() + k)
@@ -295,6 +370,18 @@ def main():
 
         def step():
             mf.matvec(A, x)
+
+        def e2e_factory():
+            hA = A.cpu().pin_memory()
+            hx = x.cpu().pin_memory()
+            hy = torch.empty(m, pin_memory=True)
+            dA, dx = torch.empty_like(A), torch.empty_like(x)
+
+            def e2e_step():
+                dA.copy_(hA, non_blocking=True)
+                dx.copy_(hx, non_blocking=True)
+                hy.copy_(mf.matvec(dA, dx), non_blocking=True)
+            return e2e_step
 
     # warm-up
     for _ in range(warm):
@@ -326,13 +413,15 @@ def main():
     clk = clocks.stop()
     ms_local = e0.elapsed_time(e1) / args.steps
     ms = max_over_ranks(ms_local)
-    kern_avg_ms = max_over_ranks(kern_ms / max(kern_n, 1))
+    # device time of the tensor-core (or gemv) kernels per step, max over ranks
+    kern_step_ms = max_over_ranks(kern_ms / args.steps)
+    kern_per_step = kern_n / args.steps
     assert mf.device_status() == 0, "a kernel recorded a fault during the timed region"
 
     if args.workload == "gemv":
         bytes_rank = 4.0 * (m * k + k + m)
         value = world * bytes_rank / (ms * 1e-3) / 1e9
-        achieved = bytes_rank / (kern_avg_ms * 1e-3) / 1e9
+        achieved = bytes_rank / (kern_step_ms * 1e-3) / 1e9
         peak = peaks["hbm_gbs"]
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": achieved / peak, "traffic": profiled_traffic("gemv", "f64acc"),
@@ -340,7 +429,7 @@ def main():
                     "algorithmic_bytes_per_launch": bytes_rank}
     else:
         value = world * flops_rank / (ms * 1e-3) / 1e12
-        achieved = flops_rank / (kern_avg_ms * 1e-3) / 1e12
+        achieved = flops_rank / (kern_step_ms * 1e-3) / 1e12
         per_product = 3.0 if args.precision == "3xtf32" else 1.0
         # tcgen05 kind::tf32 runs at half the kind::f16 rate; 3xTF32 issues three MMAs per term.
         # The kernel is timed in a sub-second burst at full clocks, so the burst figure is the
@@ -353,43 +442,15 @@ def main():
                     "peak_source": (f"{peaks['source']} bf16 burst {peaks['bf16_burst']} "
                                     f"TFLOP/s / 2 (TF32) / {int(per_product)} "
                                     f"({args.precision})"),
-                    "kernel": "gemm_tc_kernel", "kernel_ms": kern_avg_ms,
-                    "algorithmic_flops_per_launch": flops_rank}
+                    "kernel": "gemm_tc_kernel", "kernel_ms_per_step": kern_step_ms,
+                    "kernel_launches_per_step": kern_per_step,
+                    "algorithmic_flops_per_step": flops_rank}
 
     # end to end through the public API with host buffers (pinned), copies inside the timing
     e2e = None
-    if args.e2e_steps > 0:
+    if args.e2e_steps > 0 and e2e_factory is not None:
         e2e_steps = min(args.e2e_steps, args.steps)
-        if args.workload in ("c2", "c5"):
-            hA = A.cpu().pin_memory()
-            hB = B.cpu().pin_memory()
-            hC = C_in.cpu().pin_memory() if C_in is not None else None
-            hbias = bias.cpu().pin_memory() if bias is not None else None
-            hout = torch.empty(m, n, pin_memory=True)
-            dA, dB = torch.empty_like(A), torch.empty_like(B)
-            dC = torch.empty_like(C_in) if C_in is not None else None
-            dbias = torch.empty_like(bias) if bias is not None else None
-
-            def e2e_step():
-                dA.copy_(hA, non_blocking=True)
-                dB.copy_(hB, non_blocking=True)
-                if dC is not None:
-                    dC.copy_(hC, non_blocking=True)
-                if dbias is not None:
-                    dbias.copy_(hbias, non_blocking=True)
-                mf.gemm(dA, dB, alpha, dC, beta, False, trans_b, bias=dbias, out=out,
-                        precision=args.precision)
-                hout.copy_(out, non_blocking=True)
-        else:
-            hA = A.cpu().pin_memory()
-            hx = x.cpu().pin_memory()
-            hy = torch.empty(m, pin_memory=True)
-            dA, dx = torch.empty_like(A), torch.empty_like(x)
-
-            def e2e_step():
-                dA.copy_(hA, non_blocking=True)
-                dx.copy_(hx, non_blocking=True)
-                hy.copy_(mf.matvec(dA, dx), non_blocking=True)
+        e2e_step = e2e_factory()
         e2e_step()
         torch.cuda.synchronize()
         barrier()
@@ -411,9 +472,25 @@ def main():
                "path": "pinned host -> device copies, mensurflow_b200 op (C ABI), device -> "
                        "pinned host copy of the result, all inside the timed region"}
 
+    allgather = None
+    if gather_step is not None:
+        gather_step()
+        torch.cuda.synchronize()
+        barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(5):
+            gather_step()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        g_ms = max_over_ranks(g0.elapsed_time(g1) / 5)
+        allgather = {"ms": g_ms, "bytes_received_per_rank": 4 * m * n * (world - 1),
+                     "what": "NCCL all_gather_into_tensor of the C row blocks (timed separately)"}
+
     cpu_baseline = None
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "c2"
-            and args.size == 8192):
+            and args.size == 8192 and not args.mnk):
         res = cpu_gemm_sample(8192, 8192, 8192, target_s=4.0, reps=3)
         if res is not None:
             secs, rows, kind, cores = res
@@ -434,7 +511,7 @@ def main():
                        "k": k, "parallelism": f"dp{world} row-block shards, no collective",
                        "l2": "inputs larger than L2 (each operand >= 256 MiB)"},
             "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu_baseline,
-            "e2e": e2e, "clocks": clk,
+            "e2e": e2e, "clocks": clk, "allgather": allgather,
         })
     if world > 1:
         dist.destroy_process_group()

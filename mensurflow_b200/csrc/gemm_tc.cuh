@@ -57,6 +57,7 @@ struct GemmArgs {
     long long ldc, c_bs;
     const float* bias;
     int act;
+    int tma_store;     // 1: C is written by TMA stores through shared memory (tmC is valid)
 };
 
 // CG: CTAs per MMA (1 or 2). BN: N of one MMA (columns of the tile). Per CTA: kBM rows of A,
@@ -69,15 +70,19 @@ struct TcConfig {
     static constexpr int kBBytes = kBRows * kBK * 4;
     static constexpr int kOps = SPLIT3 ? 2 : 1;
     static constexpr int kStageBytes = kOps * (kABytes + kBBytes);  // per CTA
-    static constexpr int kStages = (200 * 1024) / kStageBytes;
+    static constexpr int kStages = (192 * 1024) / kStageBytes;
     static constexpr int kAccStages = 2;
     static constexpr int kTmemCols = (kAccStages * BN <= 32)    ? 32
                                      : (kAccStages * BN <= 64)  ? 64
                                      : (kAccStages * BN <= 128) ? 128
                                      : (kAccStages * BN <= 256) ? 256
                                                                 : 512;
+    // Epilogue staging: each of the 4 epilogue warps owns two 32 x 32 fp32 boxes (4 KB each).
+    static constexpr int kEpiBoxBytes = 32 * 32 * 4;
+    static constexpr int kEpiBytes = 4 * 2 * kEpiBoxBytes;
     static constexpr int kBarrierBytes = 256;
-    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + kBarrierBytes;
+    static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeded");
     static_assert(CG == 1 || CG == 2, "one or two CTAs per MMA");
     static_assert(kAccStages * BN <= 512, "accumulators exceed TMEM");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be 32..256, multiple of 32");
@@ -104,6 +109,9 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& g, long long t) 
     return c;
 }
 
+// Exact GELU, 0.5*v*erfc(-v/sqrt 2), evaluated in double as the reference does
+// (src/backends/cpu/ops/elementwise/elementwise.cpp:173-192). Used by the standalone
+// bias_add/activation kernel, where it matches the reference to 1 ulp.
 __device__ __forceinline__ float gelu_exact(float value) {
     if (isinf(value)) return value < 0.0f ? -0.0f : value;
     const double v = value;
@@ -119,6 +127,51 @@ __device__ __forceinline__ float gelu_tanh(float value) {
     return static_cast<float>(v * s);
 }
 
+// The same functions in fp32 for the GEMM epilogue, where double throughput would cost more
+// than the tile's MMAs. The erfc argument -v/sqrt(2) is carried as a float pair (the product's
+// rounding error recovered with an FMA) and erfcf is corrected to first order in the low part
+// (d/dx erfc(x) = -2/sqrt(pi) e^{-x^2}), so the deep negative tail keeps its relative accuracy.
+__device__ __forceinline__ float gelu_exact_f32(float v) {
+    if (isinf(v)) return v < 0.0f ? -0.0f : v;
+    const float c_hi = 0.70710677f;       // float(1/sqrt 2)
+    const float c_lo = 1.21016175e-08f;   // 1/sqrt 2 - c_hi
+    const float x = -v * c_hi;
+    const float xe = fmaf(-v, c_hi, -x) - v * c_lo;
+    float e = erfcf(x);
+    e = fmaf(-1.12837917f * expf(-x * x), xe, e);
+    return 0.5f * v * e;
+}
+
+// v * sigmoid(z), z = 2*sqrt(2/pi)*(v + 0.044715 v^3): z is accumulated as a float pair
+// (products' rounding errors recovered with FMAs, the sum with TwoSum) and exp(-|z|) corrected
+// to first order in the low part, since exp amplifies an argument error by |z|.
+__device__ __forceinline__ float gelu_tanh_f32(float v) {
+    // beyond |v| = 30 the sigmoid is 1 or underflows (z ~ 1270): v or -0, as in double
+    if (fabsf(v) > 30.0f) return v < 0.0f ? -0.0f : v;
+    const float a_hi = 1.59576917f, a_lo = -4.53406805e-08f;    // 2*sqrt(2/pi)
+    const float b_hi = 0.0713548139f, b_lo = 2.39883247e-09f;   // 2*sqrt(2/pi)*0.044715
+    const float v2 = v * v;
+    const float v2e = fmaf(v, v, -v2);
+    const float v3 = v2 * v;
+    const float v3e = fmaf(v2, v, -v3) + v2e * v;
+    const float z1 = a_hi * v;
+    const float z1e = fmaf(a_hi, v, -z1) + a_lo * v;
+    const float z2 = b_hi * v3;
+    const float z2e = fmaf(b_hi, v3, -z2) + b_lo * v3 + b_hi * v3e;
+    const float z = z1 + z2;
+    const float bb = z - z1;
+    const float ze = ((z1 - (z - bb)) + (z2 - bb)) + z1e + z2e;
+    const float sg = z >= 0.0f ? 1.0f : -1.0f;
+    const float w = expf(-fabsf(z)) * (1.0f - sg * ze);  // exp(-|z + ze|)
+    const float s = z >= 0.0f ? 1.0f / (1.0f + w) : w / (1.0f + w);
+    return v * s;
+}
+
+// Out-of-line copies for the epilogue's unrolled loops: one body in the instruction stream
+// instead of 32.
+__device__ __noinline__ float gelu_exact_f32_call(float v) { return gelu_exact_f32(v); }
+__device__ __noinline__ float gelu_tanh_f32_call(float v) { return gelu_tanh_f32(v); }
+
 __device__ __forceinline__ float apply_act(float v, int act) {
     switch (act) {
     case kActRelu:
@@ -132,6 +185,19 @@ __device__ __forceinline__ float apply_act(float v, int act) {
     }
 }
 
+__device__ __forceinline__ float apply_act_f32(float v, int act) {
+    switch (act) {
+    case kActRelu:
+        return v < 0.0f ? 0.0f : v;
+    case kActGelu:
+        return gelu_exact_f32(v);
+    case kActGeluTanh:
+        return gelu_tanh_f32(v);
+    default:
+        return v;
+    }
+}
+
 // The reference composes alpha*AB (mul), + beta*C (scal then add) and + bias (bias_add) as
 // separate fp32 operations; each rounding step is kept (no contraction into an FMA).
 __device__ __forceinline__ float epilogue_value(float acc, float alpha, float beta, float cin,
@@ -140,7 +206,7 @@ __device__ __forceinline__ float epilogue_value(float acc, float alpha, float be
     float v = alpha == 1.0f ? acc : __fmul_rn(alpha, acc);
     if (has_cin) v = __fadd_rn(v, __fmul_rn(beta, cin));
     if (has_bias) v = __fadd_rn(v, bias);
-    return apply_act(v, act);
+    return apply_act_f32(v, act);
 }
 
 template <int CG>
@@ -272,78 +338,147 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
     }
 }
 
+// The epilogue of one 32-column chunk of a thread's row: alpha, beta*C_in, bias, activation,
+// with the reference's rounding steps. The activation is applied in a separate pass over the 32
+// values so each unrolled loop stays short.
+struct EpiRow {
+    const float* cin_row;
+    bool has_cin, has_bias, vec_cin;
+};
+
+__device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow& e, int col0,
+                                                 const uint32_t (&r)[32], float (&v)[32]) {
+    if (col0 + 32 <= g.n && (!e.has_cin || e.vec_cin)) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            float4 cin4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e.has_cin) cin4 = *reinterpret_cast<const float4*>(e.cin_row + col0 + j);
+            const float c4[4] = {cin4.x, cin4.y, cin4.z, cin4.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float x = __uint_as_float(r[j + q]);
+                if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
+                if (e.has_cin) x = __fadd_rn(x, __fmul_rn(g.beta, c4[q]));
+                if (e.has_bias) x = __fadd_rn(x, g.bias[col0 + j + q]);
+                v[j + q] = x;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int col = col0 + j;
+            float x = __uint_as_float(r[j]);
+            if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
+            if (col < g.n) {
+                if (e.has_cin) x = __fadd_rn(x, __fmul_rn(g.beta, e.cin_row[static_cast<long long>(col) * g.c_in_cs]));
+                if (e.has_bias) x = __fadd_rn(x, g.bias[col]);
+            }
+            v[j] = x;
+        }
+    }
+    if (g.act == kActRelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = v[j] < 0.0f ? 0.0f : v[j];
+    } else if (g.act == kActGelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_exact_f32_call(v[j]);
+    } else if (g.act == kActGeluTanh) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f32_call(v[j]);
+    }
+}
+
 template <int CG, int BN, bool SPLIT3>
-__device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_base,
+__device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap* tmC,
+                                            uint8_t* epi_smem, uint32_t tmem_base,
                                             uint64_t* acc_full, uint64_t* acc_empty,
                                             uint32_t rank) {
     using C = TcConfig<CG, BN, SPLIT3>;
+    constexpr int kChunks = BN / 32;
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int ew = warp - kEpiWarp0;  // TMEM lane quarter this warp may access
+    EpiRow e;
     const bool has_cin = g.c_in != nullptr && g.beta != 0.0f;
-    const bool has_bias = g.bias != nullptr;
+    e.has_bias = g.bias != nullptr;
+    e.vec_cin = has_cin && g.c_in_cs == 1 && (g.c_in_rs % 4 == 0) && (g.c_in_bs % 4 == 0) &&
+                ((reinterpret_cast<uintptr_t>(g.c_in) & 15) == 0);
+    // Only alpha to apply: the warp-uniform short path.
+    const bool plain = !has_cin && !e.has_bias && g.act == kActNone;
     const bool vec_out = (g.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0) &&
                          (g.c_bs % 4 == 0);
-    const bool vec_cin = has_cin && g.c_in_cs == 1 && (g.c_in_rs % 4 == 0) &&
-                         (g.c_in_bs % 4 == 0) &&
-                         ((reinterpret_cast<uintptr_t>(g.c_in) & 15) == 0);
+    // This warp's two staging boxes (32 rows of 128 B, SWIZZLE_128B as the TMA store reads them).
+    const uint32_t box0 = smem_u32(epi_smem + ew * 2 * C::kEpiBoxBytes);
+    int box = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
         const TileCoord tc = tile_coord(g, t);
-        if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) return;
+        if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) break;
         tc_fence_after();
-        const int row = tc.tm * C::kTileM + static_cast<int>(rank) * kBM + ew * 32 + lane;
+        const int row0 = tc.tm * C::kTileM + static_cast<int>(rank) * kBM + ew * 32;
+        const int row = row0 + lane;
         const bool row_ok = row < g.m;
         float* crow = g.c + static_cast<long long>(tc.b) * g.c_bs + static_cast<long long>(row) * g.ldc;
-        const float* cin_row =
-            has_cin ? g.c_in + static_cast<long long>(tc.b) * g.c_in_bs +
-                          static_cast<long long>(row) * g.c_in_rs
-                    : nullptr;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN + c0);
-            tmem_ld_32x32b_x32(taddr, r);
-            const int col0 = tc.tn * BN + c0;
-            if (!row_ok || col0 >= g.n) continue;
-            if (col0 + 32 <= g.n && vec_out && (!has_cin || vec_cin)) {
+        e.has_cin = has_cin && row_ok;
+        e.cin_row = e.has_cin ? g.c_in + static_cast<long long>(tc.b) * g.c_in_bs +
+                                    static_cast<long long>(row) * g.c_in_rs
+                              : nullptr;
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
+                               static_cast<uint32_t>(acc * BN);
+        // Two register sets: the next chunk's TMEM load is in flight while this one is used.
+        uint32_t ra[32], rb[32];
+        tmem_ld_issue_32x32b_x32(tbase, ra);
+        tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    float4 cin4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (has_cin) cin4 = *reinterpret_cast<const float4*>(cin_row + col0 + j);
-                    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (has_bias) {
-                        b4.x = g.bias[col0 + j];
-                        b4.y = g.bias[col0 + j + 1];
-                        b4.z = g.bias[col0 + j + 2];
-                        b4.w = g.bias[col0 + j + 3];
+        for (int ci = 0; ci < kChunks; ++ci) {
+            uint32_t (&r)[32] = (ci & 1) ? rb : ra;
+            uint32_t (&rn)[32] = (ci & 1) ? ra : rb;
+            if (ci + 1 < kChunks) tmem_ld_issue_32x32b_x32(tbase + (ci + 1) * 32, rn);
+            const int col0 = tc.tn * BN + ci * 32;
+            if (col0 < g.n && row0 < g.m) {
+                float v[32];
+                if (plain) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float x = __uint_as_float(r[j]);
+                        v[j] = g.alpha == 1.0f ? x : __fmul_rn(g.alpha, x);
                     }
-                    float4 o;
-                    o.x = epilogue_value(__uint_as_float(r[j]), g.alpha, g.beta, cin4.x, has_cin,
-                                         b4.x, has_bias, g.act);
-                    o.y = epilogue_value(__uint_as_float(r[j + 1]), g.alpha, g.beta, cin4.y,
-                                         has_cin, b4.y, has_bias, g.act);
-                    o.z = epilogue_value(__uint_as_float(r[j + 2]), g.alpha, g.beta, cin4.z,
-                                         has_cin, b4.z, has_bias, g.act);
-                    o.w = epilogue_value(__uint_as_float(r[j + 3]), g.alpha, g.beta, cin4.w,
-                                         has_cin, b4.w, has_bias, g.act);
-                    *reinterpret_cast<float4*>(crow + col0 + j) = o;
+                } else {
+                    epilogue_general(g, e, col0, r, v);
                 }
-            } else {
+                if (g.tma_store) {
+                    const uint32_t buf = box0 + box * C::kEpiBoxBytes;
+                    if (lane == 0) bulk_wait_read<1>();  // the store issued from this box has read it
+                    __syncwarp();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int col = col0 + j;
-                    if (col < g.n) {
-                        const float cin =
-                            has_cin ? cin_row[static_cast<long long>(col) * g.c_in_cs] : 0.0f;
-                        const float bv = has_bias ? g.bias[col] : 0.0f;
-                        crow[col] = epilogue_value(__uint_as_float(r[j]), g.alpha, g.beta, cin,
-                                                   has_cin, bv, has_bias, g.act);
+                    for (int q = 0; q < 8; ++q) {
+                        st_shared_v4(buf + lane * 128 + ((q ^ (lane & 7)) << 4), v[4 * q],
+                                     v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(tmC, epi_smem + (buf - smem_u32(epi_smem)), col0, row0, tc.b);
+                        bulk_commit();
+                    }
+                    box ^= 1;
+                } else if (row_ok) {
+                    if (col0 + 32 <= g.n && vec_out) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            *reinterpret_cast<float4*>(crow + col0 + j) =
+                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (col0 + j < g.n) crow[col0 + j] = v[j];
+                        }
                     }
                 }
             }
+            if (ci + 1 < kChunks) tmem_ld_wait();
         }
         tc_fence_before();
         __syncwarp();
@@ -359,6 +494,9 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, uint32_t tmem_bas
             acc_phase ^= 1u;
         }
     }
+    // Stores must have finished reading shared memory (and landed) before the CTA exits.
+    if (g.tma_store && lane == 0) bulk_wait<0>();
+    __syncwarp();
 }
 
 template <int CG, int BN, bool SPLIT3>
@@ -366,12 +504,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0,
                    const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB0,
-                   const __grid_constant__ CUtensorMap tmB1, const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmB1,
+                   const __grid_constant__ CUtensorMap tmC, const GemmArgs g) {
     using C = TcConfig<CG, BN, SPLIT3>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* stages = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + C::kStages * C::kStageBytes);
+    uint8_t* epi_smem = stages + C::kStages * C::kStageBytes;  // 1024-aligned
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + C::kEpiBytes);
     uint64_t* full = bars;
     uint64_t* empty = full + C::kStages;
     uint64_t* acc_full = empty + C::kStages;
@@ -402,6 +542,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_prefetch_desc(&tmA1);
             tma_prefetch_desc(&tmB1);
         }
+        if (g.tma_store) tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
         if constexpr (CG == 1) {
@@ -432,7 +573,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         __syncwarp();
     } else if (warp >= kEpiWarp0) {
-        tc_epilogue<CG, BN, SPLIT3>(g, tmem_base, acc_full, acc_empty, rank);
+        tc_epilogue<CG, BN, SPLIT3>(g, &tmC, epi_smem, tmem_base, acc_full, acc_empty, rank);
     }
 
     tc_fence_before();

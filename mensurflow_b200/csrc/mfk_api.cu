@@ -153,6 +153,23 @@ bool make_kmajor_map(CUtensorMap* map, const float* base, int64_t depth, int64_t
     return r == CUDA_SUCCESS;
 }
 
+// The output C as a TMA store target: n columns x m rows x nmat matrices, row stride ldc, matrix
+// stride c_bs (elements), 32 x 32 boxes with the 128-byte swizzle the epilogue stages in.
+bool make_store_map(CUtensorMap* map, float* c, int64_t n, int64_t m, int64_t nmat, int64_t ldc,
+                    int64_t c_bs) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    if (nmat == 1) c_bs = ldc * std::max<int64_t>(m, 1);
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m),
+                          static_cast<cuuint64_t>(nmat)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ldc) * 4, static_cast<cuuint64_t>(c_bs) * 4};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, c, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Batch placement of one operand: matrix z starts at shift + z*stride elements, or at
 // offsets[z] when the caller's offsets are not evenly spaced.
 struct BatchLayout {
@@ -208,8 +225,8 @@ bool can_read_direct(const Operand& o, int64_t k, bool split3) {
 // One kernel instantiation per (CG, BN, SPLIT3); `slot` indexes its per-device set-up flags.
 template <int CG, int BN, bool SPLIT3>
 int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
-              const CUtensorMap& b1, const GemmArgs& g, DeviceInfo* info, int slot,
-              cudaStream_t stream) {
+              const CUtensorMap& b1, const CUtensorMap& cmap, const GemmArgs& g, DeviceInfo* info,
+              int slot, cudaStream_t stream) {
     using C = mfk::TcConfig<CG, BN, SPLIT3>;
     auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3>;
     cudaLaunchConfig_t cfg = {};
@@ -248,7 +265,7 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
     cfg.gridDim = dim3(static_cast<unsigned>(units * CG), 1, 1);
     {
         TimedLaunch timed(stream);
-        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, a0, a1, b0, b1, g));
+        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, a0, a1, b0, b1, cmap, g));
     }
     g_launches.fetch_add(1);
     return MFK_OK;
@@ -432,16 +449,23 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     g.group_m = cg == 2 ? 8 : 12;
     g.num_tiles = static_cast<long long>(batch) * g.tiles_m * g.tiles_n;
 
+    // C through TMA stores when its layout allows (16-byte aligned rows and matrices).
+    CUtensorMap mc;
+    std::memset(&mc, 0, sizeof(mc));
+    const bool c_ok = aligned16(d->c) && d->ldc % 4 == 0 && (batch == 1 || g.c_bs % 4 == 0) &&
+                      d->ldc < (int64_t(1) << 37) && g.c_bs >= 0 && g.c_bs < (int64_t(1) << 37);
+    g.tma_store = (c_ok && make_store_map(&mc, d->c, d->n, d->m, batch, d->ldc, g.c_bs)) ? 1 : 0;
+
     if (cg == 2 && BN == 256) {
-        return split3 ? launch_tc<2, 256, true>(ma0, ma1, mb0, mb1, g, info, 0, stream)
-                      : launch_tc<2, 256, false>(ma0, ma1, mb0, mb1, g, info, 1, stream);
+        return split3 ? launch_tc<2, 256, true>(ma0, ma1, mb0, mb1, mc, g, info, 0, stream)
+                      : launch_tc<2, 256, false>(ma0, ma1, mb0, mb1, mc, g, info, 1, stream);
     }
     if (cg == 2) {
-        return split3 ? launch_tc<2, 128, true>(ma0, ma1, mb0, mb1, g, info, 2, stream)
-                      : launch_tc<2, 128, false>(ma0, ma1, mb0, mb1, g, info, 3, stream);
+        return split3 ? launch_tc<2, 128, true>(ma0, ma1, mb0, mb1, mc, g, info, 2, stream)
+                      : launch_tc<2, 128, false>(ma0, ma1, mb0, mb1, mc, g, info, 3, stream);
     }
-    return split3 ? launch_tc<1, 128, true>(ma0, ma1, mb0, mb1, g, info, 4, stream)
-                  : launch_tc<1, 128, false>(ma0, ma1, mb0, mb1, g, info, 5, stream);
+    return split3 ? launch_tc<1, 128, true>(ma0, ma1, mb0, mb1, mc, g, info, 4, stream)
+                  : launch_tc<1, 128, false>(ma0, ma1, mb0, mb1, mc, g, info, 5, stream);
 }
 
 }  // namespace

@@ -337,3 +337,27 @@ def test_precision_knob(cuda):
         assert mf.get_default_precision() == "1xtf32"
     finally:
         mf.set_default_precision("3xtf32")
+
+
+@pytest.mark.parametrize("act,approx", [("gelu", False), ("gelu_tanh", True)])
+def test_epilogue_activation_accuracy(cuda, act, approx):
+    """The fused epilogue evaluates GELU in fp32 (erfcf with the argument carried as a float
+    pair). A k = 0 GEMM with beta = 1 returns act(0 + C_in) exactly, isolating the activation:
+    against the reference's double evaluation it stays within a few ulp (and relative 1e-6)."""
+    x = np.concatenate([seeded_inputs()["act_x"], np.linspace(-12, 12, 4001, dtype=np.float32),
+                        np.array([0.0, -0.0, 1e-30, -1e-30, 3.4e38, -3.4e38], np.float32)])
+    x = x.astype(np.float32).reshape(-1, 1)
+    c = dev(x, cuda)
+    got = host(mf.gemm(torch.empty(x.shape[0], 0, device=cuda), torch.empty(0, 1, device=cuda),
+                       1.0, c, 1.0, activation=act))
+    want = O.activation(x, act)
+    from helpers import ulp_diff
+    d = ulp_diff(got, want)
+    big = np.abs(want) > 1e-30
+    rel = np.abs(got[big].astype(np.float64) - want[big]) / np.abs(want[big].astype(np.float64))
+    print(f"{act}: max ulp {d.max()}, max rel {rel.max():.3e}")
+    assert d[np.abs(x) < 10].max() <= 8, f"{act}: {d.max()} ulp"
+    assert rel.max() <= 2e-6
+    ref_gelu = golden("seeded_cases.npz")["act_gelu_tanh" if approx else "act_gelu"]
+    assert ulp_diff(got[:4096, 0], ref_gelu).max() <= 8
+    no_fault()
