@@ -59,6 +59,7 @@ typedef enum mfk_precision {
 #define MFK_DEVERR_PRODUCER_TIMEOUT 0x1u
 #define MFK_DEVERR_MMA_TIMEOUT 0x2u
 #define MFK_DEVERR_EPILOGUE_TIMEOUT 0x4u
+#define MFK_DEVERR_CONVERT_TIMEOUT 0x8u
 
 /* One GEMM: c = act(alpha * op(A) op(B) + beta * c_in + bias).
  * op(A) is m x k with element (i, p) at a[i*a_rs + p*a_cs]; op(B) is k x n with element (p, j)
@@ -115,9 +116,10 @@ int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream);
  *
  * Same descriptor, same arithmetic and same results as mfk_gemm_f32; the caller still provides
  * every input and the output. The operand copies must fit: 4 bytes x (number of copies) x
- * (rows of each packed operand) x k rounded up to 32, where 3xTF32 packs both A (m rows) and
- * B (n rows) twice, and 1xTF32 packs only an operand TMA cannot read where it lies. Larger
- * problems return MFK_ERR_SCRATCH_LIMIT before anything is launched.
+ * (rows of each packed operand) x k rounded up to 32. 3xTF32 packs B (n rows) twice, and A
+ * (m rows) twice only when TMA cannot read it where it lies (not K-major, or rows not 16-byte
+ * aligned); 1xTF32 packs once only an operand TMA cannot read. Larger problems return
+ * MFK_ERR_SCRATCH_LIMIT before anything is launched.
  *
  * The first call on a device looks up the scratch array's device address (cudaGetSymbolAddress)
  * with that device current; make that first call before any stream capture. All calls share the

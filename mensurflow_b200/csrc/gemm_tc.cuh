@@ -32,11 +32,14 @@ constexpr int kBM = 128;          // rows of A per CTA = TMEM lanes
 constexpr int kBK = 32;           // fp32 depth per stage: one 128-byte swizzle row
 constexpr int kGemmThreads = 256;
 constexpr int kEpiWarp0 = 4;      // warps 4..7 are the epilogue warpgroup
+constexpr int kCvtWarp0 = 2;      // warps 2..3 split A in shared memory (ASPLIT kernels)
+constexpr int kCvtThreads = 64;
 
 enum : unsigned int {
     kErrProducerWait = 1u << 0,
     kErrMmaWait = 1u << 1,
     kErrEpilogueWait = 1u << 2,
+    kErrConvertWait = 1u << 3,
 };
 
 enum Activation : int { kActNone = 0, kActRelu = 1, kActGelu = 2, kActGeluTanh = 3 };
@@ -58,6 +61,7 @@ struct GemmArgs {
     const float* bias;
     int act;
     int tma_store;     // 1: C is written by TMA stores through shared memory (tmC is valid)
+    int raw_hi;        // ASPLIT: the MMA reads raw A as hi (truncating), write only lo
 };
 
 // CG: CTAs per MMA (1 or 2). BN: N of one MMA (columns of the tile). Per CTA: kBM rows of A,
@@ -219,13 +223,19 @@ __device__ __forceinline__ long long tile_step() {
     return gridDim.x / CG;
 }
 
-template <int CG, int BN, bool SPLIT3>
+// ASPLIT (3xTF32 only): A arrives as raw fp32 in the A_hi slot, completing on this CTA's own
+// a_full barrier, and the converter warps write hi (in place) and lo; B arrives pre-split.
+template <int CG, int BN, bool SPLIT3, bool ASPLIT>
 __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap* tmA0,
                                             const CUtensorMap* tmA1, const CUtensorMap* tmB0,
                                             const CUtensorMap* tmB1, uint8_t* stages,
-                                            uint64_t* full, uint64_t* empty, uint32_t rank) {
+                                            uint64_t* full, uint64_t* empty, uint64_t* a_full,
+                                            uint32_t rank) {
     using C = TcConfig<CG, BN, SPLIT3>;
+    static_assert(!ASPLIT || SPLIT3, "the in-kernel split is a 3xTF32 feature");
     const uint64_t pol = l2_policy_evict_last();
+    // bytes that complete on `full`: everything, or only B's pair when A has its own barrier
+    constexpr uint32_t kFullBytes = ASPLIT ? 2 * C::kBBytes : C::kStageBytes;
     int stage = 0;
     uint32_t phase = 0;
     for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
@@ -237,25 +247,98 @@ __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap
         for (int kb = 0; kb < g.num_kb; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, kErrProducerWait)) return;
             uint8_t* s = stages + stage * C::kStageBytes;
+            uint8_t* s_ahi = s;
+            uint8_t* s_bhi = s + C::kABytes;
+            uint8_t* s_alo = s + C::kABytes + C::kBBytes;
+            uint8_t* s_blo = s + 2 * C::kABytes + C::kBBytes;
             const int kx = kb * kBK;
+            if constexpr (ASPLIT) {
+                mbar_arrive_expect_tx(&a_full[stage], C::kABytes);
+                tma_load_3d(s_ahi, tmA0, &a_full[stage], kx, ya, za, pol);
+            }
             if constexpr (CG == 1) {
-                mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-                tma_load_3d(s, tmA0, &full[stage], kx, ya, za, pol);
-                tma_load_3d(s + C::kABytes, tmB0, &full[stage], kx, yb, zb, pol);
+                mbar_arrive_expect_tx(&full[stage], kFullBytes);
+                if constexpr (!ASPLIT) tma_load_3d(s_ahi, tmA0, &full[stage], kx, ya, za, pol);
+                tma_load_3d(s_bhi, tmB0, &full[stage], kx, yb, zb, pol);
                 if constexpr (SPLIT3) {
-                    tma_load_3d(s + C::kABytes + C::kBBytes, tmA1, &full[stage], kx, ya, za, pol);
-                    tma_load_3d(s + 2 * C::kABytes + C::kBBytes, tmB1, &full[stage], kx, yb, zb,
-                                pol);
+                    if constexpr (!ASPLIT) tma_load_3d(s_alo, tmA1, &full[stage], kx, ya, za, pol);
+                    tma_load_3d(s_blo, tmB1, &full[stage], kx, yb, zb, pol);
                 }
             } else {
                 // Both CTAs' bytes complete on the first CTA's barrier, which expects them all.
-                if (rank == 0) mbar_arrive_expect_tx(&full[stage], CG * C::kStageBytes);
+                if (rank == 0) mbar_arrive_expect_tx(&full[stage], CG * kFullBytes);
                 const uint32_t bar = mapa_shared(&full[stage], 0);
-                tma_load_3d_cg2(s, tmA0, bar, kx, ya, za, pol);
-                tma_load_3d_cg2(s + C::kABytes, tmB0, bar, kx, yb, zb, pol);
+                if constexpr (!ASPLIT) tma_load_3d_cg2(s_ahi, tmA0, bar, kx, ya, za, pol);
+                tma_load_3d_cg2(s_bhi, tmB0, bar, kx, yb, zb, pol);
                 if constexpr (SPLIT3) {
-                    tma_load_3d_cg2(s + C::kABytes + C::kBBytes, tmA1, bar, kx, ya, za, pol);
-                    tma_load_3d_cg2(s + 2 * C::kABytes + C::kBBytes, tmB1, bar, kx, yb, zb, pol);
+                    if constexpr (!ASPLIT) tma_load_3d_cg2(s_alo, tmA1, bar, kx, ya, za, pol);
+                    tma_load_3d_cg2(s_blo, tmB1, bar, kx, yb, zb, pol);
+                }
+            }
+            if (++stage == C::kStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+}
+
+// The converter warps of an ASPLIT kernel: for every stage, once this CTA's raw A tile has
+// landed, hi = tf32_rna(x) in place and lo = tf32_rna(x - hi) into the A_lo slot (an elementwise
+// pass, so the 128-byte swizzle of the tile carries over) — or, where the tensor cores are known
+// to truncate fp32 operands (g.raw_hi), only lo = tf32_rna(x - trunc(x)) — then a proxy fence
+// so the MMA's async reads see the generic writes, and one arrival per warp on the MMA issuer's
+// `converted` barrier.
+template <int CG, int BN, bool SPLIT3>
+__device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, uint64_t* a_full,
+                                           uint64_t* converted) {
+    using C = TcConfig<CG, BN, SPLIT3>;
+    const int ct = threadIdx.x - kCvtWarp0 * 32;
+    const int lane = threadIdx.x % 32;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+            if (!mbar_wait(&a_full[stage], phase, kErrConvertWait)) return;
+            float4* hi = reinterpret_cast<float4*>(stages + stage * C::kStageBytes);
+            float4* lo = reinterpret_cast<float4*>(stages + stage * C::kStageBytes + C::kABytes +
+                                                   C::kBBytes);
+            if (g.raw_hi) {
+                // the tensor cores truncate fp32 to tf32, so x already is hi: only lo is written
+#pragma unroll 4
+                for (int i = ct; i < C::kABytes / 16; i += kCvtThreads) {
+                    const float4 x = hi[i];
+                    float4 l;
+                    l.x = tf32_rna(x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u));
+                    l.y = tf32_rna(x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u));
+                    l.z = tf32_rna(x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u));
+                    l.w = tf32_rna(x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u));
+                    lo[i] = l;
+                }
+            } else {
+#pragma unroll 4
+                for (int i = ct; i < C::kABytes / 16; i += kCvtThreads) {
+                    const float4 x = hi[i];
+                    float4 h, l;
+                    h.x = tf32_rna(x.x);
+                    h.y = tf32_rna(x.y);
+                    h.z = tf32_rna(x.z);
+                    h.w = tf32_rna(x.w);
+                    l.x = tf32_rna(x.x - h.x);
+                    l.y = tf32_rna(x.y - h.y);
+                    l.z = tf32_rna(x.z - h.z);
+                    l.w = tf32_rna(x.w - h.w);
+                    hi[i] = h;
+                    lo[i] = l;
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (CG == 1) {
+                    mbar_arrive(&converted[stage]);
+                } else {
+                    mbar_arrive_cluster(mapa_shared(&converted[stage], 0));
                 }
             }
             if (++stage == C::kStages) {
@@ -267,10 +350,10 @@ __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap
 }
 
 // Runs on one lane of the pair's first CTA (or of the single CTA).
-template <int CG, int BN, bool SPLIT3>
+template <int CG, int BN, bool SPLIT3, bool ASPLIT>
 __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, uint8_t* stages,
                                        uint64_t* full, uint64_t* empty, uint64_t* acc_full,
-                                       uint64_t* acc_empty) {
+                                       uint64_t* acc_empty, uint64_t* converted) {
     using C = TcConfig<CG, BN, SPLIT3>;
     constexpr uint32_t idesc = idesc_tf32(C::kTileM, BN, false, false);
     constexpr uint16_t kPair = (1u << CG) - 1u;
@@ -285,6 +368,9 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < g.num_kb; ++kb) {
             if (!mbar_wait(&full[stage], phase, kErrMmaWait)) return;
+            if constexpr (ASPLIT) {
+                if (!mbar_wait(&converted[stage], phase, kErrMmaWait)) return;
+            }
             tc_fence_after();
             const uint32_t a_hi = stage0 + stage * C::kStageBytes;
             const uint32_t b_hi = a_hi + C::kABytes;
@@ -499,7 +585,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     __syncwarp();
 }
 
-template <int CG, int BN, bool SPLIT3>
+template <int CG, int BN, bool SPLIT3, bool ASPLIT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0,
                    const __grid_constant__ CUtensorMap tmA1,
@@ -517,7 +603,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* acc_full = empty + C::kStages;
     uint64_t* acc_empty = acc_full + C::kAccStages;
     uint64_t* drain = acc_empty + C::kAccStages;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* a_full = drain + 1;                // ASPLIT: raw A landed in this CTA
+    uint64_t* converted = a_full + C::kStages;   // ASPLIT: both CTAs' A split (first CTA's)
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(converted + C::kStages);
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -533,6 +621,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&acc_empty[s], 4 * CG);  // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
+        if constexpr (ASPLIT) {
+            for (int s = 0; s < C::kStages; ++s) {
+                mbar_init(&a_full[s], 1);
+                mbar_init(&converted[s], 2 * CG);  // both converter warps of every CTA
+            }
+        }
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -559,10 +653,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (warp == 0) {
         if (lane == 0)
-            tc_producer<CG, BN, SPLIT3>(g, &tmA0, &tmA1, &tmB0, &tmB1, stages, full, empty, rank);
+            tc_producer<CG, BN, SPLIT3, ASPLIT>(g, &tmA0, &tmA1, &tmB0, &tmB1, stages, full, empty,
+                                                a_full, rank);
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            tc_mma<CG, BN, SPLIT3>(g, tmem_base, stages, full, empty, acc_full, acc_empty);
+            tc_mma<CG, BN, SPLIT3, ASPLIT>(g, tmem_base, stages, full, empty, acc_full, acc_empty,
+                                           converted);
             // Every MMA issued above must finish before TMEM is released, also on an error exit.
             if constexpr (CG == 1) {
                 mma_commit(drain);
@@ -572,6 +668,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_wait(drain, 0, kErrMmaWait);
         }
         __syncwarp();
+    } else if (ASPLIT && warp >= kCvtWarp0 && warp < kCvtWarp0 + kCvtThreads / 32) {
+        tc_convert<CG, BN, SPLIT3>(g, stages, a_full, converted);
     } else if (warp >= kEpiWarp0) {
         tc_epilogue<CG, BN, SPLIT3>(g, &tmC, epi_smem, tmem_base, acc_full, acc_empty, rank);
     }

@@ -91,6 +91,9 @@ struct DeviceInfo {
     bool smem_set[16] = {};
     int resident_units[16] = {};  // CTAs (CG = 1) or clusters (CG = 2) resident at once
     void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    // Whether tcgen05 kind::tf32 reads an fp32 operand by truncating it to tf32 (measured once
+    // per device by a known-answer GEMM; until known, 3xTF32 splits hi explicitly).
+    std::atomic<int> tf32_truncates{-1};  // -1 unknown, 0 no, 1 yes
 };
 
 std::mutex g_mutex;
@@ -204,8 +207,7 @@ struct Operand {
     int64_t rs, cs;
     int64_t rows;
     BatchLayout bl;
-    bool direct = false;      // TMA straight from the caller's memory
-    bool bcast = false;       // direct with one shared matrix
+    bool direct = false;      // TMA reads the caller's memory
     float* hi = nullptr;      // packed copies (workspace)
     float* lo = nullptr;
     int64_t* dev_offsets = nullptr;
@@ -213,22 +215,30 @@ struct Operand {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Whether TMA can read the operand where it lies (1xTF32 only: 3xTF32 needs the split copy).
-bool can_read_direct(const Operand& o, int64_t k, bool split3) {
-    if (split3 || o.cs != 1 || o.bl.offsets != nullptr) return false;
+// Whether TMA can read the operand where it lies: K-major, 16-byte aligned rows and matrices.
+bool tma_readable(const Operand& o, int64_t k) {
+    if (o.cs != 1 || o.bl.offsets != nullptr) return false;
     if (!aligned16(o.ptr) || o.rs <= 0 || (o.rs % 4) != 0 || o.rs < k) return false;
     if (o.bl.stride < 0 || (o.bl.stride % 4) != 0) return false;
     if (o.rs >= (int64_t(1) << 37) || o.bl.stride >= (int64_t(1) << 37)) return false;
     return true;
 }
 
+// 1xTF32 reads a readable operand in place. 3xTF32 needs it split: the pre-pass costs 12 bytes of
+// HBM traffic per element once, the in-kernel split of A (converter warps) costs shared-memory
+// bandwidth on every N-tile of the product. Measured on B200 the in-kernel split wins below
+// N ~ 360 (C4's P @ V, N = 128: 8.1 -> 5.6 ms) and loses above (C3 4096^2 x 1024: 0.19 -> 0.26 ms).
+constexpr int64_t kInKernelSplitMaxN = 384;
+
+
+
 // One kernel instantiation per (CG, BN, SPLIT3); `slot` indexes its per-device set-up flags.
-template <int CG, int BN, bool SPLIT3>
+template <int CG, int BN, bool SPLIT3, bool ASPLIT>
 int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
               const CUtensorMap& b1, const CUtensorMap& cmap, const GemmArgs& g, DeviceInfo* info,
               int slot, cudaStream_t stream) {
     using C = mfk::TcConfig<CG, BN, SPLIT3>;
-    auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3>;
+    auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3, ASPLIT>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.blockDim = dim3(mfk::kGemmThreads, 1, 1);
@@ -271,6 +281,63 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
     return MFK_OK;
 }
 
+int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream,
+             const FixedScratch* fixed);
+
+// Known answer: 1xTF32 reads A in place; a = 1 + 3*2^-12 holds 0.75 ulp of tf32 beyond 1, so
+// a * 1 is 1 when the tensor cores truncate fp32 operands and 1 + 2^-10 when they round. Runs
+// once per device, on a private stream, only where allocating is allowed and the caller's
+// stream is not being captured; any failure leaves the explicit (always valid) split in use.
+bool tf32_truncates(DeviceInfo* info, cudaStream_t caller, bool may_allocate) {
+#ifdef MFK_FORCE_EXPLICIT_SPLIT
+    return false;  // build option: always split hi explicitly
+#endif
+    const int known = info->tf32_truncates.load();
+    if (known >= 0) return known == 1;
+    if (!may_allocate) return false;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(caller, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return false;
+    }
+    float host_a[32] = {}, host_b[32] = {}, host_c = 0.0f;
+    host_a[0] = 1.0f + 3.0f * 0x1p-12f;
+    host_b[0] = 1.0f;
+    float* buf = nullptr;
+    cudaStream_t s = nullptr;
+    int verdict = 0;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess &&
+        cudaMalloc(&buf, 4 * 96) == cudaSuccess &&
+        cudaMemcpyAsync(buf, host_a, sizeof(host_a), cudaMemcpyHostToDevice, s) == cudaSuccess &&
+        cudaMemcpyAsync(buf + 32, host_b, sizeof(host_b), cudaMemcpyHostToDevice, s) ==
+            cudaSuccess) {
+        mfk_gemm_desc d{};
+        d.a = buf;                // A [1, 32], row-major, read in place
+        d.a_rs = 32;
+        d.a_cs = 1;
+        d.b = buf + 32;           // B [32, 1]
+        d.b_rs = 1;
+        d.b_cs = 1;
+        d.c = buf + 64;
+        d.ldc = 1;
+        d.m = 1;
+        d.n = 1;
+        d.k = 32;
+        d.alpha = 1.0f;
+        d.precision = MFK_PRECISION_1XTF32;
+        if (run_gemm(&d, nullptr, s, nullptr) == MFK_OK &&
+            cudaMemcpyAsync(&host_c, buf + 64, 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+            cudaStreamSynchronize(s) == cudaSuccess) {
+            verdict = host_c == 1.0f ? 1 : 0;
+        }
+    }
+    if (buf != nullptr) cudaFree(buf);
+    if (s != nullptr) cudaStreamDestroy(s);
+    cudaGetLastError();
+    info->tf32_truncates.store(verdict);
+    return verdict == 1;
+}
+
 int check_desc(const mfk_gemm_desc* d) {
     if (d == nullptr) return MFK_ERR_INVALID_ARGUMENT;
     if (d->m < 0 || d->n < 0 || d->k < 0) return MFK_ERR_INVALID_ARGUMENT;
@@ -287,7 +354,7 @@ int check_desc(const mfk_gemm_desc* d) {
 }
 
 int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream,
-             const FixedScratch* fixed = nullptr) {
+             const FixedScratch* fixed) {
     int rc = check_desc(d);
     if (rc != MFK_OK) return rc;
     const int64_t batch = bd ? bd->batch : 1;
@@ -305,6 +372,10 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     const int precision = d->precision == MFK_PRECISION_DEFAULT ? g_default_precision.load()
                                                                  : d->precision;
     const bool split3 = precision == MFK_PRECISION_3XTF32;
+    // The in-kernel split of A may leave hi as the raw fp32 values where the tensor cores are
+    // known to truncate them (writing only lo: a third less shared-memory traffic).
+    const bool raw_hi = split3 && d->k > 0 && d->n <= kInKernelSplitMaxN &&
+                        tf32_truncates(info, stream, fixed == nullptr);
 
     GemmArgs g{};
     g.m = static_cast<int>(d->m);
@@ -348,11 +419,19 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     B.ptr += B.bl.shift;
 
     // Direct TMA reads when the layout allows; the maps are encoded now so that a layout the
-    // driver rejects falls back to packing instead of failing.
+    // driver rejects falls back to packing instead of failing. In 3xTF32 only A of a small-N
+    // product is read in place (split inside the kernel); every other operand is packed as an
+    // explicitly rounded (hi, lo) pair. Reading raw fp32 as hi elsewhere (the tensor cores
+    // truncate) saves a third of the pre-pass but measured ~9% slower on the 8192^3 kernel under
+    // the power cap: the 13 low bits left in hi keep toggling through shared memory and the MMA
+    // datapath, where rounded hi has them zeroed.
     CUtensorMap ma0, ma1, mb0, mb1;
     auto direct_map = [&](Operand& o, int box_rows, CUtensorMap* m0, CUtensorMap* m1,
                           int* bcast) {
-        if (!can_read_direct(o, d->k, split3)) return;
+        const bool is_a = &o == &A;
+        const bool in_kernel = split3 && is_a && d->n <= kInKernelSplitMaxN;
+        if (split3 && !in_kernel) return;
+        if (!tma_readable(o, d->k)) return;
         *bcast = (o.bl.stride == 0 && batch > 1) ? 1 : 0;
         const int64_t nmat = *bcast ? 1 : batch;
         if (make_kmajor_map(m0, o.ptr, d->k, o.rows, nmat, o.rs, o.bl.stride, box_rows)) {
@@ -368,6 +447,7 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     // Workspace: packed operands plus device copies of non-arithmetic offset tables.
     const int nops = split3 ? 2 : 1;
     auto packed_elems = [&](const Operand& o) { return o.rows * Kp * batch; };
+    auto copies = [&](const Operand& o) { return o.direct ? 0 : nops; };
     size_t bytes = 0;
     auto reserve = [&](size_t n) {
         const size_t off = bytes;
@@ -375,10 +455,10 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         return off;
     };
     size_t a_off = 0, b_off = 0, ao_off = 0, bo_off = 0;
-    if (!A.direct) a_off = reserve(sizeof(float) * packed_elems(A) * nops);
-    if (!B.direct) b_off = reserve(sizeof(float) * packed_elems(B) * nops);
-    if (!A.direct && A.bl.offsets) ao_off = reserve(sizeof(int64_t) * batch);
-    if (!B.direct && B.bl.offsets) bo_off = reserve(sizeof(int64_t) * batch);
+    if (copies(A)) a_off = reserve(sizeof(float) * packed_elems(A) * copies(A));
+    if (copies(B)) b_off = reserve(sizeof(float) * packed_elems(B) * copies(B));
+    if (copies(A) && A.bl.offsets) ao_off = reserve(sizeof(int64_t) * batch);
+    if (copies(B) && B.bl.offsets) bo_off = reserve(sizeof(int64_t) * batch);
 
     uint8_t* ws = nullptr;
     if (bytes > 0 && fixed != nullptr) {
@@ -404,6 +484,26 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
                                      cudaMemcpyHostToDevice, stream));
         }
         const int mode = split3 ? mfk::kPackSplit : mfk::kPackRound;
+        if (o.cs == 1 && o.rs % 4 == 0 && d->k % 4 == 0 && aligned16(o.ptr) &&
+            (o.dev_offsets != nullptr || o.bl.stride % 4 == 0)) {
+            // already K-major and aligned: a straight vectorised pass
+            bool offs_aligned = true;
+            if (o.bl.offsets) {
+                for (int64_t i = 0; i < batch && offs_aligned; ++i) offs_aligned = o.bl.offsets[i] % 4 == 0;
+            }
+            if (offs_aligned) {
+                const int64_t total4 = o.rows * (Kp / 4) * batch;
+                const int64_t blocks = std::min<int64_t>((total4 + 255) / 256,
+                                                         static_cast<int64_t>(info->sm_count) * 16);
+                mfk::pack_kmajor_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                    o.ptr, reinterpret_cast<const long long*>(o.dev_offsets), o.bl.stride, o.rs,
+                    static_cast<int>(o.rows), static_cast<int>(d->k), static_cast<int>(Kp),
+                    static_cast<int>(batch), o.hi, o.lo, mode);
+                g_launches.fetch_add(1);
+                MFK_CUDA(cudaGetLastError());
+                return MFK_OK;
+            }
+        }
         const int p_contig = (o.cs == 1) || (o.rs != 1 && std::llabs(o.cs) <= std::llabs(o.rs));
         if (o.rows > 65535LL * 32) return MFK_ERR_UNSUPPORTED;
         for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
@@ -423,8 +523,8 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         }
         return MFK_OK;
     };
-    if (!A.direct && (rc = pack(A, a_off, ao_off)) != MFK_OK) return rc;
-    if (!B.direct && (rc = pack(B, b_off, bo_off)) != MFK_OK) return rc;
+    if (copies(A) && (rc = pack(A, a_off, ao_off)) != MFK_OK) return rc;
+    if (copies(B) && (rc = pack(B, b_off, bo_off)) != MFK_OK) return rc;
 
     auto packed_maps = [&](const Operand& o, int box_rows, CUtensorMap* m0, CUtensorMap* m1) {
         bool ok = make_kmajor_map(m0, o.hi, Kp, o.rows, batch, Kp, o.rows * Kp, box_rows);
@@ -435,8 +535,8 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         }
         return ok;
     };
-    if ((!A.direct && !packed_maps(A, mfk::kBM, &ma0, &ma1)) ||
-        (!B.direct && !packed_maps(B, b_box_rows, &mb0, &mb1))) {
+    if ((copies(A) && !packed_maps(A, mfk::kBM, &ma0, &ma1)) ||
+        (copies(B) && !packed_maps(B, b_box_rows, &mb0, &mb1))) {
         t_cuda_error = "cuTensorMapEncodeTiled rejected a packed operand";
         return MFK_ERR_UNSUPPORTED;
     }
@@ -456,16 +556,22 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
                       d->ldc < (int64_t(1) << 37) && g.c_bs >= 0 && g.c_bs < (int64_t(1) << 37);
     g.tma_store = (c_ok && make_store_map(&mc, d->c, d->n, d->m, batch, d->ldc, g.c_bs)) ? 1 : 0;
 
+    // 3xTF32 with A read in place: the kernel splits A in shared memory.
+    const bool asplit = split3 && A.direct;
+    g.raw_hi = raw_hi ? 1 : 0;
     if (cg == 2 && BN == 256) {
-        return split3 ? launch_tc<2, 256, true>(ma0, ma1, mb0, mb1, mc, g, info, 0, stream)
-                      : launch_tc<2, 256, false>(ma0, ma1, mb0, mb1, mc, g, info, 1, stream);
+        if (asplit) return launch_tc<2, 256, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 6, stream);
+        return split3 ? launch_tc<2, 256, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 0, stream)
+                      : launch_tc<2, 256, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 1, stream);
     }
     if (cg == 2) {
-        return split3 ? launch_tc<2, 128, true>(ma0, ma1, mb0, mb1, mc, g, info, 2, stream)
-                      : launch_tc<2, 128, false>(ma0, ma1, mb0, mb1, mc, g, info, 3, stream);
+        if (asplit) return launch_tc<2, 128, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 7, stream);
+        return split3 ? launch_tc<2, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 2, stream)
+                      : launch_tc<2, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 3, stream);
     }
-    return split3 ? launch_tc<1, 128, true>(ma0, ma1, mb0, mb1, mc, g, info, 4, stream)
-                  : launch_tc<1, 128, false>(ma0, ma1, mb0, mb1, mc, g, info, 5, stream);
+    if (asplit) return launch_tc<1, 128, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 8, stream);
+    return split3 ? launch_tc<1, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 4, stream)
+                  : launch_tc<1, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 5, stream);
 }
 
 }  // namespace
@@ -473,7 +579,7 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
 extern "C" {
 
 int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream) {
-    return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream));
+    return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream), nullptr);
 }
 
 int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream) {
@@ -498,7 +604,7 @@ int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream) {
 int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc* batch,
                                  void* stream) {
     if (batch == nullptr) return MFK_ERR_INVALID_ARGUMENT;
-    return run_gemm(desc, batch, static_cast<cudaStream_t>(stream));
+    return run_gemm(desc, batch, static_cast<cudaStream_t>(stream), nullptr);
 }
 
 int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_t transpose,

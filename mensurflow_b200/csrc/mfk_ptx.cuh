@@ -332,6 +332,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
                  : "memory");
 }
 
+// Round to the nearest tf32 (ties away from zero), with the documented PTX conversion.
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

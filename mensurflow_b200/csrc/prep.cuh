@@ -12,13 +12,6 @@
 
 namespace mfk {
 
-// Round to the nearest tf32 (ties away from zero), with the documented PTX conversion.
-__device__ __forceinline__ float tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
-
 enum PackMode : int {
     kPackCopy = 0,   // hi = x
     kPackRound = 1,  // hi = tf32(x)
@@ -70,6 +63,45 @@ __global__ void __launch_bounds__(256) pack_kmajor_kernel(
                 const float h = tf32_rna(v);
                 hi[o] = h;
                 if (mode == kPackSplit) lo[o] = tf32_rna(v - h);
+            }
+        }
+    }
+}
+
+// The same pass for an operand that is already K-major with 16-byte aligned rows and K % 4 == 0
+// (the common case: A row-major, or B read transposed): no transpose needed, so each thread
+// moves one float4 straight through, coalesced on both sides. Grid-stride over
+// rows x Kp/4 float4s of `batch` matrices.
+__global__ void __launch_bounds__(256) pack_kmajor_vec4_kernel(
+    const float* __restrict__ x, const long long* __restrict__ offsets, long long bstride,
+    long long rs, int R, int K, int Kp, int batch, float* __restrict__ hi,
+    float* __restrict__ lo, int mode) {
+    const long long per_row = Kp / 4;
+    const long long per_mat = static_cast<long long>(R) * per_row;
+    const long long total = per_mat * batch;
+    const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += step) {
+        const long long b = i / per_mat;
+        const long long rem = i - b * per_mat;
+        const long long r = rem / per_row;
+        const int p = static_cast<int>(rem - r * per_row) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p < K) {
+            const long long base = offsets ? offsets[b] : b * bstride;
+            v = __ldcs(reinterpret_cast<const float4*>(x + base + r * rs + p));
+        }
+        float4* h4 = reinterpret_cast<float4*>(hi) + i;
+        if (mode == kPackCopy) {
+            *h4 = v;
+        } else {
+            const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z),
+                                         tf32_rna(v.w));
+            *h4 = h;
+            if (mode == kPackSplit) {
+                reinterpret_cast<float4*>(lo)[i] =
+                    make_float4(tf32_rna(v.x - h.x), tf32_rna(v.y - h.y), tf32_rna(v.z - h.z),
+                                tf32_rna(v.w - h.w));
             }
         }
     }

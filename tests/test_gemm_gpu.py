@@ -361,3 +361,20 @@ def test_epilogue_activation_accuracy(cuda, act, approx):
     ref_gelu = golden("seeded_cases.npz")["act_gelu_tanh" if approx else "act_gelu"]
     assert ulp_diff(got[:4096, 0], ref_gelu).max() <= 8
     no_fault()
+
+
+def test_tf32_conversion_of_raw_fp32_operands(cuda):
+    """Known answer for how the tensor cores read an fp32 operand as tf32 (1xTF32 reads A in
+    place): a = 1 + 3*2^-12 has 0.75 ulp of tf32 beyond 1, so truncation gives 1 and rounding
+    gives 1 + 2^-10. Either is within the 1xTF32 bound; the test records which one the hardware
+    does (the 3xTF32 paths never depend on it: they round hi and lo explicitly)."""
+    a = torch.zeros(1, 32, device=cuda)
+    a[0, 0] = 1.0 + 3.0 * 2.0 ** -12
+    b = torch.zeros(32, 1, device=cuda)
+    b[0, 0] = 1.0
+    got = float(host(mf.matmul(a, b, precision="1xtf32"))[0, 0])
+    print(f"tf32 conversion of raw fp32: {'truncation' if got == 1.0 else 'rounding'} ({got!r})")
+    assert got in (1.0, 1.0 + 2.0 ** -10)
+    got3 = float(host(mf.matmul(a, b, precision="3xtf32"))[0, 0])
+    assert got3 == 1.0 + 3.0 * 2.0 ** -12  # the split keeps every bit
+    no_fault()

@@ -71,10 +71,11 @@ def test_noalloc_matches_allocating_entry_point(cuda, precision, tol, transpose_
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
     so = _lib.lib()
-    # 3xTF32 packs A and B twice: 8 bytes x (m + n) x k rounded up to 32 > 64 MiB here.
+    # 3xTF32 packs B (hi and lo): 8 bytes x n x k rounded up to 32 > 64 MiB here (A is
+    # K-major and aligned, so the kernel splits it in place and it needs no copy).
     m = n = 4096
-    k = 1056
-    assert 8 * (m + n) * k > _lib.NOALLOC_SCRATCH_BYTES
+    k = 2080
+    assert 8 * n * k > _lib.NOALLOC_SCRATCH_BYTES
     a = torch.zeros(m, k, device=cuda)
     b = torch.zeros(k, n, device=cuda)
     out = torch.zeros(m, n, device=cuda)
