@@ -50,7 +50,7 @@ def parse_args():
     p.add_argument("--size", type=int, default=8192,
                    help="c2 only: M = N = K per rank (profiling captures use a smaller case)")
     p.add_argument("--mnk", type=str, default=None,
-                   help="c2 only: 'M,N,K' per rank instead of --size (profiling other shapes)")
+                   help="c2: 'M,N,K' per rank instead of --size; gemv: 'M,1,K' (profiling shapes)")
     return p.parse_args()
 
 
@@ -153,14 +153,23 @@ def emit(obj):
 
 # ---- the reference arm / CPU baseline ----------------------------------------------------------
 
+def host_threads() -> int:
+    """Every host CPU this process may run on (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_gemm_sample(m_full, n, k, target_s, reps, warmup=1):
-    """Times the reference's own public gemm (+ bias_add) on a row sample of the C2 workload.
-    Returns (seconds per call list, sample rows, kind, cores)."""
+    """Times the reference's own public gemm (+ bias_add) on a row sample of the C2 workload,
+    with all host threads. Returns (seconds per call list, sample rows, kind, cores)."""
     from oracle import oracle as O
 
     ref = O.reference()
     if ref is None:
         return None
+    ref.mfref_set_threads(host_threads())
     cores = int(ref.mfref_max_threads())
     rows = 64
     bench = O.RefGemmBench(rows, n, k, True, 1)
@@ -229,6 +238,7 @@ def main():
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    os.environ["NCCL_DEBUG"] = "WARN"  # keep rank 0's stdout to the one JSON line
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
@@ -358,9 +368,11 @@ def main():
             mf.gemm_strided_batched(P, V, precision=args.precision)
     else:
         m, k = 65536, 8192
+        if args.mnk:
+            m, _, k = (int(v) for v in args.mnk.split(","))
         n = 1
         scaling = "weak"
-        wl = "gemv: y = A x, A [65536, 8192] per rank, x [8192], double accumulation"
+        wl = f"gemv: y = A x, A [{m}, {k}] per rank, x [{k}], double accumulation"
         A = torch.rand(m, k, device=device, generator=gen) * 2 - 1
         x = torch.rand(k, device=device, generator=gen) * 2 - 1
         flops_rank = 2.0 * m * k
