@@ -1,0 +1,33 @@
+"""The reference's own test programs for the path, run on the B200 through the drop-in.
+
+mensurflow_b200/host/Makefile compiles the unmodified reference library with this repository's
+CUDA backend (mensurflow_b200/host/cuda_backend.cpp, which calls the sm_100a kernels through
+include/mfk.h) in place of its cuBLAS backend, and links the reference's matmul_test,
+matvec_test and elementwise_ops_test against it. Those programs check values on every device
+whose dispatcher has the kernel (tests/ops/matmul_test.cpp:97-100, matvec_test.cpp:69-72,
+elementwise_ops_test.cpp has_bias), so on a GPU box they run their CPU checks and then the same
+checks on cuda:0. The build needs the reference sources, so it happens where they are; the
+programs themselves run anywhere."""
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BUILD = os.path.join(ROOT, "mensurflow_b200", "host", "_build")
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["matmul_test", "matvec_test", "elementwise_ops_test"])
+def test_reference_program_passes_on_b200(cuda, name):
+    path = os.path.join(BUILD, name)
+    if not os.path.exists(path):
+        pytest.skip("integration build absent (it is made where the reference sources are)")
+    r = subprocess.run([path], capture_output=True, text=True, timeout=900)
+    out = r.stdout + r.stderr
+    assert r.returncode == 0, out[-4000:]
+    assert "passed" in out
+    if name == "matmul_test":
+        # the program lists each device it checks; the CUDA one must be among them
+        assert "matmul on cuda:0" in out, out[-2000:]
