@@ -87,12 +87,80 @@ def _gemm_desc(a_op, b_op, out, alpha, c_in, beta, bias, act, precision) -> Gemm
     return d
 
 
+def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activation, precision,
+                    out, chunks):
+    """Execution::GPU on host-resident tensors, as the reference's run_on does for data that lives
+    elsewhere (src/core/dispatcher.cpp:308-323: copy the inputs to the device, run, copy the
+    result back) — pipelined: op(B) and the bias go first, then row blocks of op(A) and C stream
+    in on one stream, are multiplied on the caller's stream and stream back on a third, so the
+    transfers overlap each other and the math. Returns a host tensor; the copies are complete when
+    this returns (the reference's copy_d2h waits the same way)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    left = a.t() if transpose_a else a
+    right = b.t() if transpose_b else b
+    m, k = left.shape
+    n = right.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, pin_memory=True)
+    compute = torch.cuda.current_stream(dev)
+    copy_in = torch.cuda.Stream(dev)
+    copy_out = torch.cuda.Stream(dev)
+    copy_in.wait_stream(compute)
+    with torch.cuda.stream(copy_in):
+        d_b = b.to(dev, non_blocking=True)
+        d_bias = bias.to(dev, non_blocking=True) if bias is not None else None
+    right_d = d_b.t() if transpose_b else d_b
+    d_out = torch.empty((m, n), dtype=torch.float32, device=dev)
+    # row blocks of op(A) are contiguous host slices only when A is not transposed
+    nchunks = 1 if transpose_a or m < 512 else max(1, min(chunks, m // 256))
+    bounds = [round(i * m / nchunks) // 128 * 128 for i in range(nchunks)] + [m]
+    d_a = torch.empty_like(left, device=dev) if not transpose_a else None
+    d_c = torch.empty((m, n), dtype=torch.float32, device=dev) if c is not None else None
+    for i in range(nchunks):
+        r0, r1 = bounds[i], bounds[i + 1]
+        if r1 <= r0:
+            continue
+        with torch.cuda.stream(copy_in):
+            if transpose_a:
+                a_blk = a.to(dev, non_blocking=True).t()
+            else:
+                d_a[r0:r1].copy_(a[r0:r1], non_blocking=True)
+                a_blk = d_a[r0:r1]
+            c_blk = None
+            if d_c is not None:
+                d_c[r0:r1].copy_(c[r0:r1], non_blocking=True)
+                c_blk = d_c[r0:r1]
+        ready = torch.cuda.Event()
+        ready.record(copy_in)
+        compute.wait_event(ready)
+        gemm(a_blk, right_d, alpha, c_blk, beta, False, False, bias=d_bias,
+             activation=activation, precision=precision, out=d_out[r0:r1])
+        done = torch.cuda.Event()
+        done.record(compute)
+        copy_out.wait_event(done)
+        with torch.cuda.stream(copy_out):
+            out[r0:r1].copy_(d_out[r0:r1], non_blocking=True)
+    # the device buffers stay alive until the copies that read them have finished
+    for t in (d_a, d_c, d_b, d_bias, d_out):
+        if t is not None:
+            t.record_stream(copy_out)
+            t.record_stream(copy_in)
+    copy_out.synchronize()
+    return out
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch.Tensor] = None,
          beta: float = 0.0, transpose_a: bool = False, transpose_b: bool = False, *,
          bias: Optional[torch.Tensor] = None, activation: Optional[str] = None,
-         precision: Optional[str] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+         precision: Optional[str] = None, out: Optional[torch.Tensor] = None,
+         execution: str = "auto", chunks: int = 8) -> torch.Tensor:
     """alpha * op(a) @ op(b) + beta * c, as mensurflow::gemm (blas.hpp:59, blas.cpp:234-262),
-    in ONE kernel; `bias` and `activation` fuse the following bias_add/relu/gelu."""
+    in ONE kernel; `bias` and `activation` fuse the following bias_add/relu/gelu.
+
+    `execution` follows the reference's Execution (include/mensurflow/execution.hpp): with CUDA
+    tensors the op runs on their device; with host tensors "gpu" streams them through the current
+    CUDA device and returns a host tensor, while "auto"/"cpu" have no kernel here
+    (NotImplementedError — the reference's CPU path is not part of this library)."""
     _require(a, "gemm", "a", 2)
     _require(b, "gemm", "b", 2)
     if c is not None:
@@ -113,6 +181,13 @@ def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch
         raise ValueError(f"gemm: bias must be [{n}], got {tuple(bias.shape)}")
     if activation not in _ACTS:
         raise ValueError(f"gemm: unknown activation {activation!r}")
+    if execution not in ("auto", "cpu", "gpu"):
+        raise ValueError(f"gemm: unknown execution {execution!r}")
+    if a.device.type == "cpu" and execution == "gpu" and a.dtype == torch.float32:
+        if out is not None and (tuple(out.shape) != (m, n) or out.device.type != "cpu"):
+            raise ValueError("gemm: out must be a host [m, n] tensor for host inputs")
+        return _gemm_from_host(a, b, alpha, c if beta != 0.0 else None, beta, transpose_a,
+                               transpose_b, bias, activation, precision, out, chunks)
     _kernel_for("gemm", a)
     if bias is not None:
         bias = bias.contiguous()

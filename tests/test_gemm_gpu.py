@@ -378,3 +378,29 @@ def test_tf32_conversion_of_raw_fp32_operands(cuda):
     got3 = float(host(mf.matmul(a, b, precision="3xtf32"))[0, 0])
     assert got3 == 1.0 + 3.0 * 2.0 ** -12  # the split keeps every bit
     no_fault()
+
+
+@pytest.mark.parametrize("trans", [(False, True), (True, False)])
+def test_host_tensors_with_gpu_execution(cuda, trans):
+    """Host inputs with execution="gpu": copied to the device, computed, copied back (the
+    reference's run_on for data that lives elsewhere), pipelined by row blocks — the same values
+    as the device-resident call."""
+    ta, tb = trans
+    m, n, k = 1300, 700, 900
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((k, m) if ta else (m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k) if tb else (k, n)).astype(np.float32)
+    c = rng.standard_normal((m, n)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    ha, hb, hc, hbias = (torch.from_numpy(x).pin_memory() for x in (a, b, c, bias))
+    got = mf.gemm(ha, hb, 0.5, hc, 1.0, ta, tb, bias=hbias, execution="gpu", chunks=4)
+    assert got.device.type == "cpu" and tuple(got.shape) == (m, n)
+    want = host(mf.gemm(dev(a, cuda), dev(b, cuda), 0.5, dev(c, cuda), 1.0, ta, tb,
+                        bias=dev(bias, cuda)))
+    mag = 0.5 * O.abs_product(a, b, ta, tb) + np.abs(c) + np.abs(bias)[None, :]
+    assert_close(got.numpy(), want, mag, TOL_3X, "host path vs device path")
+    assert_close(got.numpy(), O.gemm(a, b, 0.5, c, 1.0, ta, tb, bias=bias), mag, TOL_3X,
+                 "host path vs oracle")
+    with pytest.raises(NotImplementedError):
+        mf.gemm(ha, hb, transpose_a=ta, transpose_b=tb)  # "auto" on host data: no CPU kernel here
+    no_fault()
