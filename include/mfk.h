@@ -155,6 +155,31 @@ int mfk_matvec_f32(const float* a, int64_t m, int64_t k, const float* x, float* 
 int mfk_bias_act_f32(const float* x, const float* bias, float* out, int64_t rows, int64_t cols,
                      int32_t activation, void* stream);
 
+/* softmax (log_softmax when `log` != 0) along the middle axis of a contiguous [outer, length,
+ * inner] tensor: max (NaN poisons the line), exp in fp32, sum in double, multiply by 1/sum; an
+ * all -inf line gives zeros (-inf for log_softmax). Replaces the OpId::Softmax / LogSoftmax kernels
+ * (CPU adapter: src/backends/cpu/backend.cpp:549-552 -> softmax_f32 / log_softmax_f32,
+ * src/backends/cpu/ops/softmax/softmax.cpp:11-80). out may be x. */
+int mfk_softmax_f32(const float* x, float* out, int64_t outer, int64_t length, int64_t inner,
+                    int32_t log, void* stream);
+
+/* The softmax between attention's GEMMs with its masking fused in: for a contiguous
+ * [batch, rows, cols] score tensor, entry (b, i, j) counts as -inf unless (keep == NULL or
+ * keep[b*keep_bs + i*keep_rs + j] != 0) and (causal == 0 or j <= i); then softmax along cols.
+ * Equal to the reference's where(keep, scores, -inf) [+ causal where] followed by softmax(-1)
+ * (src/ops/attention.cpp:82-96) in one pass. keep is a Bool (one byte per entry) mask with unit
+ * column stride; keep_bs / keep_rs may be 0 (broadcast). out may be scores. No counterpart kernel
+ * in the reference (it composes where and softmax). */
+int mfk_masked_softmax_f32(const float* scores, const uint8_t* keep, int64_t keep_bs,
+                           int64_t keep_rs, int32_t causal, float* out, int64_t batch,
+                           int64_t rows, int64_t cols, void* stream);
+
+/* out[i] = cond[i] ? x[i] : y[i] over n contiguous elements (cond: one byte per element, Bool).
+ * Replaces the OpId::Where kernel (CPU adapter src/backends/cpu/backend.cpp:625-630 -> where_f32);
+ * the op expands and packs its inputs first (src/ops/elementwise.cpp:455-481). */
+int mfk_where_f32(const uint8_t* cond, const float* x, const float* y, float* out, int64_t n,
+                  void* stream);
+
 /* Process-wide precision used when a descriptor says MFK_PRECISION_DEFAULT. The reference's
  * public signatures have no precision argument, so its adapters leave the default in place. */
 int mfk_set_default_precision(int32_t precision);

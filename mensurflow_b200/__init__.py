@@ -5,6 +5,7 @@ mirrors the reference's op API over torch CUDA tensors, ``sharded`` splits a GEM
 """
 from ._lib import MfkError, build  # noqa: F401
 from .ops import (  # noqa: F401
+    attention,
     bias_add,
     device_status,
     gelu,
@@ -13,14 +14,17 @@ from .ops import (  # noqa: F401
     gemv,
     get_default_precision,
     linear,
+    log_softmax,
     matmul,
     matvec,
     relu,
     set_default_precision,
+    softmax,
+    where,
 )
 
 __all__ = [
-    "MfkError", "build", "bias_add", "device_status", "gelu", "gemm", "gemm_strided_batched",
+    "MfkError", "build", "attention", "bias_add", "log_softmax", "softmax", "where", "device_status", "gelu", "gemm", "gemm_strided_batched",
     "gemv", "get_default_precision", "linear", "matmul", "matvec", "relu",
     "set_default_precision",
 ]

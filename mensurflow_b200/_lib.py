@@ -34,6 +34,9 @@ EXPORTED = (
     "mfk_gemv_f32",
     "mfk_matvec_f32",
     "mfk_bias_act_f32",
+    "mfk_softmax_f32",
+    "mfk_masked_softmax_f32",
+    "mfk_where_f32",
     "mfk_set_default_precision",
     "mfk_get_default_precision",
     "mfk_device_status",
@@ -106,6 +109,9 @@ def lib() -> ctypes.CDLL:
             so.mfk_gemv_f32.argtypes = [vp, i64, i64, i64, i32, vp, i64, f32, f32, vp, vp, vp]
             so.mfk_matvec_f32.argtypes = [vp, i64, i64, vp, vp, vp]
             so.mfk_bias_act_f32.argtypes = [vp, vp, vp, i64, i64, i32, vp]
+            so.mfk_softmax_f32.argtypes = [vp, vp, i64, i64, i64, i32, vp]
+            so.mfk_masked_softmax_f32.argtypes = [vp, vp, i64, i64, i32, vp, i64, i64, i64, vp]
+            so.mfk_where_f32.argtypes = [vp, vp, vp, vp, i64, vp]
             so.mfk_set_default_precision.argtypes = [i32]
             so.mfk_get_default_precision.restype = i32
             so.mfk_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]

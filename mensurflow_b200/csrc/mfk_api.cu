@@ -696,6 +696,78 @@ int mfk_bias_act_f32(const float* x, const float* bias, float* out, int64_t rows
     return MFK_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+int launch_softmax(const float* x, float* out, int64_t outer, int64_t length, int64_t inner,
+                   int log, const mfk::SoftmaxMask& mk, cudaStream_t stream) {
+    if (outer < 0 || length < 0 || inner < 1) return MFK_ERR_INVALID_ARGUMENT;
+    if (outer == 0 || length == 0) return MFK_OK;
+    if (x == nullptr || out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    g_launches.fetch_add(1);
+    if (inner == 1) {
+        const int64_t blocks = (outer * 32 + 255) / 256;
+        if (blocks > INT32_MAX) return MFK_ERR_UNSUPPORTED;
+        mfk::softmax_lastdim_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            x, out, outer, length, log, mk);
+    } else {
+        const int64_t blocks = (outer * inner + 255) / 256;
+        if (blocks > INT32_MAX) return MFK_ERR_UNSUPPORTED;
+        mfk::softmax_strided_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            x, out, outer, length, inner, log);
+    }
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mfk_softmax_f32(const float* x, float* out, int64_t outer, int64_t length, int64_t inner,
+                    int32_t log, void* stream) {
+    mfk::SoftmaxMask mk{nullptr, 0, 0, 0, 1};
+    return launch_softmax(x, out, outer, length, inner, log != 0, mk,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int mfk_masked_softmax_f32(const float* scores, const uint8_t* keep, int64_t keep_bs,
+                           int64_t keep_rs, int32_t causal, float* out, int64_t batch,
+                           int64_t rows, int64_t cols, void* stream) {
+    if (batch < 0 || rows < 0 || cols < 0 || keep_bs < 0 || keep_rs < 0)
+        return MFK_ERR_INVALID_ARGUMENT;
+    mfk::SoftmaxMask mk{keep, keep_bs, keep_rs, causal != 0 ? 1 : 0, rows > 0 ? rows : 1};
+    return launch_softmax(scores, out, batch * rows, cols, 1, 0, mk,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int mfk_where_f32(const uint8_t* cond, const float* x, const float* y, float* out, int64_t n,
+                  void* stream) {
+    if (n < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (n == 0) return MFK_OK;
+    if (cond == nullptr || x == nullptr || y == nullptr || out == nullptr)
+        return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, int64_t(info->sm_count) * 8);
+    g_launches.fetch_add(1);
+    mfk::where_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        cond, x, y, out, n);
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
 int mfk_set_default_precision(int32_t precision) {
     if (precision != MFK_PRECISION_3XTF32 && precision != MFK_PRECISION_1XTF32)
         return MFK_ERR_INVALID_ARGUMENT;

@@ -175,3 +175,125 @@ __global__ void __launch_bounds__(256) epilogue_only_kernel(GemmArgs g) {
 }
 
 }  // namespace mfk
+
+namespace mfk {
+
+// ---- softmax / log_softmax / where (the ops between attention's two GEMMs) -------------------
+// Softmax along one axis of a contiguous [outer, length, inner] tensor, as the reference's
+// softmax_f32 / log_softmax_f32 (src/backends/cpu/ops/softmax/softmax.cpp:11-80): the line's max
+// (a NaN anywhere makes the whole line NaN), e = exp(x - max) in fp32, the sum of e in double,
+// out = e * float(1 / sum) — or, for log_softmax, (x - max) - float(log(sum)). A line that is
+// entirely -inf gives zeros (softmax) or -inf (log_softmax). `keep`/`causal` (attention) mask
+// entries to -inf first, as the reference's where(keep, scores, -inf) does before its softmax
+// (src/ops/attention.cpp:82-96): entry (b, i, j) of a [batch, rows, cols] last-axis softmax is
+// kept when keep[b*keep_bs + i*keep_rs + j] != 0 and, with causal, j <= i.
+
+__device__ __forceinline__ float nan_max(float a, float b) {
+    return (isnan(a) || a > b) ? a : b;
+}
+
+__device__ __forceinline__ float warp_nan_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = nan_max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+struct SoftmaxMask {
+    const unsigned char* keep;  // optional
+    long long keep_bs, keep_rs;
+    int causal;
+    long long rows;             // lines per matrix (for the causal index and keep addressing)
+};
+
+__device__ __forceinline__ float masked_value(float v, const SoftmaxMask& mk, long long line,
+                                              long long j) {
+    if (mk.causal || mk.keep) {
+        const long long i = line % mk.rows;
+        if (mk.causal && j > i) return -INFINITY;
+        if (mk.keep) {
+            const long long b = line / mk.rows;
+            if (!mk.keep[b * mk.keep_bs + i * mk.keep_rs + j]) return -INFINITY;
+        }
+    }
+    return v;
+}
+
+// Last-axis lines (inner == 1): one warp per line; values re-read from L1/L2 between passes.
+__global__ void __launch_bounds__(256) softmax_lastdim_kernel(const float* __restrict__ x,
+                                                              float* __restrict__ out,
+                                                              long long lines, long long length,
+                                                              int log_softmax, SoftmaxMask mk) {
+    const int lane = threadIdx.x % 32;
+    const long long line = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    if (line >= lines) return;
+    const float* in = x + line * length;
+    float* dst = out + line * length;
+    float m = -INFINITY;
+    for (long long j = lane; j < length; j += 32) m = nan_max(m, masked_value(in[j], mk, line, j));
+    m = warp_nan_max(m);
+    if (m == -INFINITY) {
+        for (long long j = lane; j < length; j += 32) dst[j] = log_softmax ? -INFINITY : 0.0f;
+        return;
+    }
+    double sum = 0.0;
+    for (long long j = lane; j < length; j += 32) {
+        const float e = expf(masked_value(in[j], mk, line, j) - m);
+        if (!log_softmax) dst[j] = e;
+        sum += static_cast<double>(e);
+    }
+    sum = warp_sum(sum);
+    if (log_softmax) {
+        const float log_sum = static_cast<float>(log(sum));
+        for (long long j = lane; j < length; j += 32)
+            dst[j] = (masked_value(in[j], mk, line, j) - m) - log_sum;
+    } else {
+        const float scale = static_cast<float>(1.0 / sum);
+        __syncwarp();
+        for (long long j = lane; j < length; j += 32) dst[j] *= scale;
+    }
+}
+
+// Lines along a non-last axis (inner > 1): one thread per line, neighbouring threads on
+// neighbouring `inner` positions so every pass reads coalesced.
+__global__ void __launch_bounds__(256) softmax_strided_kernel(const float* __restrict__ x,
+                                                              float* __restrict__ out,
+                                                              long long outer, long long length,
+                                                              long long inner, int log_softmax) {
+    const long long line = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (line >= outer * inner) return;
+    const long long base = (line / inner) * length * inner + line % inner;
+    const float* in = x + base;
+    float* dst = out + base;
+    float m = -INFINITY;
+    for (long long j = 0; j < length; ++j) m = nan_max(m, in[j * inner]);
+    if (m == -INFINITY) {
+        for (long long j = 0; j < length; ++j) dst[j * inner] = log_softmax ? -INFINITY : 0.0f;
+        return;
+    }
+    double sum = 0.0;
+    for (long long j = 0; j < length; ++j) {
+        const float e = expf(in[j * inner] - m);
+        if (!log_softmax) dst[j * inner] = e;
+        sum += static_cast<double>(e);
+    }
+    if (log_softmax) {
+        const float log_sum = static_cast<float>(log(sum));
+        for (long long j = 0; j < length; ++j) dst[j * inner] = (in[j * inner] - m) - log_sum;
+    } else {
+        const float scale = static_cast<float>(1.0 / sum);
+        for (long long j = 0; j < length; ++j) dst[j * inner] *= scale;
+    }
+}
+
+// out[i] = cond[i] ? x[i] : y[i] over contiguous, already broadcast inputs (where_f32).
+__global__ void __launch_bounds__(256) where_kernel(const unsigned char* __restrict__ cond,
+                                                    const float* __restrict__ x,
+                                                    const float* __restrict__ y,
+                                                    float* __restrict__ out, long long n) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += stride)
+        out[i] = cond[i] ? x[i] : y[i];
+}
+
+}  // namespace mfk

@@ -287,6 +287,42 @@ void matvec_kernel(const OpArgs& args, Stream& stream) {
               "matvec");
 }
 
+// OpId::Softmax / LogSoftmax: a contiguous input, the axis in OpArgs (src/ops/softmax.cpp:33-43),
+// lines around that axis as the CPU adapter's lines_around (src/backends/cpu/backend.cpp:549).
+template <int Log>
+void softmax_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& x = args.inputs[0];
+    std::int64_t outer = 1, length = 1, inner = 1;
+    if (x.dim() > 0) {
+        for (int d = 0; d < x.dim(); ++d) {
+            if (d < args.axis) {
+                outer *= x.size(d);
+            } else if (d == args.axis) {
+                length = x.size(d);
+            } else {
+                inner *= x.size(d);
+            }
+        }
+    }
+    check_mfk(mfk_softmax_f32(TensorAccess::data<float>(x),
+                              TensorAccess::data<float>(args.outputs[0]), outer, length, inner,
+                              Log, s.raw()),
+              Log ? "log_softmax" : "softmax");
+}
+
+// OpId::Where: values {x, y} then the Bool condition, all expanded and packed by the op
+// (src/ops/elementwise.cpp:455-481), as the CPU adapter reads them (backend.cpp:625-630).
+void where_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& out = args.outputs[0];
+    check_mfk(mfk_where_f32(TensorAccess::data<std::uint8_t>(args.inputs[2]),
+                            TensorAccess::data<float>(args.inputs[0]),
+                            TensorAccess::data<float>(args.inputs[1]),
+                            TensorAccess::data<float>(out), out.numel(), s.raw()),
+              "where");
+}
+
 class CudaBackend final : public Backend {
   public:
     CudaBackend() {
@@ -321,6 +357,9 @@ class CudaBackend final : public Backend {
         dispatcher.register_kernel(key(OpId::Gelu), activation_kernel<MFK_ACT_GELU>);
         dispatcher.register_kernel(key(OpId::Gemv), gemv_kernel);
         dispatcher.register_kernel(key(OpId::Matvec), matvec_kernel);
+        dispatcher.register_kernel(key(OpId::Softmax), softmax_kernel<0>);
+        dispatcher.register_kernel(key(OpId::LogSoftmax), softmax_kernel<1>);
+        dispatcher.register_kernel(key(OpId::Where), where_kernel);
 #ifdef MENSURFLOW_HAS_OPID_GEMM
         dispatcher.register_kernel(key(OpId::Gemm), gemm_kernel);
 #else

@@ -379,6 +379,123 @@ def gelu(x: torch.Tensor, approximate: bool = False) -> torch.Tensor:
     return _bias_act(x, None, _lib.ACT_GELU_TANH if approximate else _lib.ACT_GELU, "gelu")
 
 
+def _softmax(x: torch.Tensor, axis: int, log: bool, op: str) -> torch.Tensor:
+    _require(x, op, "input")
+    if x.dtype != torch.float32:
+        raise ValueError(f"{op}: input must be F32, got {x.dtype}")
+    rank = x.dim()
+    extent = rank if rank else 1
+    ax = axis + extent if axis < 0 else axis
+    if not 0 <= ax < extent:
+        raise ValueError(f"{op}: axis {axis} is out of range for a {rank}-d tensor")
+    _kernel_for(op, x)
+    x = x.contiguous()
+    shape = tuple(x.shape) if rank else (1,)
+    outer = int(np.prod(shape[:ax])) if ax else 1
+    inner = int(np.prod(shape[ax + 1:])) if ax + 1 < len(shape) else 1
+    out = torch.empty_like(x)
+    check(_lib.lib().mfk_softmax_f32(x.data_ptr(), out.data_ptr(), outer, shape[ax], inner,
+                                     1 if log else 0, _stream()), op)
+    return out
+
+
+def softmax(x: torch.Tensor, axis: int = -1) -> torch.Tensor:
+    """exp(x - max) / sum(exp(x - max)) along `axis`, as mensurflow::softmax (softmax.hpp:20):
+    sums in double, an all -inf line gives zeros, a NaN poisons its line."""
+    return _softmax(x, axis, False, "softmax")
+
+
+def log_softmax(x: torch.Tensor, axis: int = -1) -> torch.Tensor:
+    """x - logsumexp(x) along `axis`, as mensurflow::log_softmax (softmax.hpp:24)."""
+    return _softmax(x, axis, True, "log_softmax")
+
+
+def where(condition: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """condition ? x : y with NumPy broadcasting, as mensurflow::where (elementwise.hpp:141)."""
+    if x is None or y is None or not isinstance(x, torch.Tensor) or not isinstance(y, torch.Tensor):
+        raise ValueError("where: undefined value tensor")
+    if condition is None or not isinstance(condition, torch.Tensor):
+        raise ValueError("where: undefined condition tensor")
+    if condition.dtype != torch.bool:
+        raise ValueError("where: condition must have Bool dtype")
+    if x.dtype != y.dtype:
+        raise ValueError("where: dtypes differ")
+    if condition.device != x.device or x.device != y.device:
+        raise ValueError("where: condition and values must be on the same device")
+    try:
+        shape = tuple(torch.broadcast_shapes(tuple(x.shape), tuple(y.shape), tuple(condition.shape)))
+    except RuntimeError as e:
+        raise ValueError(f"where: {e}")
+    _kernel_for("where", x)
+    xx = x.expand(shape).contiguous()
+    yy = y.expand(shape).contiguous()
+    cc = condition.expand(shape).contiguous()
+    out = torch.empty(shape, dtype=torch.float32, device=x.device)
+    check(_lib.lib().mfk_where_f32(cc.data_ptr(), xx.data_ptr(), yy.data_ptr(), out.data_ptr(),
+                                   out.numel(), _stream()), "where")
+    return out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+              mask: Optional[torch.Tensor] = None, causal: bool = False, scale: float = 0.0, *,
+              precision: Optional[str] = None) -> torch.Tensor:
+    """Scaled dot-product attention as mensurflow::attention (attention.hpp:21,
+    src/ops/attention.cpp:48-98): scores = scale * q @ k^T (batched GEMM, scale in alpha), entries
+    outside `mask` (Bool, broadcast to the scores) and, with `causal`, above the diagonal set to
+    -inf, softmax over the keys, then weights @ v. The masking is fused into the softmax pass
+    (one read and one write of the scores instead of the reference's where + softmax passes)."""
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        if t is None or not isinstance(t, torch.Tensor):
+            raise ValueError(f"attention: undefined {name}")
+        if t.dtype != torch.float32:
+            raise ValueError(f"attention: {name} must be F32, got {t.dtype}")
+        if t.dim() < 2:
+            raise ValueError(f"attention: {name} needs at least 2 dimensions, got "
+                             f"{tuple(t.shape)}")
+        if t.device != q.device:
+            raise ValueError("attention: q, k and v must be on the same device")
+    depth, queries, keys = q.shape[-1], q.shape[-2], k.shape[-2]
+    if k.shape[-1] != depth:
+        raise ValueError(f"attention: q {tuple(q.shape)} and k {tuple(k.shape)} differ in the last "
+                         "dimension")
+    if v.shape[-2] != keys:
+        raise ValueError(f"attention: k {tuple(k.shape)} and v {tuple(v.shape)} differ in the "
+                         "number of keys")
+    if scale == 0.0:
+        scale = float(np.float32(1.0 / np.sqrt(depth))) if depth > 0 else 1.0
+    scores = gemm_strided_batched(q, k, scale, None, 0.0, False, True, precision=precision)
+    keep = None
+    if mask is not None:
+        if not isinstance(mask, torch.Tensor) or mask.dtype != torch.bool:
+            raise ValueError("attention: mask must be a defined Bool tensor")
+        if mask.device != q.device:
+            raise ValueError("attention: mask must be on the inputs' device")
+        try:
+            ok = tuple(torch.broadcast_shapes(tuple(mask.shape), tuple(scores.shape))) == \
+                tuple(scores.shape)
+        except RuntimeError:
+            ok = False
+        if not ok:
+            raise ValueError(f"attention: mask {tuple(mask.shape)} does not broadcast to the "
+                             f"scores {tuple(scores.shape)}")
+        keep = mask.expand(scores.shape)
+    if scores.numel() == 0:
+        return gemm_strided_batched(scores, v, precision=precision)
+    batch = scores.numel() // (queries * keys)
+    keep_ptr, keep_bs, keep_rs = None, 0, 0
+    if keep is not None:
+        flat = keep.reshape(batch, queries, keys) if keep.dim() > 2 else keep.reshape(1, queries, keys)
+        if flat.stride(-1) != 1:
+            flat = flat.contiguous()
+        bs = flat.stride(0) if flat.shape[0] > 1 else 0
+        keep_ptr, keep_bs, keep_rs = flat.data_ptr(), bs, flat.stride(1)
+        keep = flat  # keep alive
+    check(_lib.lib().mfk_masked_softmax_f32(scores.data_ptr(), keep_ptr, keep_bs, keep_rs,
+                                            1 if causal else 0, scores.data_ptr(), batch, queries,
+                                            keys, _stream()), "attention")
+    return gemm_strided_batched(scores, v, precision=precision)
+
+
 def device_status() -> int:
     """Kernel error bits of the current device (0 = none); clears them."""
     return _lib.device_status(True)

@@ -212,3 +212,48 @@ void mfo_gemv(const float* a, int64_t rows, int64_t cols, int64_t lda, const flo
         y[i] = (float)(alpha * sum + (beta == 0.0f ? 0.0 : beta * y0[i]));
     }
 }
+
+/* softmax_f32 / log_softmax_f32, src/backends/cpu/ops/softmax/softmax.cpp:11-80: along the middle
+ * axis of a contiguous [outer, length, inner] tensor. max with NaN poisoning; an all -inf line ->
+ * zeros (log: -inf); e = expf(x - max) in float, sum in double, out = e * float(1/sum); log:
+ * (x - max) - float(log(sum)). */
+void mfo_softmax(const float* x, float* out, int64_t outer, int64_t length, int64_t inner,
+                 int log_softmax) {
+#pragma omp parallel for schedule(static)
+    for (int64_t line = 0; line < outer * inner; ++line) {
+        const int64_t base = (line / inner) * length * inner + line % inner;
+        const float* in = x + base;
+        float* dst = out + base;
+        float maximum = -INFINITY;
+        for (int64_t j = 0; j < length; ++j) {
+            const float value = in[j * inner];
+            if (isnan(value) || value > maximum) {
+                maximum = value;
+                if (isnan(value)) break;
+            }
+        }
+        if (maximum == -INFINITY) {
+            for (int64_t j = 0; j < length; ++j) dst[j * inner] = log_softmax ? -INFINITY : 0.0f;
+            continue;
+        }
+        double sum = 0.0;
+        for (int64_t j = 0; j < length; ++j) {
+            const float e = expf(in[j * inner] - maximum);
+            if (!log_softmax) dst[j * inner] = e;
+            sum += (double)e;
+        }
+        if (log_softmax) {
+            const float log_sum = (float)log(sum);
+            for (int64_t j = 0; j < length; ++j) dst[j * inner] = (in[j * inner] - maximum) - log_sum;
+        } else {
+            const float scale = (float)(1.0 / sum);
+            for (int64_t j = 0; j < length; ++j) dst[j * inner] *= scale;
+        }
+    }
+}
+
+/* where_f32 (src/backends/cpu/backend.cpp:625-630): out = cond ? x : y over broadcast, packed
+ * inputs. */
+void mfo_where(const uint8_t* cond, const float* x, const float* y, float* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = cond[i] ? x[i] : y[i];
+}

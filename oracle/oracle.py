@@ -69,6 +69,8 @@ def lib():
             so.mfo_relu.argtypes = [_ptr, _ptr, _i64]
             so.mfo_gelu.argtypes = [_ptr, _ptr, _i64, ctypes.c_int]
             so.mfo_gemv.argtypes = [_ptr, _i64, _i64, _i64, _ptr, _f32, _f32, _ptr, _ptr, ctypes.c_int]
+            so.mfo_softmax.argtypes = [_ptr, _ptr, _i64, _i64, _i64, ctypes.c_int]
+            so.mfo_where.argtypes = [_ptr, _ptr, _ptr, _ptr, _i64]
             _oracle = so
     return _oracle
 
@@ -105,6 +107,11 @@ def reference():
                 so.mfref_openmp.restype = ctypes.c_int
                 so.mfref_time_gemv.argtypes = [_i64, _i64, _u64, ctypes.c_int, ctypes.c_int, _ptr]
                 so.mfref_set_threads.argtypes = [ctypes.c_int]
+                so.mfref_softmax.argtypes = [_ptr, _ptr, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             _ptr]
+                so.mfref_attention.argtypes = [_ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int,
+                                               _ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int,
+                                               ctypes.c_int, _f32, _ptr, _ptr, _ptr]
                 _ref = so
     return _ref
 
@@ -208,6 +215,54 @@ def activation(x, act):
     else:
         raise ValueError(f"unknown activation {act!r}")
     return out
+
+
+def softmax(x, axis=-1, log=False):
+    """The restated softmax / log_softmax along `axis`."""
+    x = np.ascontiguousarray(x, np.float32)
+    axis = axis % x.ndim if x.ndim else 0
+    shape = x.shape if x.ndim else (1,)
+    outer = int(np.prod(shape[:axis]))
+    length = shape[axis]
+    inner = int(np.prod(shape[axis + 1:]))
+    out = np.empty_like(x)
+    lib().mfo_softmax(_p(x), _p(out), outer, length, inner, 1 if log else 0)
+    return out
+
+
+def where(cond, x, y):
+    shape = np.broadcast_shapes(np.shape(cond), np.shape(x), np.shape(y))
+    c = np.ascontiguousarray(np.broadcast_to(cond, shape), np.uint8)
+    xx = np.ascontiguousarray(np.broadcast_to(x, shape), np.float32)
+    yy = np.ascontiguousarray(np.broadcast_to(y, shape), np.float32)
+    out = np.empty(shape, np.float32)
+    lib().mfo_where(_p(c), _p(xx), _p(yy), _p(out), out.size)
+    return out
+
+
+def attention(q, k, v, mask=None, causal=False, scale=0.0):
+    """The reference's attention composition (src/ops/attention.cpp:48-98) with the restated
+    pieces: batched q k^T * scale, where(mask, s, -inf), causal where, softmax, batched w v."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    d = q.shape[-1]
+    if scale == 0.0:
+        scale = float(np.float32(1.0 / np.sqrt(d))) if d > 0 else 1.0
+    bshape = np.broadcast_shapes(q.shape[:-2], k.shape[:-2], v.shape[:-2])
+    lq, lk = q.shape[-2], k.shape[-2]
+    qq = np.broadcast_to(q, bshape + q.shape[-2:]).reshape(-1, lq, d)
+    kk = np.broadcast_to(k, bshape + k.shape[-2:]).reshape(-1, lk, d)
+    vv = np.broadcast_to(v, bshape + v.shape[-2:]).reshape(-1, lk, v.shape[-1])
+    s = np.stack([gemm(qq[i], kk[i], scale, None, 0.0, False, True) for i in range(qq.shape[0])])
+    s = s.reshape(bshape + (lq, lk))
+    if mask is not None:
+        s = where(mask, s, np.float32(-np.inf))
+    if causal:
+        s = where(np.tril(np.ones((lq, lk), bool)), s, np.float32(-np.inf))
+    w = softmax(s, -1).reshape(-1, lq, lk)
+    out = np.stack([gemm(w[i], vv[i]) for i in range(w.shape[0])])
+    return out.reshape(bshape + (lq, v.shape[-1]))
 
 
 def gemv(a, x, alpha=1.0, y=None, beta=0.0, transpose_a=False):
@@ -329,3 +384,30 @@ def ref_time_gemv(rows, cols, seed, warmup, reps):
     secs = np.zeros(reps, np.float64)
     _check_ref(reference().mfref_time_gemv(rows, cols, seed, warmup, reps, _p(secs)))
     return secs
+
+
+def ref_softmax(x, axis=-1, log=False):
+    x = np.ascontiguousarray(x, np.float32)
+    shape = np.array(x.shape, np.int64)
+    out = np.empty_like(x)
+    _check_ref(reference().mfref_softmax(_p(x), _p(shape), x.ndim, axis, int(log), _p(out)))
+    return out
+
+
+def ref_attention(q, k, v, mask=None, causal=False, scale=0.0):
+    arrs = [np.ascontiguousarray(t, np.float32) for t in (q, k, v)]
+    shapes = [np.array(t.shape, np.int64) for t in arrs]
+    m = None if mask is None else np.ascontiguousarray(mask, np.uint8)
+    ms = None if m is None else np.array(m.shape, np.int64)
+    oshape = np.zeros(8, np.int64)
+    ond = ctypes.c_int(0)
+    args = []
+    for t, sh in zip(arrs, shapes):
+        args += [_p(t), _p(sh), t.ndim]
+    lib_ = reference()
+    _check_ref(lib_.mfref_attention(*args, _p(m), _p(ms), 0 if m is None else m.ndim, int(causal),
+                                    scale, None, _p(oshape), ctypes.byref(ond)))
+    out = np.empty(tuple(int(x) for x in oshape[: ond.value]), np.float32)
+    _check_ref(lib_.mfref_attention(*args, _p(m), _p(ms), 0 if m is None else m.ndim, int(causal),
+                                    scale, _p(out), _p(oshape), ctypes.byref(ond)))
+    return out

@@ -170,6 +170,42 @@ int mfref_matvec(const float* a, std::int64_t m, std::int64_t k, const float* x,
         [&] { copy_out(matvec(host_tensor(a, {m, k}), host_tensor(x, {k}), Execution::CPU), out); });
 }
 
+// softmax / log_softmax along `axis` of a host tensor of the given shape.
+int mfref_softmax(const float* x, const std::int64_t* shape, int nd, int axis, int log_softmax_,
+                  float* out) {
+    return guarded([&] {
+        const Tensor t = host_tensor(x, make_shape(shape, nd));
+        copy_out(log_softmax_ ? log_softmax(t, axis, Execution::CPU) : softmax(t, axis, Execution::CPU),
+                 out);
+    });
+}
+
+// The reference's attention (src/ops/attention.cpp:48-98) on host tensors; mask (optional) is a
+// Bool tensor given as bytes. out_shape/out_nd receive the result's shape.
+int mfref_attention(const float* q, const std::int64_t* qs, int qnd, const float* k,
+                    const std::int64_t* ks, int knd, const float* v, const std::int64_t* vs,
+                    int vnd, const std::uint8_t* mask, const std::int64_t* ms, int mnd, int causal,
+                    float scale, float* out, std::int64_t* out_shape, int* out_nd) {
+    return guarded([&] {
+        const Tensor tq = host_tensor(q, make_shape(qs, qnd));
+        const Tensor tk = host_tensor(k, make_shape(ks, knd));
+        const Tensor tv = host_tensor(v, make_shape(vs, vnd));
+        Tensor tm;
+        if (mask != nullptr) {
+            tm = Tensor::from_host(mask, make_shape(ms, mnd), DType::Bool, Device{});
+        }
+        const Tensor r = attention(tq, tk, tv, mask ? &tm : nullptr, causal != 0, scale,
+                                   Execution::CPU);
+        *out_nd = r.dim();
+        for (int d = 0; d < r.dim(); ++d) {
+            out_shape[d] = r.size(d);
+        }
+        if (out != nullptr) {
+            copy_out(r, out);
+        }
+    });
+}
+
 // Timing harness for the CPU baselines: inputs are made once by the reference's own normal() /
 // uniform() factories (outside any timed region), then each run times `reps` calls of the
 // reference's public gemm (+ bias_add) exactly as a user would make them.

@@ -133,6 +133,36 @@ def main():
                philox_normal_s1=O.ref_normal(1029, 0, 1, 1, 3),
                philox_normal_s3=O.ref_normal(515, 0, float(np.float32(1 / np.sqrt(128))), 3, 77))
     np.savez_compressed(os.path.join(HERE, "seeded_cases.npz"), **cfg)
+
+    # softmax / log_softmax (src/ops/softmax.cpp) and attention (src/ops/attention.cpp) through the
+    # reference, on Philox inputs regenerated by the tests (attention_inputs in tests/helpers.py):
+    # the four cases of tests/ops/softmax_loss_test.cpp test_attention (plain, mask, causal, both
+    # with scale 0.5; query 2 sees no key) and k/v broadcast over heads.
+    att = {}
+    x = O.ref_normal(3 * 5 * 17, 0, 30, 9, 0).reshape(3, 5, 17)
+    x[0, 1, :] = -np.inf
+    x[1, 2, 3] = np.nan
+    x[2, 0, :] += 1000
+    for axis in (-1, 1, 0):
+        for log in (False, True):
+            att[f"softmax_a{axis}_l{int(log)}"] = O.ref_softmax(x, axis, log)
+    b, h, lq, lk, d, dv = 2, 3, 5, 7, 8, 4
+    q = O.ref_normal(b * h * lq * d, 0, 1, 21, 0).reshape(b, h, lq, d)
+    k = O.ref_normal(b * h * lk * d, 0, 1, 22, 0).reshape(b, h, lk, d)
+    v = O.ref_normal(b * h * lk * dv, 0, 1, 23, 0).reshape(b, h, lk, dv)
+    keep = np.array([[i != 2 and (i + j) % 3 != 0 for j in range(lk)] for i in range(lq)])
+    for name, mask, causal, scale in (("plain", None, False, 0.0), ("mask", keep, False, 0.0),
+                                      ("causal", None, True, 0.0), ("both", keep, True, 0.5)):
+        att[f"attention_{name}"] = O.ref_attention(q, k, v, mask, causal, scale)
+    k1 = O.ref_normal(b * lk * d, 0, 1, 24, 0).reshape(b, 1, lk, d)
+    v1 = O.ref_normal(b * lk * dv, 0, 1, 25, 0).reshape(b, 1, lk, dv)
+    att["attention_broadcast_kv"] = O.ref_attention(q, k1, v1)
+    lq2 = 64
+    q2 = O.ref_normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 26, 0).reshape(4, lq2, 32)
+    k2 = O.ref_normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 27, 0).reshape(4, lq2, 32)
+    v2 = O.ref_normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 28, 0).reshape(4, lq2, 32)
+    att["attention_causal_64"] = O.ref_attention(q2, k2, v2, None, True)
+    np.savez_compressed(os.path.join(HERE, "attention_cases.npz"), **att)
     print("wrote", sorted(os.listdir(HERE)))
 
 

@@ -83,3 +83,25 @@ def ulp_diff(a, b):
     ai = np.where(ai < 0, np.int64(-(2 ** 31)) - ai, ai)
     bi = np.where(bi < 0, np.int64(-(2 ** 31)) - bi, bi)
     return np.abs(ai - bi)
+
+
+def attention_inputs():
+    """Inputs of tests/golden/attention_cases.npz, regenerated with the oracle's Philox."""
+    d = {}
+    x = O.normal(3 * 5 * 17, 0, 30, 9, 0).reshape(3, 5, 17)
+    x[0, 1, :] = -np.inf
+    x[1, 2, 3] = np.nan
+    x[2, 0, :] += 1000
+    d["softmax_x"] = x
+    b, h, lq, lk, dd, dv = 2, 3, 5, 7, 8, 4
+    d["q"] = O.normal(b * h * lq * dd, 0, 1, 21, 0).reshape(b, h, lq, dd)
+    d["k"] = O.normal(b * h * lk * dd, 0, 1, 22, 0).reshape(b, h, lk, dd)
+    d["v"] = O.normal(b * h * lk * dv, 0, 1, 23, 0).reshape(b, h, lk, dv)
+    d["keep"] = np.array([[i != 2 and (i + j) % 3 != 0 for j in range(lk)] for i in range(lq)])
+    d["k1"] = O.normal(b * lk * dd, 0, 1, 24, 0).reshape(b, 1, lk, dd)
+    d["v1"] = O.normal(b * lk * dv, 0, 1, 25, 0).reshape(b, 1, lk, dv)
+    lq2 = 64
+    d["q2"] = O.normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 26, 0).reshape(4, lq2, 32)
+    d["k2"] = O.normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 27, 0).reshape(4, lq2, 32)
+    d["v2"] = O.normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 28, 0).reshape(4, lq2, 32)
+    return d

@@ -1,0 +1,111 @@
+"""Attention end to end on the B200 (§8(f) "next", rank 1): the batched GEMMs plus the softmax
+and masking between them, against the reference's own outputs (tests/golden/attention_cases.npz,
+made by running the reference's attention and softmax). Cases follow the reference's
+tests/ops/softmax_loss_test.cpp test_attention: plain, Bool mask broadcast over batch and heads
+(query 2 sees no key), causal, both with an explicit scale, and k/v shared by every head."""
+import numpy as np
+import pytest
+import torch
+
+import mensurflow_b200 as mf
+from helpers import attention_inputs, golden, ulp_diff
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(x, cuda):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+
+
+def test_softmax_matches_reference(cuda):
+    g = golden("attention_cases.npz")
+    x = attention_inputs()["softmax_x"]
+    for axis in (-1, 1, 0):
+        for log in (False, True):
+            fn = mf.log_softmax if log else mf.softmax
+            got = fn(dev(x, cuda), axis).cpu().numpy()
+            want = g[f"softmax_a{axis}_l{int(log)}"]
+            assert np.array_equal(np.isnan(got), np.isnan(want)), "NaN lines differ"
+            assert np.array_equal(np.isinf(got), np.isinf(want)), "-inf entries differ"
+            ok = ~np.isnan(want) & ~np.isinf(want)
+            if log:
+                # (x - max) - log(sum): near zero this cancels, so bound the error by the size of
+                # log(sum) (<= log(17) here): a few ulp of it, absolute
+                err = np.abs(got[ok].astype(np.float64) - want[ok])
+                assert err.max() <= 1e-6, f"log_softmax axis {axis}: {err.max():.3g}"
+            else:
+                d = ulp_diff(got[ok], want[ok])
+                # exp is CUDA's expf on the device and the C library's on the host: a few ulp
+                assert d.max() <= 4, f"softmax axis {axis}: {int(d.max())} ulp"
+    with pytest.raises(ValueError):
+        mf.softmax(dev(x, cuda), 3)
+    assert mf.device_status() == 0
+
+
+def test_where_matches_reference_semantics(cuda):
+    rng = np.random.default_rng(2)
+    cond = rng.random((4, 1, 6)) > 0.5
+    x = rng.standard_normal((4, 5, 6)).astype(np.float32)
+    y = np.float32(-np.inf)
+    got = mf.where(dev(cond, cuda), dev(x, cuda), torch.tensor(y, device=cuda)).cpu().numpy()
+    np.testing.assert_array_equal(got, O.where(cond, x, y))
+    with pytest.raises(ValueError):
+        mf.where(dev(x, cuda), dev(x, cuda), dev(x, cuda))  # condition must be Bool
+    assert mf.device_status() == 0
+
+
+@pytest.mark.parametrize("name", ["plain", "mask", "causal", "both"])
+def test_attention_cases(cuda, name):
+    a = attention_inputs()
+    g = golden("attention_cases.npz")
+    mask, causal, scale = {"plain": (None, False, 0.0), "mask": (a["keep"], False, 0.0),
+                           "causal": (None, True, 0.0), "both": (a["keep"], True, 0.5)}[name]
+    got = mf.attention(dev(a["q"], cuda), dev(a["k"], cuda), dev(a["v"], cuda),
+                       None if mask is None else dev(mask, cuda), causal, scale).cpu().numpy()
+    want = g[f"attention_{name}"]
+    # the reference's own attention test tolerance (softmax_loss_test.cpp: 1e-4, 1e-6)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-6, err_msg=name)
+    if mask is not None:
+        assert (got[:, :, 2, :] == 0.0).all(), "a query that sees no key gets zeros"
+    assert mf.device_status() == 0
+
+
+def test_attention_broadcast_and_causal_sizes(cuda):
+    a = attention_inputs()
+    g = golden("attention_cases.npz")
+    got = mf.attention(dev(a["q"], cuda), dev(a["k1"], cuda), dev(a["v1"], cuda)).cpu().numpy()
+    np.testing.assert_allclose(got, g["attention_broadcast_kv"], rtol=1e-4, atol=1e-6)
+    got = mf.attention(dev(a["q2"], cuda), dev(a["k2"], cuda), dev(a["v2"], cuda), None,
+                       True).cpu().numpy()
+    np.testing.assert_allclose(got, g["attention_causal_64"], rtol=1e-4, atol=1e-6)
+    with pytest.raises(ValueError):
+        mf.attention(dev(a["q"], cuda), torch.zeros(2, 3, 7, 9, device=cuda), dev(a["v"], cuda))
+    with pytest.raises(ValueError):
+        mf.attention(dev(a["q"], cuda), dev(a["k"], cuda), dev(a["v"], cuda),
+                     torch.ones(5, 7, device=cuda))  # non-Bool mask
+    with pytest.raises(ValueError):
+        mf.attention(dev(a["q"], cuda), dev(a["k"], cuda), dev(a["v"], cuda),
+                     torch.ones(4, 1, 5, 7, dtype=torch.bool, device=cuda))
+    assert mf.device_status() == 0
+
+
+def test_fused_mask_equals_where_then_softmax(cuda):
+    """The fused masked softmax gives the same bits as the reference's composition run with this
+    library's own where and softmax kernels."""
+    rng = np.random.default_rng(3)
+    s = dev(rng.standard_normal((6, 33, 47)).astype(np.float32) * 4, cuda)
+    keep = dev(rng.random((33, 47)) > 0.3, cuda)
+    lower = torch.ones(33, 47, dtype=torch.bool, device=cuda).tril()
+    composed = mf.softmax(mf.where(lower, mf.where(keep, s, torch.tensor(-np.inf, device=cuda)),
+                                   torch.tensor(-np.inf, device=cuda)), -1)
+    fused = s.clone()
+    kk = keep.expand(6, 33, 47)
+    from mensurflow_b200 import _lib
+    import ctypes  # noqa: F401
+    rc = _lib.lib().mfk_masked_softmax_f32(fused.data_ptr(), kk.data_ptr(), 0, 47, 1,
+                                           fused.data_ptr(), 6, 33, 47,
+                                           torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert torch.equal(fused, composed)
+    assert mf.device_status() == 0

@@ -109,3 +109,26 @@ def test_restatement_tracks_reference_on_random_inputs():
         want = O.ref_gemm(a, b, 1.5, c, -0.5)
         mag = 1.5 * O.abs_product(a, b) + 0.5 * np.abs(c)
         assert_close(got, want, mag, (1e-6, 1e-7), f"{m}x{n}x{k}")
+
+
+def test_softmax_and_attention_restatements_match_reference():
+    """Softmax restated bit for bit (expf per element, double sum); the composed attention oracle
+    within float rounding of the reference's attention (its own tests allow 1e-4)."""
+    from helpers import attention_inputs
+
+    g = golden("attention_cases.npz")
+    a = attention_inputs()
+    for axis in (-1, 1, 0):
+        for log in (False, True):
+            np.testing.assert_array_equal(O.softmax(a["softmax_x"], axis, log),
+                                          g[f"softmax_a{axis}_l{int(log)}"])
+    cases = {"plain": (None, False, 0.0), "mask": (a["keep"], False, 0.0),
+             "causal": (None, True, 0.0), "both": (a["keep"], True, 0.5)}
+    for name, (mask, causal, scale) in cases.items():
+        got = O.attention(a["q"], a["k"], a["v"], mask, causal, scale)
+        np.testing.assert_allclose(got, g[f"attention_{name}"], rtol=1e-5, atol=1e-6,
+                                   err_msg=name)
+    np.testing.assert_allclose(O.attention(a["q"], a["k1"], a["v1"]), g["attention_broadcast_kv"],
+                               rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(O.attention(a["q2"], a["k2"], a["v2"], None, True),
+                               g["attention_causal_64"], rtol=1e-5, atol=1e-6)

@@ -6,8 +6,9 @@ include/mfk.h) in place of its cuBLAS backend, and links the reference's matmul_
 matvec_test and elementwise_ops_test against it. Those programs check values on every device
 whose dispatcher has the kernel (tests/ops/matmul_test.cpp:97-100, matvec_test.cpp:69-72,
 elementwise_ops_test.cpp has_bias), so on a GPU box they run their CPU checks and then the same
-checks on cuda:0. The build needs the reference sources, so it happens where they are; the
-programs themselves run anywhere."""
+checks on cuda:0. reference_api_check is this repository's own program over the same library: it
+calls the reference's public API with Execution::GPU and Execution::CPU and compares them. The
+build needs the reference sources, so it happens where they are; the programs run anywhere."""
 import os
 import subprocess
 
@@ -19,7 +20,8 @@ BUILD = os.path.join(ROOT, "mensurflow_b200", "host", "_build")
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("name", ["matmul_test", "matvec_test", "elementwise_ops_test"])
+@pytest.mark.parametrize("name", ["matmul_test", "matvec_test", "elementwise_ops_test",
+                                  "reference_api_check"])
 def test_reference_program_passes_on_b200(cuda, name):
     path = os.path.join(BUILD, name)
     if not os.path.exists(path):
@@ -31,3 +33,9 @@ def test_reference_program_passes_on_b200(cuda, name):
     if name == "matmul_test":
         # the program lists each device it checks; the CUDA one must be among them
         assert "matmul on cuda:0" in out, out[-2000:]
+    if name == "reference_api_check":
+        # this repository's check program (mensurflow_b200/host/reference_api_check.cpp): the
+        # reference's public API with Execution::GPU against Execution::CPU, including
+        # gemm_strided_batched, attention and softmax, which the reference's programs do not run
+        # on a GPU
+        assert "on cuda:0" in out and "attention both" in out, out[-2000:]
