@@ -8,10 +8,10 @@
 //  * persistent: one CTA (CG = 1) or one CTA pair (CG = 2, a 2-CTA cluster on neighbouring SMs)
 //    per output tile of (128*CG) x BN, walking tiles in a grouped raster order so the A and B
 //    panels in flight stay in L2;
-//  * warp-specialised, 256 threads per CTA: warp 0 issues TMA loads into an mbarrier ring of
+//  * warp-specialised, 384 threads per CTA: warp 0 issues TMA loads into an mbarrier ring of
 //    STAGES shared-memory stages; warp 1 owns TMEM and one lane of the pair's first CTA issues
-//    tcgen05.mma; warps 4-7 are the epilogue (TMEM -> registers -> alpha/beta/bias/activation ->
-//    global memory);
+//    tcgen05.mma; warps 2-3 split A in shared memory (ASPLIT kernels); warps 4-11 are the
+//    epilogue (TMEM -> registers -> alpha/beta/bias/activation -> shared box -> TMA store);
 //  * operands are K-major fp32 tiles of 32 elements (128 B) per row, SWIZZLE_128B, read by the
 //    MMA through shared-memory descriptors; kind::tf32 with an fp32 accumulator in TMEM;
 //  * CG = 2 (cta_group::2): each CTA of the pair loads its 128 rows of A and its BN/2 rows of B
@@ -30,8 +30,10 @@ namespace mfk {
 
 constexpr int kBM = 128;          // rows of A per CTA = TMEM lanes
 constexpr int kBK = 32;           // fp32 depth per stage: one 128-byte swizzle row
-constexpr int kGemmThreads = 256;
-constexpr int kEpiWarp0 = 4;      // warps 4..7 are the epilogue warpgroup
+constexpr int kGemmThreads = 384;
+constexpr int kEpiWarp0 = 4;      // warps 4..11 are the epilogue (two warpgroups)
+constexpr int kEpiWarps = 8;
+constexpr int kEpiCols = 16;      // columns per epilogue chunk (one TMEM load, one store box)
 constexpr int kCvtWarp0 = 2;      // warps 2..3 split A in shared memory (ASPLIT kernels)
 constexpr int kCvtThreads = 64;
 
@@ -81,9 +83,9 @@ struct TcConfig {
                                      : (kAccStages * BN <= 128) ? 128
                                      : (kAccStages * BN <= 256) ? 256
                                                                 : 512;
-    // Epilogue staging: each of the 4 epilogue warps owns two 32 x 32 fp32 boxes (4 KB each).
-    static constexpr int kEpiBoxBytes = 32 * 32 * 4;
-    static constexpr int kEpiBytes = 4 * 2 * kEpiBoxBytes;
+    // Epilogue staging: each of the 8 epilogue warps owns two 32 x 16 fp32 boxes (2 KB each).
+    static constexpr int kEpiBoxBytes = 32 * kEpiCols * 4;
+    static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBoxBytes;
     static constexpr int kBarrierBytes = 256;
     static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + kBarrierBytes;
     static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeded");
@@ -424,19 +426,20 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
     }
 }
 
-// The epilogue of one 32-column chunk of a thread's row: alpha, beta*C_in, bias, activation,
-// with the reference's rounding steps. The activation is applied in a separate pass over the 32
-// values so each unrolled loop stays short.
+// The epilogue of one kEpiCols-column chunk of a thread's row: alpha, beta*C_in, bias,
+// activation, with the reference's rounding steps. The activation is applied in a separate pass
+// over the values so each unrolled loop stays short.
 struct EpiRow {
     const float* cin_row;
     bool has_cin, has_bias, vec_cin;
 };
 
 __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow& e, int col0,
-                                                 const uint32_t (&r)[32], float (&v)[32]) {
-    if (col0 + 32 <= g.n && (!e.has_cin || e.vec_cin)) {
+                                                 const uint32_t (&r)[kEpiCols],
+                                                 float (&v)[kEpiCols]) {
+    if (col0 + kEpiCols <= g.n && (!e.has_cin || e.vec_cin)) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
+        for (int j = 0; j < kEpiCols; j += 4) {
             float4 cin4 = make_float4(0.f, 0.f, 0.f, 0.f);
             if (e.has_cin) cin4 = *reinterpret_cast<const float4*>(e.cin_row + col0 + j);
             const float c4[4] = {cin4.x, cin4.y, cin4.z, cin4.w};
@@ -451,7 +454,7 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < kEpiCols; ++j) {
             const int col = col0 + j;
             float x = __uint_as_float(r[j]);
             if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
@@ -464,26 +467,30 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
     }
     if (g.act == kActRelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = v[j] < 0.0f ? 0.0f : v[j];
+        for (int j = 0; j < kEpiCols; ++j) v[j] = v[j] < 0.0f ? 0.0f : v[j];
     } else if (g.act == kActGelu) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_exact_f32_call(v[j]);
+        for (int j = 0; j < kEpiCols; ++j) v[j] = gelu_exact_f32_call(v[j]);
     } else if (g.act == kActGeluTanh) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f32_call(v[j]);
+        for (int j = 0; j < kEpiCols; ++j) v[j] = gelu_tanh_f32_call(v[j]);
     }
 }
 
+// Eight epilogue warps: warp w (4..11) reads TMEM lane quarter (w % 4) — the 32 rows it may
+// access — and the columns of its half of the tile ((w - 4) / 4), in chunks of kEpiCols.
 template <int CG, int BN, bool SPLIT3>
 __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap* tmC,
                                             uint8_t* epi_smem, uint32_t tmem_base,
                                             uint64_t* acc_full, uint64_t* acc_empty,
                                             uint32_t rank) {
     using C = TcConfig<CG, BN, SPLIT3>;
-    constexpr int kChunks = BN / 32;
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunks = kHalf / kEpiCols;
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    const int ew = warp - kEpiWarp0;  // TMEM lane quarter this warp may access
+    const int ew = warp % 4;                     // TMEM lane quarter this warp may access
+    const int half = (warp - kEpiWarp0) / 4;     // which half of the tile's columns
     EpiRow e;
     const bool has_cin = g.c_in != nullptr && g.beta != 0.0f;
     e.has_bias = g.bias != nullptr;
@@ -493,8 +500,8 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     const bool plain = !has_cin && !e.has_bias && g.act == kActNone;
     const bool vec_out = (g.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0) &&
                          (g.c_bs % 4 == 0);
-    // This warp's two staging boxes (32 rows of 128 B, SWIZZLE_128B as the TMA store reads them).
-    const uint32_t box0 = smem_u32(epi_smem + ew * 2 * C::kEpiBoxBytes);
+    // This warp's two staging boxes: 32 rows of 64 B, SWIZZLE_64B as the TMA store reads them.
+    const uint32_t box0 = smem_u32(epi_smem + (warp - kEpiWarp0) * 2 * C::kEpiBoxBytes);
     int box = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -511,22 +518,22 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                                     static_cast<long long>(row) * g.c_in_rs
                               : nullptr;
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
-                               static_cast<uint32_t>(acc * BN);
+                               static_cast<uint32_t>(acc * BN + half * kHalf);
         // Two register sets: the next chunk's TMEM load is in flight while this one is used.
-        uint32_t ra[32], rb[32];
-        tmem_ld_issue_32x32b_x32(tbase, ra);
+        uint32_t ra[kEpiCols], rb[kEpiCols];
+        tmem_ld_issue_32x32b_x16(tbase, ra);
         tmem_ld_wait();
 #pragma unroll
         for (int ci = 0; ci < kChunks; ++ci) {
-            uint32_t (&r)[32] = (ci & 1) ? rb : ra;
-            uint32_t (&rn)[32] = (ci & 1) ? ra : rb;
-            if (ci + 1 < kChunks) tmem_ld_issue_32x32b_x32(tbase + (ci + 1) * 32, rn);
-            const int col0 = tc.tn * BN + ci * 32;
+            uint32_t (&r)[kEpiCols] = (ci & 1) ? rb : ra;
+            uint32_t (&rn)[kEpiCols] = (ci & 1) ? ra : rb;
+            if (ci + 1 < kChunks) tmem_ld_issue_32x32b_x16(tbase + (ci + 1) * kEpiCols, rn);
+            const int col0 = tc.tn * BN + half * kHalf + ci * kEpiCols;
             if (col0 < g.n && row0 < g.m) {
-                float v[32];
+                float v[kEpiCols];
                 if (plain) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < kEpiCols; ++j) {
                         const float x = __uint_as_float(r[j]);
                         v[j] = g.alpha == 1.0f ? x : __fmul_rn(g.alpha, x);
                     }
@@ -537,10 +544,11 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                     const uint32_t buf = box0 + box * C::kEpiBoxBytes;
                     if (lane == 0) bulk_wait_read<1>();  // the store issued from this box has read it
                     __syncwarp();
+                    // row `lane` of the box: four 16-byte chunks, chunk q at q ^ ((lane >> 1) & 3)
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        st_shared_v4(buf + lane * 128 + ((q ^ (lane & 7)) << 4), v[4 * q],
-                                     v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    for (int q = 0; q < kEpiCols / 4; ++q) {
+                        st_shared_v4(buf + lane * (kEpiCols * 4) + ((q ^ ((lane >> 1) & 3)) << 4),
+                                     v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -550,15 +558,15 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                     }
                     box ^= 1;
                 } else if (row_ok) {
-                    if (col0 + 32 <= g.n && vec_out) {
+                    if (col0 + kEpiCols <= g.n && vec_out) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
+                        for (int j = 0; j < kEpiCols; j += 4) {
                             *reinterpret_cast<float4*>(crow + col0 + j) =
                                 make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
                         }
                     } else {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
+                        for (int j = 0; j < kEpiCols; ++j) {
                             if (col0 + j < g.n) crow[col0 + j] = v[j];
                         }
                     }
@@ -618,7 +626,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int s = 0; s < C::kAccStages; ++s) {
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], 4 * CG);  // every epilogue warp of the pair
+            mbar_init(&acc_empty[s], kEpiWarps * CG);  // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
         if constexpr (ASPLIT) {

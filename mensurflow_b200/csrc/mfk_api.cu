@@ -157,7 +157,8 @@ bool make_kmajor_map(CUtensorMap* map, const float* base, int64_t depth, int64_t
 }
 
 // The output C as a TMA store target: n columns x m rows x nmat matrices, row stride ldc, matrix
-// stride c_bs (elements), 32 x 32 boxes with the 128-byte swizzle the epilogue stages in.
+// stride c_bs (elements), boxes of 16 columns x 32 rows with the 64-byte swizzle the epilogue
+// stages in.
 bool make_store_map(CUtensorMap* map, float* c, int64_t n, int64_t m, int64_t nmat, int64_t ldc,
                     int64_t c_bs) {
     auto fn = encode_fn();
@@ -166,10 +167,10 @@ bool make_store_map(CUtensorMap* map, float* c, int64_t n, int64_t m, int64_t nm
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m),
                           static_cast<cuuint64_t>(nmat)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(ldc) * 4, static_cast<cuuint64_t>(c_bs) * 4};
-    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(mfk::kEpiCols), 32, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, c, dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
