@@ -12,6 +12,11 @@
 //    STAGES shared-memory stages; warp 1 owns TMEM and one lane of the pair's first CTA issues
 //    tcgen05.mma; warps 2-3 split A in shared memory (ASPLIT kernels); warps 4-11 are the
 //    epilogue (TMEM -> registers -> alpha/beta/bias/activation -> shared box -> TMA store);
+//  * ATMEM kernels (3xTF32, N <= 128, A read in place), 512 threads: A arrives raw and two
+//    groups of four converter warps (warps 4-7 and 12-15, alternate k-blocks) write its
+//    (hi, lo) split into a ring of TMEM slots that the MMA reads as its A operand (tcgen05.mma
+//    with A in tensor memory), so shared memory holds only raw A and B; warps 8-11 are the
+//    epilogue;
 //  * operands are K-major fp32 tiles of 32 elements (128 B) per row, SWIZZLE_128B, read by the
 //    MMA through shared-memory descriptors; kind::tf32 with an fp32 accumulator in TMEM;
 //  * CG = 2 (cta_group::2): each CTA of the pair loads its 128 rows of A and its BN/2 rows of B
@@ -36,6 +41,13 @@ constexpr int kEpiWarps = 8;
 constexpr int kEpiCols = 16;      // columns per epilogue chunk (one TMEM load, one store box)
 constexpr int kCvtWarp0 = 2;      // warps 2..3 split A in shared memory (ASPLIT kernels)
 constexpr int kCvtThreads = 64;
+// ATMEM kernels (A split into tensor memory), 512 threads: warps 4..7 and 12..15 convert (two
+// groups of one warp per TMEM lane quarter, taking alternate k-blocks), warps 8..11 are the
+// epilogue.
+constexpr int kTmCvtWarp0 = 4;
+constexpr int kTmCvtWarp1 = 12;
+constexpr int kTmEpiWarp0 = 8;
+constexpr int kTmThreads = 512;
 
 enum : unsigned int {
     kErrProducerWait = 1u << 0,
@@ -67,26 +79,38 @@ struct GemmArgs {
 };
 
 // CG: CTAs per MMA (1 or 2). BN: N of one MMA (columns of the tile). Per CTA: kBM rows of A,
-// BN/CG rows of B, a kBM x BN accumulator in TMEM.
-template <int CG, int BN, bool SPLIT3>
+// BN/CG rows of B, a kBM x BN accumulator in TMEM. ATMEM: A arrives raw and is split into a
+// ring of (hi, lo) slots in tensor memory, so a stage holds raw A and B's (hi, lo) only.
+template <int CG, int BN, bool SPLIT3, bool ATMEM = false>
 struct TcConfig {
     static constexpr int kBRows = BN / CG;
     static constexpr int kTileM = kBM * CG;
     static constexpr int kABytes = kBM * kBK * 4;
     static constexpr int kBBytes = kBRows * kBK * 4;
     static constexpr int kOps = SPLIT3 ? 2 : 1;
-    static constexpr int kStageBytes = kOps * (kABytes + kBBytes);  // per CTA
+    // per CTA; stage layout: A (hi or raw) | B hi | A lo | B lo  (ATMEM: A raw | B hi | B lo)
+    static constexpr int kStageBytes = ATMEM ? kABytes + 2 * kBBytes : kOps * (kABytes + kBBytes);
+    static constexpr int kOffBHi = kABytes;
+    static constexpr int kOffALo = kABytes + kBBytes;
+    static constexpr int kOffBLo = ATMEM ? kABytes + kBBytes : 2 * kABytes + kBBytes;
     static constexpr int kStages = (192 * 1024) / kStageBytes;
     static constexpr int kAccStages = 2;
-    static constexpr int kTmemCols = (kAccStages * BN <= 32)    ? 32
+    static constexpr int kTmemCols = ATMEM                      ? 512
+                                     : (kAccStages * BN <= 32)  ? 32
                                      : (kAccStages * BN <= 64)  ? 64
                                      : (kAccStages * BN <= 128) ? 128
                                      : (kAccStages * BN <= 256) ? 256
                                                                 : 512;
-    // Epilogue staging: each of the 8 epilogue warps owns two 32 x 16 fp32 boxes (2 KB each).
+    // ATMEM: slots of 64 columns (hi: 32, lo: 32 — one k-block) after the accumulators
+    static constexpr int kACol0 = kAccStages * BN;
+    static constexpr int kASlots = ATMEM ? (512 - kACol0) / 64 : 0;
+    static constexpr int kThreads = ATMEM ? kTmThreads : kGemmThreads;
+    static constexpr int kEpiWarp0C = ATMEM ? kTmEpiWarp0 : kEpiWarp0;
+    static constexpr int kEpiWarpsC = ATMEM ? 4 : kEpiWarps;
+    // Epilogue staging: each epilogue warp owns two 32 x 16 fp32 boxes (2 KB each).
     static constexpr int kEpiBoxBytes = 32 * kEpiCols * 4;
-    static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBoxBytes;
-    static constexpr int kBarrierBytes = 256;
+    static constexpr int kEpiBytes = kEpiWarpsC * 2 * kEpiBoxBytes;
+    static constexpr int kBarrierBytes = 512;
     static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + kBarrierBytes;
     static_assert(kSmemBytes <= 232448, "shared memory per CTA exceeded");
     static_assert(CG == 1 || CG == 2, "one or two CTAs per MMA");
@@ -94,6 +118,7 @@ struct TcConfig {
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be 32..256, multiple of 32");
     static_assert(kBRows % 8 == 0, "B rows per CTA must be a multiple of 8");
     static_assert(kStages >= 2, "need at least two stages");
+    static_assert(!ATMEM || (SPLIT3 && kASlots >= 2), "ATMEM: 3xTF32 with two or more A slots");
 };
 
 struct TileCoord {
@@ -226,14 +251,15 @@ __device__ __forceinline__ long long tile_step() {
 }
 
 // ASPLIT (3xTF32 only): A arrives as raw fp32 in the A_hi slot, completing on this CTA's own
-// a_full barrier, and the converter warps write hi (in place) and lo; B arrives pre-split.
-template <int CG, int BN, bool SPLIT3, bool ASPLIT>
+// a_full barrier, and the converter warps write hi and lo (in shared memory, or for ATMEM into
+// tensor memory); B arrives pre-split.
+template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM>
 __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap* tmA0,
                                             const CUtensorMap* tmA1, const CUtensorMap* tmB0,
                                             const CUtensorMap* tmB1, uint8_t* stages,
                                             uint64_t* full, uint64_t* empty, uint64_t* a_full,
                                             uint32_t rank) {
-    using C = TcConfig<CG, BN, SPLIT3>;
+    using C = TcConfig<CG, BN, SPLIT3, ATMEM>;
     static_assert(!ASPLIT || SPLIT3, "the in-kernel split is a 3xTF32 feature");
     const uint64_t pol = l2_policy_evict_last();
     // bytes that complete on `full`: everything, or only B's pair when A has its own barrier
@@ -250,9 +276,9 @@ __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap
             if (!mbar_wait(&empty[stage], phase ^ 1u, kErrProducerWait)) return;
             uint8_t* s = stages + stage * C::kStageBytes;
             uint8_t* s_ahi = s;
-            uint8_t* s_bhi = s + C::kABytes;
-            uint8_t* s_alo = s + C::kABytes + C::kBBytes;
-            uint8_t* s_blo = s + 2 * C::kABytes + C::kBBytes;
+            uint8_t* s_bhi = s + C::kOffBHi;
+            uint8_t* s_alo = s + C::kOffALo;
+            uint8_t* s_blo = s + C::kOffBLo;
             const int kx = kb * kBK;
             if constexpr (ASPLIT) {
                 mbar_arrive_expect_tx(&a_full[stage], C::kABytes);
@@ -286,9 +312,9 @@ __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap
 }
 
 // The converter warps of an ASPLIT kernel: for every stage, once this CTA's raw A tile has
-// landed, hi = tf32_rna(x) in place and lo = tf32_rna(x - hi) into the A_lo slot (an elementwise
-// pass, so the 128-byte swizzle of the tile carries over) — or, where the tensor cores are known
-// to truncate fp32 operands (g.raw_hi), only lo = tf32_rna(x - trunc(x)) — then a proxy fence
+// landed, split_tf32(x) writes hi in place and lo into the A_lo slot (an elementwise pass, so
+// the 128-byte swizzle of the tile carries over) — or, where the tensor cores are known to
+// truncate fp32 operands (g.raw_hi), only lo, since truncated x is hi — then a proxy fence
 // so the MMA's async reads see the generic writes, and one arrival per warp on the MMA issuer's
 // `converted` barrier.
 template <int CG, int BN, bool SPLIT3>
@@ -310,11 +336,11 @@ __device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, u
 #pragma unroll 4
                 for (int i = ct; i < C::kABytes / 16; i += kCvtThreads) {
                     const float4 x = hi[i];
-                    float4 l;
-                    l.x = tf32_rna(x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u));
-                    l.y = tf32_rna(x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u));
-                    l.z = tf32_rna(x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u));
-                    l.w = tf32_rna(x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u));
+                    float4 h, l;
+                    split_tf32(x.x, h.x, l.x);
+                    split_tf32(x.y, h.y, l.y);
+                    split_tf32(x.z, h.z, l.z);
+                    split_tf32(x.w, h.w, l.w);
                     lo[i] = l;
                 }
             } else {
@@ -322,14 +348,10 @@ __device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, u
                 for (int i = ct; i < C::kABytes / 16; i += kCvtThreads) {
                     const float4 x = hi[i];
                     float4 h, l;
-                    h.x = tf32_rna(x.x);
-                    h.y = tf32_rna(x.y);
-                    h.z = tf32_rna(x.z);
-                    h.w = tf32_rna(x.w);
-                    l.x = tf32_rna(x.x - h.x);
-                    l.y = tf32_rna(x.y - h.y);
-                    l.z = tf32_rna(x.z - h.z);
-                    l.w = tf32_rna(x.w - h.w);
+                    split_tf32(x.x, h.x, l.x);
+                    split_tf32(x.y, h.y, l.y);
+                    split_tf32(x.z, h.z, l.z);
+                    split_tf32(x.w, h.w, l.w);
                     hi[i] = h;
                     lo[i] = l;
                 }
@@ -351,18 +373,90 @@ __device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, u
     }
 }
 
+// The converter warps of an ATMEM kernel, one per TMEM lane quarter (warp % 4): thread `lane`
+// of warp q owns row 32q + lane of the CTA's A tile. For every k-block it reads the row's 32
+// raw fp32 values out of the swizzled stage (16-byte chunk c of row r sits at c ^ (r % 8)),
+// releases the stage's A half, and writes split_tf32(x) into the next slot of the TMEM ring:
+// columns [slot*64, +32) hold hi, [+32, +64) lo, one k per column. hi and lo are both exact
+// tf32 values, so the MMA's own fp32 -> tf32 conversion never applies.
+template <int CG, int BN>
+__device__ __forceinline__ void tc_convert_tmem(const GemmArgs& g, uint8_t* stages,
+                                                uint64_t* a_full, uint64_t* empty,
+                                                uint64_t* tfull, uint64_t* tempty,
+                                                uint32_t tmem_base, int group) {
+    using C = TcConfig<CG, BN, true, true>;
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int q = warp % 4;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const long long total = (g.num_tiles - first_tile<CG>() + tile_step<CG>() - 1) /
+                            tile_step<CG>() * g.num_kb;
+    // k-block i of this CTA's sequence uses stage i % kStages and slot i % kASlots
+    for (long long i = group; i < total; i += 2) {
+        {
+            const int stage = static_cast<int>(i % C::kStages);
+            const uint32_t phase = static_cast<uint32_t>((i / C::kStages) & 1);
+            const int slot = static_cast<int>(i % C::kASlots);
+            const uint32_t tphase = static_cast<uint32_t>((i / C::kASlots) & 1);
+            if (!mbar_wait(&a_full[stage], phase, kErrConvertWait)) return;
+            const uint32_t rowp = smem_u32(stages + stage * C::kStageBytes) + row * 128;
+            float x[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float4 v = ld_shared_v4(rowp + ((c ^ (row & 7)) << 4));
+                x[4 * c] = v.x;
+                x[4 * c + 1] = v.y;
+                x[4 * c + 2] = v.z;
+                x[4 * c + 3] = v.w;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);  // this warp's rows of A are read
+            if (!mbar_wait(&tempty[slot], tphase ^ 1u, kErrConvertWait)) return;
+            tc_fence_after();
+            const uint32_t col = static_cast<uint32_t>(C::kACol0 + slot * 64);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float fh, fl;
+                    split_tf32(x[16 * h + j], fh, fl);
+                    hi[j] = __float_as_uint(fh);
+                    lo[j] = __float_as_uint(fl);
+                }
+                tmem_st_32x32b_x16(lane_base + col + 16 * h, hi);
+                tmem_st_32x32b_x16(lane_base + col + 32 + 16 * h, lo);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (CG == 1) {
+                    mbar_arrive(&tfull[slot]);
+                } else {
+                    mbar_arrive_cluster(mapa_shared(&tfull[slot], 0));
+                }
+            }
+        }
+    }
+}
+
 // Runs on one lane of the pair's first CTA (or of the single CTA).
-template <int CG, int BN, bool SPLIT3, bool ASPLIT>
+template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM>
 __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, uint8_t* stages,
                                        uint64_t* full, uint64_t* empty, uint64_t* acc_full,
-                                       uint64_t* acc_empty, uint64_t* converted) {
-    using C = TcConfig<CG, BN, SPLIT3>;
+                                       uint64_t* acc_empty, uint64_t* converted,
+                                       uint64_t* tempty) {
+    using C = TcConfig<CG, BN, SPLIT3, ATMEM>;
     constexpr uint32_t idesc = idesc_tf32(C::kTileM, BN, false, false);
     constexpr uint16_t kPair = (1u << CG) - 1u;
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int slot = 0;             // ATMEM: the TMEM ring slot holding this k-block's A (hi, lo)
+    uint32_t tphase = 0;
     const uint32_t stage0 = smem_u32(stages);
     for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kErrMmaWait)) return;
@@ -370,44 +464,80 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < g.num_kb; ++kb) {
             if (!mbar_wait(&full[stage], phase, kErrMmaWait)) return;
-            if constexpr (ASPLIT) {
+            if constexpr (ATMEM) {
+                if (!mbar_wait(&converted[slot], tphase, kErrMmaWait)) return;
+            } else if constexpr (ASPLIT) {
                 if (!mbar_wait(&converted[stage], phase, kErrMmaWait)) return;
             }
             tc_fence_after();
             const uint32_t a_hi = stage0 + stage * C::kStageBytes;
-            const uint32_t b_hi = a_hi + C::kABytes;
-            const uint32_t a_lo = b_hi + C::kBBytes;
-            const uint32_t b_lo = a_lo + C::kABytes;
+            const uint32_t b_hi = a_hi + C::kOffBHi;
+            const uint32_t a_lo = a_hi + C::kOffALo;
+            const uint32_t b_lo = a_hi + C::kOffBLo;
+            if constexpr (ATMEM) {
+                // A from the TMEM slot: hi at column kACol0 + slot*64 + k, lo 32 columns on
+                const uint32_t ta = tmem_base + static_cast<uint32_t>(C::kACol0 + slot * 64);
 #pragma unroll
-            for (int ks = 0; ks < kBK / 8; ++ks) {
-                const uint32_t koff = ks * 32;  // 8 tf32 = 32 bytes along the swizzled row
-                const uint64_t dah = smem_desc(a_hi + koff, 16, 1024, kSwizzle128B);
-                const uint64_t dbh = smem_desc(b_hi + koff, 16, 1024, kSwizzle128B);
-                const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
-                if constexpr (SPLIT3) {
-                    const uint64_t dal = smem_desc(a_lo + koff, 16, 1024, kSwizzle128B);
+                for (int ks = 0; ks < kBK / 8; ++ks) {
+                    const uint32_t koff = ks * 32;
+                    const uint64_t dbh = smem_desc(b_hi + koff, 16, 1024, kSwizzle128B);
                     const uint64_t dbl = smem_desc(b_lo + koff, 16, 1024, kSwizzle128B);
+                    const uint32_t tah = ta + ks * 8;
+                    const uint32_t tal = tah + 32;
+                    const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
                     if constexpr (CG == 1) {
-                        mma_tf32(d_tmem, dal, dbh, idesc, accumulate);
-                        mma_tf32(d_tmem, dah, dbl, idesc, 1u);
-                        mma_tf32(d_tmem, dah, dbh, idesc, 1u);
+                        mma_tf32_ts(d_tmem, tal, dbh, idesc, accumulate);
+                        mma_tf32_ts(d_tmem, tah, dbl, idesc, 1u);
+                        mma_tf32_ts(d_tmem, tah, dbh, idesc, 1u);
                     } else {
-                        mma_tf32_cg2(d_tmem, dal, dbh, idesc, accumulate);
-                        mma_tf32_cg2(d_tmem, dah, dbl, idesc, 1u);
-                        mma_tf32_cg2(d_tmem, dah, dbh, idesc, 1u);
-                    }
-                } else {
-                    if constexpr (CG == 1) {
-                        mma_tf32(d_tmem, dah, dbh, idesc, accumulate);
-                    } else {
-                        mma_tf32_cg2(d_tmem, dah, dbh, idesc, accumulate);
+                        mma_tf32_ts_cg2(d_tmem, tal, dbh, idesc, accumulate);
+                        mma_tf32_ts_cg2(d_tmem, tah, dbl, idesc, 1u);
+                        mma_tf32_ts_cg2(d_tmem, tah, dbh, idesc, 1u);
                     }
                 }
-            }
-            if constexpr (CG == 1) {
-                mma_commit(&empty[stage]);
+                if constexpr (CG == 1) {
+                    mma_commit(&empty[stage]);
+                    mma_commit(&tempty[slot]);
+                } else {
+                    mma_commit_cg2_mc(&empty[stage], kPair);
+                    mma_commit_cg2_mc(&tempty[slot], kPair);
+                }
+                if (++slot == C::kASlots) {
+                    slot = 0;
+                    tphase ^= 1u;
+                }
             } else {
-                mma_commit_cg2_mc(&empty[stage], kPair);  // frees the stage in both CTAs
+#pragma unroll
+                for (int ks = 0; ks < kBK / 8; ++ks) {
+                    const uint32_t koff = ks * 32;  // 8 tf32 = 32 bytes along the swizzled row
+                    const uint64_t dah = smem_desc(a_hi + koff, 16, 1024, kSwizzle128B);
+                    const uint64_t dbh = smem_desc(b_hi + koff, 16, 1024, kSwizzle128B);
+                    const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
+                    if constexpr (SPLIT3) {
+                        const uint64_t dal = smem_desc(a_lo + koff, 16, 1024, kSwizzle128B);
+                        const uint64_t dbl = smem_desc(b_lo + koff, 16, 1024, kSwizzle128B);
+                        if constexpr (CG == 1) {
+                            mma_tf32(d_tmem, dal, dbh, idesc, accumulate);
+                            mma_tf32(d_tmem, dah, dbl, idesc, 1u);
+                            mma_tf32(d_tmem, dah, dbh, idesc, 1u);
+                        } else {
+                            mma_tf32_cg2(d_tmem, dal, dbh, idesc, accumulate);
+                            mma_tf32_cg2(d_tmem, dah, dbl, idesc, 1u);
+                            mma_tf32_cg2(d_tmem, dah, dbh, idesc, 1u);
+                        }
+                    } else {
+                        if constexpr (CG == 1) {
+                            mma_tf32(d_tmem, dah, dbh, idesc, accumulate);
+                        } else {
+                            mma_tf32_cg2(d_tmem, dah, dbh, idesc, accumulate);
+                        }
+                    }
+                }
+                if constexpr (CG == 1) {
+                    mma_commit(&empty[stage]);
+                } else {
+                    mma_commit_cg2_mc(&empty[stage], kPair);  // frees the stage in both CTAs
+                }
             }
             if (++stage == C::kStages) {
                 stage = 0;
@@ -477,20 +607,21 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
     }
 }
 
-// Eight epilogue warps: warp w (4..11) reads TMEM lane quarter (w % 4) — the 32 rows it may
-// access — and the columns of its half of the tile ((w - 4) / 4), in chunks of kEpiCols.
-template <int CG, int BN, bool SPLIT3>
+// The epilogue warps (eight, or four in ATMEM kernels): warp w reads TMEM lane quarter (w % 4)
+// — the 32 rows it may access — and, with eight warps, the columns of its half of the tile, in
+// chunks of kEpiCols.
+template <int CG, int BN, bool SPLIT3, bool ATMEM>
 __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap* tmC,
                                             uint8_t* epi_smem, uint32_t tmem_base,
                                             uint64_t* acc_full, uint64_t* acc_empty,
                                             uint32_t rank) {
-    using C = TcConfig<CG, BN, SPLIT3>;
-    constexpr int kHalf = BN / 2;
+    using C = TcConfig<CG, BN, SPLIT3, ATMEM>;
+    constexpr int kHalf = BN / (C::kEpiWarpsC / 4);  // columns per warp
     constexpr int kChunks = kHalf / kEpiCols;
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    const int ew = warp % 4;                     // TMEM lane quarter this warp may access
-    const int half = (warp - kEpiWarp0) / 4;     // which half of the tile's columns
+    const int ew = warp % 4;                            // TMEM lane quarter this warp may access
+    const int half = (warp - C::kEpiWarp0C) / 4;        // which part of the tile's columns
     EpiRow e;
     const bool has_cin = g.c_in != nullptr && g.beta != 0.0f;
     e.has_bias = g.bias != nullptr;
@@ -501,7 +632,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     const bool vec_out = (g.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0) &&
                          (g.c_bs % 4 == 0);
     // This warp's two staging boxes: 32 rows of 64 B, SWIZZLE_64B as the TMA store reads them.
-    const uint32_t box0 = smem_u32(epi_smem + (warp - kEpiWarp0) * 2 * C::kEpiBoxBytes);
+    const uint32_t box0 = smem_u32(epi_smem + (warp - C::kEpiWarp0C) * 2 * C::kEpiBoxBytes);
     int box = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -593,14 +724,15 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     __syncwarp();
 }
 
-template <int CG, int BN, bool SPLIT3, bool ASPLIT>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM = false>
+__global__ void __launch_bounds__(TcConfig<CG, BN, SPLIT3, ATMEM>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0,
                    const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmB1,
                    const __grid_constant__ CUtensorMap tmC, const GemmArgs g) {
-    using C = TcConfig<CG, BN, SPLIT3>;
+    using C = TcConfig<CG, BN, SPLIT3, ATMEM>;
+    static_assert(!ATMEM || ASPLIT, "the TMEM split is a form of the in-kernel split");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* stages = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -612,8 +744,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* acc_empty = acc_full + C::kAccStages;
     uint64_t* drain = acc_empty + C::kAccStages;
     uint64_t* a_full = drain + 1;                // ASPLIT: raw A landed in this CTA
-    uint64_t* converted = a_full + C::kStages;   // ASPLIT: both CTAs' A split (first CTA's)
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(converted + C::kStages);
+    // ASPLIT: both CTAs' A split (first CTA's barrier; per stage, or per TMEM slot for ATMEM)
+    uint64_t* converted = a_full + C::kStages;
+    uint64_t* tempty = converted + C::kStages;   // ATMEM: the MMAs reading a TMEM slot are done
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + (ATMEM ? C::kASlots : 0));
+    static_assert((3 * C::kStages + 2 * C::kAccStages + 1 + C::kASlots) * 8 + 4 <=
+                      C::kBarrierBytes,
+                  "barrier area too small");
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -622,14 +759,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            // ATMEM: the MMAs' commit (B read) and this CTA's four converter warps (A read)
+            mbar_init(&empty[s], ATMEM ? 5 : 1);
         }
         for (int s = 0; s < C::kAccStages; ++s) {
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], kEpiWarps * CG);  // every epilogue warp of the pair
+            mbar_init(&acc_empty[s], C::kEpiWarpsC * CG);  // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
-        if constexpr (ASPLIT) {
+        if constexpr (ATMEM) {
+            for (int s = 0; s < C::kStages; ++s) mbar_init(&a_full[s], 1);
+            for (int s = 0; s < C::kASlots; ++s) {
+                mbar_init(&converted[s], 4 * CG);  // the four converter warps of every CTA
+                mbar_init(&tempty[s], 1);
+            }
+        } else if constexpr (ASPLIT) {
             for (int s = 0; s < C::kStages; ++s) {
                 mbar_init(&a_full[s], 1);
                 mbar_init(&converted[s], 2 * CG);  // both converter warps of every CTA
@@ -661,12 +805,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (warp == 0) {
         if (lane == 0)
-            tc_producer<CG, BN, SPLIT3, ASPLIT>(g, &tmA0, &tmA1, &tmB0, &tmB1, stages, full, empty,
-                                                a_full, rank);
+            tc_producer<CG, BN, SPLIT3, ASPLIT, ATMEM>(g, &tmA0, &tmA1, &tmB0, &tmB1, stages, full,
+                                                       empty, a_full, rank);
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            tc_mma<CG, BN, SPLIT3, ASPLIT>(g, tmem_base, stages, full, empty, acc_full, acc_empty,
-                                           converted);
+            tc_mma<CG, BN, SPLIT3, ASPLIT, ATMEM>(g, tmem_base, stages, full, empty, acc_full,
+                                                  acc_empty, converted, tempty);
             // Every MMA issued above must finish before TMEM is released, also on an error exit.
             if constexpr (CG == 1) {
                 mma_commit(drain);
@@ -676,10 +820,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_wait(drain, 0, kErrMmaWait);
         }
         __syncwarp();
-    } else if (ASPLIT && warp >= kCvtWarp0 && warp < kCvtWarp0 + kCvtThreads / 32) {
+    } else if (ATMEM && ((warp >= kTmCvtWarp0 && warp < kTmCvtWarp0 + 4) || warp >= kTmCvtWarp1)) {
+        if constexpr (ATMEM) {
+            tc_convert_tmem<CG, BN>(g, stages, a_full, empty, converted, tempty, tmem_base,
+                                    warp >= kTmCvtWarp1 ? 1 : 0);
+        }
+    } else if (!ATMEM && ASPLIT && warp >= kCvtWarp0 && warp < kCvtWarp0 + kCvtThreads / 32) {
         tc_convert<CG, BN, SPLIT3>(g, stages, a_full, converted);
-    } else if (warp >= kEpiWarp0) {
-        tc_epilogue<CG, BN, SPLIT3>(g, &tmC, epi_smem, tmem_base, acc_full, acc_empty, rank);
+    } else if (warp >= C::kEpiWarp0C && warp < C::kEpiWarp0C + C::kEpiWarpsC) {
+        tc_epilogue<CG, BN, SPLIT3, ATMEM>(g, &tmC, epi_smem, tmem_base, acc_full, acc_empty,
+                                           rank);
     }
 
     tc_fence_before();

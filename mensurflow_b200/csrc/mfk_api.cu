@@ -233,16 +233,17 @@ constexpr int64_t kInKernelSplitMaxN = 384;
 
 
 
-// One kernel instantiation per (CG, BN, SPLIT3); `slot` indexes its per-device set-up flags.
-template <int CG, int BN, bool SPLIT3, bool ASPLIT>
+// One kernel instantiation per (CG, BN, SPLIT3, ASPLIT, ATMEM); `slot` indexes its per-device
+// set-up flags.
+template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM = false>
 int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
               const CUtensorMap& b1, const CUtensorMap& cmap, const GemmArgs& g, DeviceInfo* info,
               int slot, cudaStream_t stream) {
-    using C = mfk::TcConfig<CG, BN, SPLIT3>;
-    auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3, ASPLIT>;
+    using C = mfk::TcConfig<CG, BN, SPLIT3, ATMEM>;
+    auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3, ASPLIT, ATMEM>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    cfg.blockDim = dim3(mfk::kGemmThreads, 1, 1);
+    cfg.blockDim = dim3(C::kThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = stream;
     if (CG > 1) {
@@ -375,8 +376,8 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     const bool split3 = precision == MFK_PRECISION_3XTF32;
     // The in-kernel split of A may leave hi as the raw fp32 values where the tensor cores are
     // known to truncate them (writing only lo: a third less shared-memory traffic).
-    const bool raw_hi = split3 && d->k > 0 && d->n <= kInKernelSplitMaxN &&
-                        tf32_truncates(info, stream, fixed == nullptr);
+    const bool raw_hi = split3 && d->k > 0 && d->n > 128 && d->n <= kInKernelSplitMaxN &&
+                        d->m > mfk::kBM && tf32_truncates(info, stream, fixed == nullptr);
 
     GemmArgs g{};
     g.m = static_cast<int>(d->m);
@@ -565,12 +566,16 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         return split3 ? launch_tc<2, 256, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 0, stream)
                       : launch_tc<2, 256, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 1, stream);
     }
+    // N <= 128 with A split in place: the split goes to tensor memory (ATMEM), which leaves
+    // shared memory to the B tiles and the raw A stages.
     if (cg == 2) {
-        if (asplit) return launch_tc<2, 128, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 7, stream);
+        if (asplit) {
+            return launch_tc<2, 128, true, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 9, stream);
+        }
         return split3 ? launch_tc<2, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 2, stream)
                       : launch_tc<2, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 3, stream);
     }
-    if (asplit) return launch_tc<1, 128, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 8, stream);
+    if (asplit) return launch_tc<1, 128, true, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 10, stream);
     return split3 ? launch_tc<1, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 4, stream)
                   : launch_tc<1, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 5, stream);
 }

@@ -149,6 +149,17 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// The same with A in tensor memory, one CTA.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrives once on `bar` when every tcgen05.mma this thread issued before has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
@@ -201,6 +212,23 @@ __device__ __forceinline__ void tmem_ld_issue_32x32b_x16(uint32_t taddr, uint32_
         : "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit columns from registers into tensor memory (thread t of the
+// warp writes lane base + t).
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15])
+        : "memory");
+}
+
+// Wait until every tcgen05.st this thread issued has completed.
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // ... and wait for every load this thread issued (registers valid after it).
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -251,10 +279,13 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
     return r;
 }
 
+// Arrive on an mbarrier of another CTA of the cluster, with the default (release, CTA scope)
+// semantics, as CUTLASS's cluster barriers do: the data it publishes is either tensor memory,
+// ordered by tcgen05.wait + tcgen05.fence::before_thread_sync, or shared memory read by the
+// async proxy, ordered by fence.proxy.async. An explicit .release.cluster costs ~1700 cycles
+// per arrive on B200 (measured), which on a per-k-block signal throttles the whole pipeline.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-                     cluster_addr)
-                 : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 3-D tiled load into this CTA's shared memory whose completion is counted on an mbarrier that
@@ -291,6 +322,18 @@ __device__ __forceinline__ void mma_tf32_cg2(uint32_t d_tmem, uint64_t a_desc, u
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[tmem: lanes = the CTA's 128 rows, one 32-bit column per k]
+// * B[smem desc, N/2 rows in each CTA]. A read from tensor memory must be K-major.
+__device__ __forceinline__ void mma_tf32_ts_cg2(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -344,11 +387,43 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
                  : "memory");
 }
 
-// Round to the nearest tf32 (ties away from zero), with the documented PTX conversion.
-__device__ __forceinline__ float tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
+// Rounding of a finite fp32 bit pattern to tf32 (10 mantissa bits), nearest with ties away
+// from zero, by IEEE bit arithmetic: add half a tf32 ulp to the magnitude bits (a carry runs
+// into the exponent as it should) and clear the 13 low bits. Plain integer ops; the
+// cvt.rna.tf32.f32 instruction measured ~50 cycles per warp on B200 in an issue-bound loop.
+__device__ __forceinline__ uint32_t tf32_round_bits(uint32_t b) {
+    return (b + 0x1000u) & 0xFFFFE000u;
+}
+
+// The 3xTF32 split of x: hi = x truncated to tf32 (13 low mantissa bits cleared, so it never
+// overflows), lo = x - hi (exact) rounded to tf32. Non-finite x: hi = x with a NaN's quiet bit
+// set (clearing low bits could otherwise turn a NaN into an infinity), lo = 0, so an infinite
+// operand yields an infinite product rather than inf - inf.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    const uint32_t xb = __float_as_uint(x);
+    const bool finite = (xb & 0x7F800000u) != 0x7F800000u;
+    const uint32_t hb = xb & 0xFFFFE000u;
+    const uint32_t lb = tf32_round_bits(__float_as_uint(x - __uint_as_float(hb)));
+    hi = __uint_as_float(finite ? hb : (xb | ((xb & 0x007FFFFFu) ? 0x00400000u : 0u)));
+    lo = __uint_as_float(finite ? lb : 0u);
+}
+
+// x rounded to tf32 (nearest, ties away from zero); a finite value that would round past the
+// largest tf32 is truncated instead; non-finite values pass through.
+__device__ __forceinline__ float round_tf32(float x) {
+    const uint32_t xb = __float_as_uint(x);
+    if ((xb & 0x7F800000u) == 0x7F800000u) return x;
+    const uint32_t r = tf32_round_bits(xb);
+    return __uint_as_float((r & 0x7F800000u) == 0x7F800000u ? (xb & 0xFFFFE000u) : r);
+}
+
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -14,8 +14,8 @@ namespace mfk {
 
 enum PackMode : int {
     kPackCopy = 0,   // hi = x
-    kPackRound = 1,  // hi = tf32(x)
-    kPackSplit = 2,  // hi = tf32(x), lo = tf32(x - hi)
+    kPackRound = 1,  // hi = round_tf32(x)
+    kPackSplit = 2,  // split_tf32: hi = x truncated to tf32, lo = tf32(x - hi)
 };
 
 // op(X) of matrix b: element (r, p) at x[off(b) + r*rs + p*cs], with off(b) = offsets[b] when
@@ -59,10 +59,13 @@ __global__ void __launch_bounds__(256) pack_kmajor_kernel(
             const long long o = out_base + static_cast<long long>(r) * Kp + p;
             if (mode == kPackCopy) {
                 hi[o] = v;
+            } else if (mode == kPackRound) {
+                hi[o] = round_tf32(v);
             } else {
-                const float h = tf32_rna(v);
+                float h, l;
+                split_tf32(v, h, l);
                 hi[o] = h;
-                if (mode == kPackSplit) lo[o] = tf32_rna(v - h);
+                lo[o] = l;
             }
         }
     }
@@ -94,15 +97,16 @@ __global__ void __launch_bounds__(256) pack_kmajor_vec4_kernel(
         float4* h4 = reinterpret_cast<float4*>(hi) + i;
         if (mode == kPackCopy) {
             *h4 = v;
+        } else if (mode == kPackRound) {
+            *h4 = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
         } else {
-            const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z),
-                                         tf32_rna(v.w));
+            float4 h, l;
+            split_tf32(v.x, h.x, l.x);
+            split_tf32(v.y, h.y, l.y);
+            split_tf32(v.z, h.z, l.z);
+            split_tf32(v.w, h.w, l.w);
             *h4 = h;
-            if (mode == kPackSplit) {
-                reinterpret_cast<float4*>(lo)[i] =
-                    make_float4(tf32_rna(v.x - h.x), tf32_rna(v.y - h.y), tf32_rna(v.z - h.z),
-                                tf32_rna(v.w - h.w));
-            }
+            reinterpret_cast<float4*>(lo)[i] = l;
         }
     }
 }

@@ -166,6 +166,28 @@ def test_random_gemm(cuda, precision, shape, trans):
     no_fault()
 
 
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("shape", [(300, 64, 200), (300, 256, 200), (300, 640, 200), (100, 64, 70)])
+def test_nan_operands(cuda, precision, shape):
+    """A NaN in a row of A makes that row of C NaN on every kernel variant (A split in tensor
+    memory for N <= 128, in shared memory for N <= 384, pre-split operands above, 1xTF32);
+    the other rows are unaffected. The 3xTF32 split gives a NaN hi with a zero lo."""
+    m, n, k = shape
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    bad = [3, m // 2, m - 1]
+    for r in bad:
+        a[r, (r * 7) % k] = np.nan
+    got = host(mf.matmul(dev(a, cuda), dev(b, cuda), precision=precision))
+    assert np.isnan(got[bad]).all()
+    good = np.setdiff1d(np.arange(m), bad)
+    a_ok = a[good]
+    assert_close(got[good], O.gemm(a_ok, b), O.abs_product(a_ok, b), tol(precision),
+                 f"finite rows {shape} {precision}")
+    no_fault()
+
+
 @pytest.mark.parametrize("act", ["relu", "gelu", "gelu_tanh"])
 def test_fused_activation(cuda, act):
     s = seeded_inputs()
