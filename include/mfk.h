@@ -136,6 +136,31 @@ int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream);
 int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc* batch,
                                  void* stream);
 
+/* B split once, for many products with the same B: the device analogue of the reference's
+ * PackedB (src/backends/cpu/ops/gemm/gemm_packed.hpp:147-191: pack_b_f32, matmul_f32_prepacked),
+ * for weights that are only evaluated. The handle owns device memory on the device current at
+ * packing time holding op(B) as K-major tf32 panels — (hi, lo) for 3xTF32, rounded values for
+ * 1xTF32 — so products with it skip B's split pass.
+ *
+ * mfk_pack_b_f32: B is k x n on the current device, element (p, j) at b[p*rsb + j*csb] (row-major
+ * weights: rsb = n, csb = 1; weights stored [outputs, inputs]: rsb = 1, csb = k). b may be freed
+ * or changed once the stream has run the pack. precision: MFK_PRECISION_3XTF32 / _1XTF32, or
+ * DEFAULT for the library default at packing time. k == 0 or n == 0 gives an empty handle whose
+ * products are zeros (plus beta*C_in and bias). The handle is released by mfk_packed_b_free
+ * (device-synchronising; not while a product using it is in flight).
+ *
+ * mfk_gemm_prepacked_f32: the mfk_gemm_f32 product with B taken from the handle: desc->b, b_rs and
+ * b_cs are ignored; desc->k and desc->n must equal the handle's k and n, and the call must run
+ * on the handle's device. A 1xTF32 handle cannot serve a 3xTF32 product (MFK_ERR_INVALID_ARGUMENT);
+ * a 3xTF32 handle serves both. For 3xTF32 the result is bit-identical to mfk_gemm_f32 with the
+ * same B. */
+typedef struct mfk_packed_b mfk_packed_b;
+int mfk_pack_b_f32(const float* b, int64_t rsb, int64_t csb, int64_t k, int64_t n,
+                   int32_t precision, void* stream, mfk_packed_b** out);
+int mfk_packed_b_shape(const mfk_packed_b* packed, int64_t* k, int64_t* n, int32_t* precision);
+int mfk_packed_b_free(mfk_packed_b* packed);
+int mfk_gemm_prepacked_f32(const mfk_gemm_desc* desc, const mfk_packed_b* packed, void* stream);
+
 /* gemv: y = alpha * op(A) x + beta * y0 with A row-major [rows, cols] (row stride lda), op(A) = A
  * or its transpose, sums accumulated in double. Replaces the OpId::Gemv kernel (CPU adapter:
  * src/backends/cpu/backend.cpp:120-125 -> cpu::gemv_f32, src/backends/cpu/ops/blas/blas.cpp:66).

@@ -5,11 +5,13 @@ mirrors the reference's op API over torch CUDA tensors, ``sharded`` splits a GEM
 """
 from ._lib import MfkError, build  # noqa: F401
 from .ops import (  # noqa: F401
+    PackedB,
     attention,
     bias_add,
     device_status,
     gelu,
     gemm,
+    gemm_prepacked,
     gemm_strided_batched,
     gemv,
     get_default_precision,
@@ -17,6 +19,7 @@ from .ops import (  # noqa: F401
     log_softmax,
     matmul,
     matvec,
+    pack_b,
     relu,
     set_default_precision,
     softmax,
@@ -24,7 +27,8 @@ from .ops import (  # noqa: F401
 )
 
 __all__ = [
-    "MfkError", "build", "attention", "bias_add", "log_softmax", "softmax", "where", "device_status", "gelu", "gemm", "gemm_strided_batched",
-    "gemv", "get_default_precision", "linear", "matmul", "matvec", "relu",
-    "set_default_precision",
+    "MfkError", "PackedB", "build", "attention", "bias_add", "device_status", "gelu", "gemm",
+    "gemm_prepacked", "gemm_strided_batched", "gemv", "get_default_precision", "linear",
+    "log_softmax", "matmul", "matvec", "pack_b", "relu", "set_default_precision", "softmax",
+    "where",
 ]

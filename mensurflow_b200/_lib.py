@@ -31,6 +31,10 @@ EXPORTED = (
     "mfk_gemm_f32",
     "mfk_gemm_f32_noalloc",
     "mfk_gemm_strided_batched_f32",
+    "mfk_pack_b_f32",
+    "mfk_packed_b_shape",
+    "mfk_packed_b_free",
+    "mfk_gemm_prepacked_f32",
     "mfk_gemv_f32",
     "mfk_matvec_f32",
     "mfk_bias_act_f32",
@@ -106,6 +110,12 @@ def lib() -> ctypes.CDLL:
             so.mfk_gemm_f32_noalloc.argtypes = [ctypes.POINTER(GemmDesc), vp]
             so.mfk_gemm_strided_batched_f32.argtypes = [ctypes.POINTER(GemmDesc),
                                                         ctypes.POINTER(BatchDesc), vp]
+            so.mfk_pack_b_f32.argtypes = [vp, i64, i64, i64, i64, i32, vp,
+                                          ctypes.POINTER(ctypes.c_void_p)]
+            so.mfk_packed_b_shape.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64),
+                                              ctypes.POINTER(i32)]
+            so.mfk_packed_b_free.argtypes = [vp]
+            so.mfk_gemm_prepacked_f32.argtypes = [ctypes.POINTER(GemmDesc), vp, vp]
             so.mfk_gemv_f32.argtypes = [vp, i64, i64, i64, i32, vp, i64, f32, f32, vp, vp, vp]
             so.mfk_matvec_f32.argtypes = [vp, i64, i64, vp, vp, vp]
             so.mfk_bias_act_f32.argtypes = [vp, vp, vp, i64, i64, i32, vp]

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -18,6 +19,16 @@
 #include "gemm_tc.cuh"
 #include "prep.cuh"
 #include "simt.cuh"
+
+// A B operand split once (mfk_pack_b_f32): op(B) as K-major panels [n][kp] of tf32 values, hi
+// and (3xTF32) lo, in device memory the handle owns.
+struct mfk_packed_b {
+    float* hi = nullptr;
+    float* lo = nullptr;
+    int64_t k = 0, n = 0, kp = 0;
+    int32_t precision = MFK_PRECISION_3XTF32;
+    int device = 0;
+};
 
 namespace {
 
@@ -283,8 +294,53 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
     return MFK_OK;
 }
 
+// Writes op(X) of operand `o` as K-major panels [batch][rows][Kp] into o.hi (and o.lo for the
+// 3xTF32 split), zero in the columns k..Kp-1. o.dev_offsets must hold the per-matrix offsets on
+// the device when o.bl.offsets is set.
+int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode,
+                const DeviceInfo* info, cudaStream_t stream) {
+    if (o.cs == 1 && o.rs % 4 == 0 && k % 4 == 0 && aligned16(o.ptr) &&
+        (o.dev_offsets != nullptr || o.bl.stride % 4 == 0)) {
+        // already K-major and aligned: a straight vectorised pass
+        bool offs_aligned = true;
+        if (o.bl.offsets) {
+            for (int64_t i = 0; i < batch && offs_aligned; ++i) offs_aligned = o.bl.offsets[i] % 4 == 0;
+        }
+        if (offs_aligned) {
+            const int64_t total4 = o.rows * (Kp / 4) * batch;
+            const int64_t blocks = std::min<int64_t>((total4 + 255) / 256,
+                                                     static_cast<int64_t>(info->sm_count) * 16);
+            mfk::pack_kmajor_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                o.ptr, reinterpret_cast<const long long*>(o.dev_offsets), o.bl.stride, o.rs,
+                static_cast<int>(o.rows), static_cast<int>(k), static_cast<int>(Kp),
+                static_cast<int>(batch), o.hi, o.lo, mode);
+            g_launches.fetch_add(1);
+            MFK_CUDA(cudaGetLastError());
+            return MFK_OK;
+        }
+    }
+    const int p_contig = (o.cs == 1) || (o.rs != 1 && std::llabs(o.cs) <= std::llabs(o.rs));
+    if (o.rows > 65535LL * 32) return MFK_ERR_UNSUPPORTED;
+    for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
+        const int64_t nz = std::min<int64_t>(65535, batch - z0);
+        dim3 grid(static_cast<unsigned>(Kp / 32), static_cast<unsigned>((o.rows + 31) / 32),
+                  static_cast<unsigned>(nz));
+        const long long* offs =
+            o.dev_offsets ? reinterpret_cast<const long long*>(o.dev_offsets) + z0 : nullptr;
+        const float* src = o.dev_offsets ? o.ptr : o.ptr + z0 * o.bl.stride;
+        const int64_t out_shift = z0 * o.rows * Kp;
+        mfk::pack_kmajor_kernel<<<grid, dim3(32, 8), 0, stream>>>(
+            src, offs, o.bl.stride, o.rs, o.cs, static_cast<int>(o.rows),
+            static_cast<int>(k), static_cast<int>(Kp), o.hi + out_shift,
+            o.lo ? o.lo + out_shift : nullptr, mode, p_contig);
+        g_launches.fetch_add(1);
+        MFK_CUDA(cudaGetLastError());
+    }
+    return MFK_OK;
+}
+
 int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream,
-             const FixedScratch* fixed);
+             const FixedScratch* fixed, const mfk_packed_b* pb = nullptr);
 
 // Known answer: 1xTF32 reads A in place; a = 1 + 3*2^-12 holds 0.75 ulp of tf32 beyond 1, so
 // a * 1 is 1 when the tensor cores truncate fp32 operands and 1 + 2^-10 when they round. Runs
@@ -356,7 +412,7 @@ int check_desc(const mfk_gemm_desc* d) {
 }
 
 int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream,
-             const FixedScratch* fixed) {
+             const FixedScratch* fixed, const mfk_packed_b* pb) {
     int rc = check_desc(d);
     if (rc != MFK_OK) return rc;
     const int64_t batch = bd ? bd->batch : 1;
@@ -374,6 +430,11 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     const int precision = d->precision == MFK_PRECISION_DEFAULT ? g_default_precision.load()
                                                                  : d->precision;
     const bool split3 = precision == MFK_PRECISION_3XTF32;
+    if (pb != nullptr) {
+        if (pb->k != d->k || pb->n != d->n) return MFK_ERR_INVALID_ARGUMENT;
+        if (pb->device != dev) return MFK_ERR_INVALID_ARGUMENT;
+        if (split3 && pb->precision != MFK_PRECISION_3XTF32) return MFK_ERR_INVALID_ARGUMENT;
+    }
     // The in-kernel split of A may leave hi as the raw fp32 values where the tensor cores are
     // known to truncate them (writing only lo: a third less shared-memory traffic).
     const bool raw_hi = split3 && d->k > 0 && d->n > 128 && d->n <= kInKernelSplitMaxN &&
@@ -444,12 +505,14 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         }
     };
     direct_map(A, mfk::kBM, &ma0, &ma1, &g.a_batch_bcast);
-    direct_map(B, b_box_rows, &mb0, &mb1, &g.b_batch_bcast);
+    if (pb == nullptr) direct_map(B, b_box_rows, &mb0, &mb1, &g.b_batch_bcast);
 
     // Workspace: packed operands plus device copies of non-arithmetic offset tables.
     const int nops = split3 ? 2 : 1;
     auto packed_elems = [&](const Operand& o) { return o.rows * Kp * batch; };
-    auto copies = [&](const Operand& o) { return o.direct ? 0 : nops; };
+    auto copies = [&](const Operand& o) {
+        return (o.direct || (pb != nullptr && &o == &B)) ? 0 : nops;
+    };
     size_t bytes = 0;
     auto reserve = [&](size_t n) {
         const size_t off = bytes;
@@ -485,45 +548,8 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
             MFK_CUDA(cudaMemcpyAsync(o.dev_offsets, o.bl.offsets, sizeof(int64_t) * batch,
                                      cudaMemcpyHostToDevice, stream));
         }
-        const int mode = split3 ? mfk::kPackSplit : mfk::kPackRound;
-        if (o.cs == 1 && o.rs % 4 == 0 && d->k % 4 == 0 && aligned16(o.ptr) &&
-            (o.dev_offsets != nullptr || o.bl.stride % 4 == 0)) {
-            // already K-major and aligned: a straight vectorised pass
-            bool offs_aligned = true;
-            if (o.bl.offsets) {
-                for (int64_t i = 0; i < batch && offs_aligned; ++i) offs_aligned = o.bl.offsets[i] % 4 == 0;
-            }
-            if (offs_aligned) {
-                const int64_t total4 = o.rows * (Kp / 4) * batch;
-                const int64_t blocks = std::min<int64_t>((total4 + 255) / 256,
-                                                         static_cast<int64_t>(info->sm_count) * 16);
-                mfk::pack_kmajor_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-                    o.ptr, reinterpret_cast<const long long*>(o.dev_offsets), o.bl.stride, o.rs,
-                    static_cast<int>(o.rows), static_cast<int>(d->k), static_cast<int>(Kp),
-                    static_cast<int>(batch), o.hi, o.lo, mode);
-                g_launches.fetch_add(1);
-                MFK_CUDA(cudaGetLastError());
-                return MFK_OK;
-            }
-        }
-        const int p_contig = (o.cs == 1) || (o.rs != 1 && std::llabs(o.cs) <= std::llabs(o.rs));
-        if (o.rows > 65535LL * 32) return MFK_ERR_UNSUPPORTED;
-        for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
-            const int64_t nz = std::min<int64_t>(65535, batch - z0);
-            dim3 grid(static_cast<unsigned>(Kp / 32), static_cast<unsigned>((o.rows + 31) / 32),
-                      static_cast<unsigned>(nz));
-            const long long* offs =
-                o.dev_offsets ? reinterpret_cast<const long long*>(o.dev_offsets) + z0 : nullptr;
-            const float* src = o.dev_offsets ? o.ptr : o.ptr + z0 * o.bl.stride;
-            const int64_t out_shift = z0 * o.rows * Kp;
-            mfk::pack_kmajor_kernel<<<grid, dim3(32, 8), 0, stream>>>(
-                src, offs, o.bl.stride, o.rs, o.cs, static_cast<int>(o.rows),
-                static_cast<int>(d->k), static_cast<int>(Kp), o.hi + out_shift,
-                o.lo ? o.lo + out_shift : nullptr, mode, p_contig);
-            g_launches.fetch_add(1);
-            MFK_CUDA(cudaGetLastError());
-        }
-        return MFK_OK;
+        return launch_pack(o, d->k, Kp, batch, split3 ? mfk::kPackSplit : mfk::kPackRound,
+                           info, stream);
     };
     if (copies(A) && (rc = pack(A, a_off, ao_off)) != MFK_OK) return rc;
     if (copies(B) && (rc = pack(B, b_off, bo_off)) != MFK_OK) return rc;
@@ -541,6 +567,22 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
         (copies(B) && !packed_maps(B, b_box_rows, &mb0, &mb1))) {
         t_cuda_error = "cuTensorMapEncodeTiled rejected a packed operand";
         return MFK_ERR_UNSUPPORTED;
+    }
+    if (pb != nullptr) {
+        // the pre-split B, one matrix shared by every batch entry
+        bool ok = make_kmajor_map(&mb0, pb->hi, pb->kp, pb->n, 1, pb->kp, pb->n * pb->kp,
+                                  b_box_rows);
+        if (split3) {
+            ok = ok && make_kmajor_map(&mb1, pb->lo, pb->kp, pb->n, 1, pb->kp, pb->n * pb->kp,
+                                       b_box_rows);
+        } else {
+            mb1 = mb0;
+        }
+        if (!ok) {
+            t_cuda_error = "cuTensorMapEncodeTiled rejected a pre-split B";
+            return MFK_ERR_UNSUPPORTED;
+        }
+        g.b_batch_bcast = batch > 1 ? 1 : 0;
     }
 
     g.num_kb = static_cast<int>(Kp / mfk::kBK);
@@ -611,6 +653,86 @@ int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc
                                  void* stream) {
     if (batch == nullptr) return MFK_ERR_INVALID_ARGUMENT;
     return run_gemm(desc, batch, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int mfk_pack_b_f32(const float* b, int64_t rsb, int64_t csb, int64_t k, int64_t n,
+                   int32_t precision, void* stream_, mfk_packed_b** out) {
+    if (out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (k < 0 || n < 0 || precision < MFK_PRECISION_DEFAULT || precision > MFK_PRECISION_1XTF32)
+        return MFK_ERR_INVALID_ARGUMENT;
+    if (k > 0 && n > 0 && b == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    if (k > (int64_t(1) << 31) - 256 || n > (int64_t(1) << 31) - 256) return MFK_ERR_UNSUPPORTED;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    auto* p = new (std::nothrow) mfk_packed_b;
+    if (p == nullptr) return MFK_ERR_OUT_OF_MEMORY;
+    p->k = k;
+    p->n = n;
+    p->kp = (k + mfk::kBK - 1) / mfk::kBK * mfk::kBK;
+    p->precision = precision == MFK_PRECISION_DEFAULT ? g_default_precision.load() : precision;
+    p->device = dev;
+    if (k > 0 && n > 0) {
+        const bool split3 = p->precision == MFK_PRECISION_3XTF32;
+        const size_t elems = static_cast<size_t>(n) * static_cast<size_t>(p->kp);
+        if (cudaMalloc(reinterpret_cast<void**>(&p->hi), sizeof(float) * elems * (split3 ? 2 : 1)) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            delete p;
+            return MFK_ERR_OUT_OF_MEMORY;
+        }
+        p->lo = split3 ? p->hi + elems : nullptr;
+        // op(B) element (p, j) at p*rsb + j*csb: K-major rows over j, row stride csb, depth rsb
+        Operand o{b, csb, rsb, n, BatchLayout{}};
+        o.hi = p->hi;
+        o.lo = p->lo;
+        rc = launch_pack(o, k, p->kp, 1, split3 ? mfk::kPackSplit : mfk::kPackRound, info, stream);
+        if (rc != MFK_OK) {
+            cudaFree(p->hi);
+            delete p;
+            return rc;
+        }
+    }
+    *out = p;
+    return MFK_OK;
+}
+
+int mfk_packed_b_shape(const mfk_packed_b* packed, int64_t* k, int64_t* n, int32_t* precision) {
+    if (packed == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    if (k) *k = packed->k;
+    if (n) *n = packed->n;
+    if (precision) *precision = packed->precision;
+    return MFK_OK;
+}
+
+int mfk_packed_b_free(mfk_packed_b* packed) {
+    if (packed == nullptr) return MFK_OK;
+    int rc = MFK_OK;
+    if (packed->hi != nullptr) {
+        int cur = 0;
+        const bool switch_dev = cudaGetDevice(&cur) == cudaSuccess && cur != packed->device;
+        if (switch_dev) cudaSetDevice(packed->device);
+        if (cudaFree(packed->hi) != cudaSuccess) rc = MFK_ERR_CUDA;
+        if (switch_dev) cudaSetDevice(cur);
+        cudaGetLastError();
+    }
+    delete packed;
+    return rc;
+}
+
+int mfk_gemm_prepacked_f32(const mfk_gemm_desc* desc, const mfk_packed_b* packed, void* stream) {
+    if (desc == nullptr || packed == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    mfk_gemm_desc d = *desc;
+    d.b = packed->hi != nullptr ? packed->hi : desc->a;  // B is read from the handle
+    d.b_rs = 1;
+    d.b_cs = 1;
+    if (packed->hi == nullptr) d.k = 0;                      // an empty B: the product is zero
+    if (d.n != packed->n || desc->k != packed->k) return MFK_ERR_INVALID_ARGUMENT;
+    return run_gemm(&d, nullptr, static_cast<cudaStream_t>(stream), nullptr,
+                    packed->hi != nullptr ? packed : nullptr);
 }
 
 int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_t transpose,

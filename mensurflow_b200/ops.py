@@ -201,6 +201,123 @@ def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch
     return out
 
 
+class PackedB:
+    """B split once for many products: the device analogue of the reference's cpu::PackedB
+    (src/backends/cpu/ops/gemm/gemm_packed.hpp:147-191). Holds op(B) as K-major tf32 panels —
+    (hi, lo) for 3xTF32, rounded values for 1xTF32 — in device memory it owns; `gemm_prepacked`
+    and `linear` use it in place of B and skip B's split pass. Build it with `pack_b`."""
+
+    def __init__(self, handle: int, k: int, n: int, precision: int, device: torch.device):
+        self._handle = handle
+        self._k, self._n = k, n
+        self._precision = precision
+        self.device = device
+
+    def depth(self) -> int:
+        """k: rows of B."""
+        return self._k
+
+    def cols(self) -> int:
+        """n: columns of B."""
+        return self._n
+
+    @property
+    def precision(self) -> str:
+        return "3xtf32" if self._precision == _lib.PRECISION_3XTF32 else "1xtf32"
+
+    def empty(self) -> bool:
+        """True when it holds no values: B had no rows or columns, or the object was freed."""
+        return self._handle is None or self._k == 0 or self._n == 0
+
+    def free(self) -> None:
+        """Releases the device copy now (device-synchronising), leaving an empty object."""
+        if self._handle is not None:
+            h, self._handle = self._handle, None
+            self._k = self._n = 0
+            check(_lib.lib().mfk_packed_b_free(h), "PackedB.free")
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:  # interpreter shutdown: the driver reclaims the memory
+            pass
+
+
+def pack_b(b: torch.Tensor, *, transpose: bool = False,
+           precision: Optional[str] = None) -> PackedB:
+    """Split B [k, n] (or, with `transpose`, the weights stored [n, k]) once, as pack_b_f32
+    (gemm_packed.hpp:188): any strides; `b` may be freed or changed afterwards. The precision is
+    fixed at packing time (None: the library default then); a 3xTF32 pack serves both
+    precisions, a 1xTF32 pack only 1xTF32."""
+    _require(b, "pack_b", "b", 2)
+    _kernel_for("pack_b", b)
+    op_b = b.t() if transpose else b
+    k, n = op_b.shape
+    handle = ctypes.c_void_p()
+    check(_lib.lib().mfk_pack_b_f32(_ptr(op_b) if op_b.numel() else None, op_b.stride(0),
+                                    op_b.stride(1), k, n, _PRECISIONS[precision], _stream(),
+                                    ctypes.byref(handle)), "pack_b")
+    prec = ctypes.c_int32()
+    check(_lib.lib().mfk_packed_b_shape(handle, None, None, ctypes.byref(prec)), "pack_b")
+    return PackedB(handle.value, k, n, prec.value, b.device)
+
+
+def gemm_prepacked(a: torch.Tensor, packed: PackedB, alpha: float = 1.0,
+                   c: Optional[torch.Tensor] = None, beta: float = 0.0,
+                   transpose_a: bool = False, *, bias: Optional[torch.Tensor] = None,
+                   activation: Optional[str] = None, precision: Optional[str] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """gemm with a pre-split B: act(alpha * op(a) @ B + beta * c + bias), as
+    matmul_f32_prepacked (gemm_packed.hpp:191) plus gemm's epilogue. `precision` None means the
+    pack's own precision."""
+    if not isinstance(packed, PackedB):
+        raise TypeError("gemm_prepacked: packed must come from pack_b")
+    _require(a, "gemm_prepacked", "a", 2)
+    if c is not None:
+        _require(c, "gemm_prepacked", "c")
+    _same("gemm_prepacked", a, c, bias)
+    _kernel_for("gemm_prepacked", a)
+    if packed.device != a.device:
+        raise ValueError("gemm_prepacked: the pack lives on another device")
+    if packed._handle is None:
+        raise ValueError("gemm_prepacked: the pack was freed")
+    left = a.t() if transpose_a else a
+    m, k = left.shape
+    n = packed.cols()
+    if k != packed.depth():
+        raise ValueError(f"gemm_prepacked: inner dimensions differ ({tuple(left.shape)} times "
+                         f"[{packed.depth()}, {n}])")
+    if c is not None and tuple(c.shape) != (m, n):
+        raise ValueError("gemm_prepacked: c shape does not match result")
+    if c is None and beta != 0.0:
+        raise ValueError("gemm_prepacked: beta requires c")
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != n):
+        raise ValueError(f"gemm_prepacked: bias must be [{n}], got {tuple(bias.shape)}")
+    if activation not in _ACTS:
+        raise ValueError(f"gemm_prepacked: unknown activation {activation!r}")
+    if bias is not None:
+        bias = bias.contiguous()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    elif tuple(out.shape) != (m, n) or out.stride(1) != 1:
+        raise ValueError("gemm_prepacked: out must be [m, n] with unit column stride")
+    if m == 0 or n == 0:
+        return out
+    d = GemmDesc()
+    d.a, d.a_rs, d.a_cs = _ptr(left), left.stride(0), left.stride(1)
+    if c is not None and beta != 0.0:
+        d.c_in, d.c_in_rs, d.c_in_cs = _ptr(c), c.stride(0), c.stride(1)
+    d.c, d.ldc = _ptr(out), out.stride(0)
+    d.m, d.n, d.k = m, n, k
+    d.alpha, d.beta = float(alpha), float(beta)
+    d.bias = _ptr(bias)
+    d.activation = _ACTS[activation]
+    d.precision = (packed._precision if precision is None else _PRECISIONS[precision])
+    check(_lib.lib().mfk_gemm_prepacked_f32(ctypes.byref(d), packed._handle, _stream()),
+          "gemm_prepacked")
+    return out
+
+
 def matmul(a: torch.Tensor, b: torch.Tensor, *, precision: Optional[str] = None) -> torch.Tensor:
     """[M,K] @ [K,N] as mensurflow::matmul (blas.hpp:55, blas.cpp:186-232)."""
     _require(a, "matmul", "a", 2)
@@ -212,10 +329,15 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, precision: Optional[str] = None)
     return gemm(a, b, precision=precision)
 
 
-def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+def linear(x: torch.Tensor, w, bias: Optional[torch.Tensor] = None,
            activation: Optional[str] = None, *, transpose_w: bool = False,
            precision: Optional[str] = None) -> torch.Tensor:
-    """act(x @ op(w) + bias) in one kernel: the fused form of matmul + bias_add (+ relu/gelu)."""
+    """act(x @ op(w) + bias) in one kernel: the fused form of matmul + bias_add (+ relu/gelu).
+    `w` may be a PackedB (weights split once by `pack_b`)."""
+    if isinstance(w, PackedB):
+        if transpose_w:
+            raise ValueError("linear: a PackedB already holds op(w); pack with transpose=True")
+        return gemm_prepacked(x, w, bias=bias, activation=activation, precision=precision)
     return gemm(x, w, transpose_b=transpose_w, bias=bias, activation=activation,
                 precision=precision)
 
