@@ -180,6 +180,13 @@ int mfk_matvec_f32(const float* a, int64_t m, int64_t k, const float* x, float* 
 int mfk_bias_act_f32(const float* x, const float* bias, float* out, int64_t rows, int64_t cols,
                      int32_t activation, void* stream);
 
+/* The bias gradient of bias_add: dbias[j] = sum over rows of grad[r*ld + j], accumulated in
+ * fp32 in row order from 0 — bit-identical to the reference's backward closure, which runs this
+ * loop on the host after copying the gradient back (src/ops/elementwise.cpp:263-283). grad is
+ * rows x cols (row stride ld >= cols); rows == 0 gives zeros. */
+int mfk_bias_grad_f32(const float* grad, int64_t rows, int64_t cols, int64_t ld, float* dbias,
+                      void* stream);
+
 /* softmax (log_softmax when `log` != 0) along the middle axis of a contiguous [outer, length,
  * inner] tensor: max (NaN poisons the line), exp in fp32, sum in double, multiply by 1/sum; an
  * all -inf line gives zeros (-inf for log_softmax). Replaces the OpId::Softmax / LogSoftmax kernels

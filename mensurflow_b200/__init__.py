@@ -8,6 +8,7 @@ from .ops import (  # noqa: F401
     PackedB,
     attention,
     bias_add,
+    bias_grad,
     device_status,
     gelu,
     gemm,
@@ -16,8 +17,10 @@ from .ops import (  # noqa: F401
     gemv,
     get_default_precision,
     linear,
+    linear_backward,
     log_softmax,
     matmul,
+    matmul_backward,
     matvec,
     pack_b,
     relu,
@@ -27,8 +30,8 @@ from .ops import (  # noqa: F401
 )
 
 __all__ = [
-    "MfkError", "PackedB", "build", "attention", "bias_add", "device_status", "gelu", "gemm",
-    "gemm_prepacked", "gemm_strided_batched", "gemv", "get_default_precision", "linear",
-    "log_softmax", "matmul", "matvec", "pack_b", "relu", "set_default_precision", "softmax",
-    "where",
+    "MfkError", "PackedB", "build", "attention", "bias_add", "bias_grad", "device_status",
+    "gelu", "gemm", "gemm_prepacked", "gemm_strided_batched", "gemv", "get_default_precision",
+    "linear", "linear_backward", "log_softmax", "matmul", "matmul_backward", "matvec", "pack_b",
+    "relu", "set_default_precision", "softmax", "where",
 ]

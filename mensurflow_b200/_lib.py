@@ -38,6 +38,7 @@ EXPORTED = (
     "mfk_gemv_f32",
     "mfk_matvec_f32",
     "mfk_bias_act_f32",
+    "mfk_bias_grad_f32",
     "mfk_softmax_f32",
     "mfk_masked_softmax_f32",
     "mfk_where_f32",
@@ -119,6 +120,7 @@ def lib() -> ctypes.CDLL:
             so.mfk_gemv_f32.argtypes = [vp, i64, i64, i64, i32, vp, i64, f32, f32, vp, vp, vp]
             so.mfk_matvec_f32.argtypes = [vp, i64, i64, vp, vp, vp]
             so.mfk_bias_act_f32.argtypes = [vp, vp, vp, i64, i64, i32, vp]
+            so.mfk_bias_grad_f32.argtypes = [vp, i64, i64, i64, vp, vp]
             so.mfk_softmax_f32.argtypes = [vp, vp, i64, i64, i64, i32, vp]
             so.mfk_masked_softmax_f32.argtypes = [vp, vp, i64, i64, i32, vp, i64, i64, i64, vp]
             so.mfk_where_f32.argtypes = [vp, vp, vp, vp, i64, vp]

@@ -824,6 +824,25 @@ int mfk_bias_act_f32(const float* x, const float* bias, float* out, int64_t rows
     return MFK_OK;
 }
 
+int mfk_bias_grad_f32(const float* grad, int64_t rows, int64_t cols, int64_t ld, float* dbias,
+                      void* stream_) {
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (rows < 0 || cols < 0 || (rows > 0 && ld < cols)) return MFK_ERR_INVALID_ARGUMENT;
+    if (cols == 0) return MFK_OK;
+    if (dbias == nullptr || (rows > 0 && grad == nullptr)) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    const int64_t blocks = (cols + mfk::kBgCols - 1) / mfk::kBgCols;
+    if (blocks > INT32_MAX) return MFK_ERR_UNSUPPORTED;
+    g_launches.fetch_add(1);
+    mfk::bias_grad_kernel<<<static_cast<unsigned>(blocks), mfk::kBgThreads, 0, stream>>>(
+        grad, rows, cols, ld, dbias);
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
 }  // extern "C"
 
 namespace {

@@ -297,3 +297,71 @@ __global__ void __launch_bounds__(256) where_kernel(const unsigned char* __restr
 }
 
 }  // namespace mfk
+
+// ---- bias_add backward: the bias gradient ----------------------------------------------------
+//
+// out[j] = sum over rows r of g[r*ld + j], accumulated in fp32 in row order from 0 — the
+// reference's loop (src/ops/elementwise.cpp:263-283, on the host there), so the result is
+// identical bit for bit. The order leaves one sequential chain per column; the kernel gives each
+// block 32 columns, stages 128-row tiles of them through a 3-deep cp.async ring (all 256 threads
+// load, a warp reads one 128-byte row segment per instruction) and lets warp 0 run the 32
+// chains out of shared memory, so HBM latency hides behind the ring rather than the chains.
+namespace mfk {
+
+constexpr int kBgCols = 32;
+constexpr int kBgRows = 128;
+constexpr int kBgStages = 3;
+constexpr int kBgThreads = 256;
+
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const float* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(kBgThreads) bias_grad_kernel(const float* __restrict__ g,
+                                                               long long rows, long long cols,
+                                                               long long ld,
+                                                               float* __restrict__ out) {
+    __shared__ float tile[kBgStages][kBgRows][kBgCols];  // 48 KB
+    const int lane = threadIdx.x % 32;
+    const int warp = threadIdx.x / 32;
+    const long long col = static_cast<long long>(blockIdx.x) * kBgCols + lane;
+    const bool col_ok = col < cols;
+    const long long ntiles = (rows + kBgRows - 1) / kBgRows;
+    auto load = [&](long long t) {
+        const int buf = static_cast<int>(t % kBgStages);
+        const long long r0 = t * kBgRows;
+#pragma unroll
+        for (int i = 0; i < kBgRows / (kBgThreads / 32); ++i) {
+            const int r = warp + (kBgThreads / 32) * i;
+            if (col_ok && r0 + r < rows) {
+                cp_async_4(static_cast<uint32_t>(__cvta_generic_to_shared(&tile[buf][r][lane])),
+                           g + (r0 + r) * ld + col);
+            }
+        }
+        cp_async_commit();  // one group per tile, empty or not, so the wait counts line up
+    };
+    for (long long t = 0; t < kBgStages - 1; ++t) load(t);
+    float acc = 0.0f;
+    for (long long t = 0; t < ntiles; ++t) {
+        load(t + kBgStages - 1);           // past the last tile: an empty group
+        cp_async_wait<kBgStages - 1>();    // tile t has landed (this thread's copies)
+        __syncthreads();                   // ... and every thread's
+        if (warp == 0 && col_ok) {
+            const int buf = static_cast<int>(t % kBgStages);
+            const long long left = rows - t * kBgRows;
+            const int nr = left < kBgRows ? static_cast<int>(left) : kBgRows;
+            for (int r = 0; r < nr; ++r) acc += tile[buf][r][lane];
+        }
+        __syncthreads();                   // the buffer is free before it is refilled
+    }
+    if (warp == 0 && col_ok) out[col] = acc;
+}
+
+}  // namespace mfk

@@ -342,6 +342,54 @@ def linear(x: torch.Tensor, w, bias: Optional[torch.Tensor] = None,
                 precision=precision)
 
 
+def bias_grad(grad: torch.Tensor) -> torch.Tensor:
+    """The bias gradient of bias_add: column sums of `grad` [batch, features] over the rows,
+    accumulated in fp32 in row order — bit-identical to the reference's backward closure
+    (src/ops/elementwise.cpp:263-283), which runs this loop on the host; here one device kernel."""
+    _require(grad, "bias_grad", "grad", 2)
+    _kernel_for("bias_grad", grad)
+    rows, cols = grad.shape
+    g = grad if grad.stride(1) == 1 and (rows <= 1 or grad.stride(0) >= cols) else grad.contiguous()
+    out = torch.empty(cols, dtype=torch.float32, device=grad.device)
+    ld = g.stride(0) if rows > 1 else cols
+    check(_lib.lib().mfk_bias_grad_f32(_ptr(g) if g.numel() else None, rows, cols, ld,
+                                       _ptr(out) if cols else None, _stream()), "bias_grad")
+    return out
+
+
+def matmul_backward(grad: torch.Tensor, a: torch.Tensor, b: torch.Tensor, *,
+                    need_a: bool = True, need_b: bool = True,
+                    precision: Optional[str] = None):
+    """(dA, dB) for C = A @ B: dA = grad @ B^T and dB = A^T @ grad, the products matmul's recorded
+    backward makes (src/ops/blas.cpp:220-230). The transposes are stride swaps read in place by
+    the same tensor-core GEMM (the reference's op layer copies non-contiguous CUDA views through
+    the host first, tensor.cpp:224-229). A gradient that is not needed is None."""
+    _require(grad, "matmul_backward", "grad", 2)
+    _require(a, "matmul_backward", "a", 2)
+    _require(b, "matmul_backward", "b", 2)
+    _same("matmul_backward", grad, a, b)
+    m, k = a.shape
+    if b.shape[0] != k or tuple(grad.shape) != (m, b.shape[1]):
+        raise ValueError(f"matmul_backward: shapes {tuple(grad.shape)}, {tuple(a.shape)}, "
+                         f"{tuple(b.shape)} do not form C = A @ B")
+    da = gemm(grad, b, transpose_b=True, precision=precision) if need_a else None
+    db = gemm(a, grad, transpose_a=True, precision=precision) if need_b else None
+    return da, db
+
+
+def linear_backward(grad: torch.Tensor, x: torch.Tensor, w: torch.Tensor, *,
+                    has_bias: bool = True, transpose_w: bool = False,
+                    precision: Optional[str] = None):
+    """(dx, dw, dbias) for y = x @ op(w) + bias (no activation): the matmul backward products and
+    the bias reduction; dw has w's own layout ([n, k] when transpose_w). dbias is None without a
+    bias."""
+    w_op = w.t() if transpose_w else w
+    dx, dw = matmul_backward(grad, x, w_op, need_b=not transpose_w, precision=precision)
+    if transpose_w:
+        dw = gemm(grad, x, transpose_a=True, precision=precision)   # (x^T grad)^T = grad^T x
+    return dx, dw, (bias_grad(grad) if has_bias else None)
+
+
 def _broadcast_shapes(op: str, x: Sequence[int], y: Sequence[int]):
     try:
         return tuple(torch.broadcast_shapes(tuple(x), tuple(y)))

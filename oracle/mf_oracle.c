@@ -163,6 +163,15 @@ void mfo_bias_add(const float* x, const float* bias, float* out, int64_t rows, i
         for (int64_t j = 0; j < cols; ++j) out[r * cols + j] = x[r * cols + j] + bias[j];
 }
 
+/* bias_add's backward for the bias (src/ops/elementwise.cpp:263-283): reduced[j] is the sum
+ * of the upstream gradient's column j over the rows, accumulated in float in row order from 0.
+ * g is rows x cols with row stride ld. */
+void mfo_bias_grad(const float* g, int64_t rows, int64_t cols, int64_t ld, float* out) {
+    for (int64_t j = 0; j < cols; ++j) out[j] = 0.0f;
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t j = 0; j < cols; ++j) out[j] += g[r * ld + j];
+}
+
 /* relu_f32, elementwise.cpp relu: x < 0 ? 0 : x (NaN passes through). */
 void mfo_relu(const float* x, float* out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] = x[i] < 0.0f ? 0.0f : x[i];

@@ -66,6 +66,7 @@ def lib():
                 _ptr, _ptr, _i64, _i64, _ptr, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64,
             ]
             so.mfo_bias_add.argtypes = [_ptr, _ptr, _ptr, _i64, _i64]
+            so.mfo_bias_grad.argtypes = [_ptr, _i64, _i64, _i64, _ptr]
             so.mfo_relu.argtypes = [_ptr, _ptr, _i64]
             so.mfo_gelu.argtypes = [_ptr, _ptr, _i64, ctypes.c_int]
             so.mfo_gemv.argtypes = [_ptr, _i64, _i64, _i64, _ptr, _f32, _f32, _ptr, _ptr, ctypes.c_int]
@@ -94,6 +95,9 @@ def reference():
                     _f32, _f32, ctypes.c_int, ctypes.c_int, _ptr, _ptr, _ptr,
                 ]
                 so.mfref_bias_add.argtypes = [_ptr, _i64, _i64, _ptr, _ptr]
+                so.mfref_bias_add_backward.argtypes = [_ptr, _i64, _i64, _ptr]
+                so.mfref_matmul_backward.argtypes = [_ptr, _ptr, _ptr, _i64, _i64, _i64, _ptr,
+                                                     _ptr]
                 so.mfref_gelu.argtypes = [_ptr, _i64, ctypes.c_int, _ptr]
                 so.mfref_relu.argtypes = [_ptr, _i64, _ptr]
                 so.mfref_gemv.argtypes = [_ptr, _i64, _i64, _ptr, _f32, _ptr, _f32, ctypes.c_int, _ptr]
@@ -203,6 +207,21 @@ def bias_add(x, bias):
     out = np.empty_like(x)
     lib().mfo_bias_add(_p(x), _p(bias), _p(out), x.shape[0], x.shape[1])
     return out
+
+
+def bias_grad(g):
+    """The bias gradient of bias_add: column sums of g in row order, in float
+    (mf_oracle.c mfo_bias_grad; src/ops/elementwise.cpp:263-283)."""
+    g = np.ascontiguousarray(g, np.float32)
+    out = np.empty(g.shape[1], np.float32)
+    lib().mfo_bias_grad(_p(g), g.shape[0], g.shape[1], g.shape[1], _p(out))
+    return out
+
+
+def matmul_backward(a, b, g):
+    """(dA, dB) = (g @ b^T, a^T @ g), the products matmul's recorded backward makes
+    (src/ops/blas.cpp:220-230), with the restated GEMM."""
+    return gemm(g, b, transpose_b=True), gemm(a, g, transpose_a=True)
 
 
 def activation(x, act):
@@ -334,6 +353,25 @@ def ref_bias_add(x, bias):
     _check_ref(reference().mfref_bias_add(_p(x), x.shape[0], x.shape[1],
                                           _p(np.ascontiguousarray(bias, np.float32)), _p(out)))
     return out
+
+
+def ref_bias_add_backward(g):
+    g = np.ascontiguousarray(g, np.float32)
+    out = np.empty(g.shape[1], np.float32)
+    _check_ref(reference().mfref_bias_add_backward(_p(g), g.shape[0], g.shape[1], _p(out)))
+    return out
+
+
+def ref_matmul_backward(a, b, g):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    g = np.ascontiguousarray(g, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    da = np.empty((m, k), np.float32)
+    db = np.empty((k, n), np.float32)
+    _check_ref(reference().mfref_matmul_backward(_p(a), _p(b), _p(g), m, k, n, _p(da), _p(db)))
+    return da, db
 
 
 def ref_gelu(x, approximate=False):

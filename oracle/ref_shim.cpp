@@ -8,6 +8,7 @@
 //   gemm_strided_batched  include/mensurflow/ops/blas.hpp:75   (src/ops/blas.cpp:297-394)
 //   gemv / matvec         include/mensurflow/ops/blas.hpp:35,40 (src/ops/blas.cpp:119-183)
 //   bias_add / relu/gelu  include/mensurflow/ops/elementwise.hpp:43,56,62
+//   backward of bias_add and matmul, through the reference's autograd (Tensor::backward)
 //   uniform / normal      include/mensurflow/ops/random.hpp:20,25
 // Used by tests/golden/make_golden.py (fixtures), by tests that pin the C restatement in
 // oracle/mf_oracle.c against the reference, and by bench.py's CPU-baseline and reference arms.
@@ -136,6 +137,39 @@ int mfref_bias_add(const float* x, std::int64_t rows, std::int64_t cols, const f
     return guarded([&] {
         copy_out(bias_add(host_tensor(x, {rows, cols}), host_tensor(bias, {cols}), Execution::CPU),
                  out);
+    });
+}
+
+// The reference's own backward passes, driven through its autograd: loss = sum(out * g) has
+// d loss / d out = g exactly (mul's backward multiplies the ones from sum by g), so the leaves'
+// gradients are what bias_add's and matmul's recorded backward closures compute from g
+// (src/ops/elementwise.cpp:263-283; src/ops/blas.cpp:220-230).
+int mfref_bias_add_backward(const float* g, std::int64_t rows, std::int64_t cols, float* dbias) {
+    return guarded([&] {
+        Tensor x = Tensor::zeros({rows, cols}, DType::F32, Device{});
+        Tensor bias = Tensor::zeros({cols}, DType::F32, Device{});
+        bias.set_requires_grad(true);
+        Tensor loss = sum(mul(bias_add(x, bias, Execution::CPU), host_tensor(g, {rows, cols}),
+                              Execution::CPU),
+                          Execution::CPU);
+        loss.backward();
+        copy_out(bias.grad(), dbias);
+    });
+}
+
+int mfref_matmul_backward(const float* a, const float* b, const float* g, std::int64_t m,
+                          std::int64_t k, std::int64_t n, float* da, float* db) {
+    return guarded([&] {
+        Tensor ta = host_tensor(a, {m, k});
+        Tensor tb = host_tensor(b, {k, n});
+        ta.set_requires_grad(true);
+        tb.set_requires_grad(true);
+        Tensor loss = sum(mul(matmul(ta, tb, Execution::CPU), host_tensor(g, {m, n}),
+                              Execution::CPU),
+                          Execution::CPU);
+        loss.backward();
+        copy_out(ta.grad(), da);
+        copy_out(tb.grad(), db);
     });
 }
 

@@ -62,6 +62,11 @@ MATMUL_SHAPES = [(1, 1, 1), (1, 5, 1), (5, 1, 3), (3, 5, 7), (16, 16, 16), (17, 
                  (1000, 2, 3), (257, 129, 257)]
 
 
+# (rows, features) of the bias gradients and (m, k, n) of the matmul backward cases
+BIAS_GRAD_SHAPES = [(333, 77), (1, 7), (1000, 1), (4096, 1024), (2, 3000)]
+MATMUL_BWD_SHAPES = [(50, 40, 30), (129, 257, 65)]
+
+
 def prod(shape):
     return int(np.prod(shape)) if len(shape) else 1
 
@@ -163,6 +168,22 @@ def main():
     v2 = O.ref_normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 28, 0).reshape(4, lq2, 32)
     att["attention_causal_64"] = O.ref_attention(q2, k2, v2, None, True)
     np.savez_compressed(os.path.join(HERE, "attention_cases.npz"), **att)
+
+    # the backward closures of bias_add (src/ops/elementwise.cpp:263-283) and matmul
+    # (src/ops/blas.cpp:220-230), run through the reference's autograd on Philox inputs
+    # regenerated by the tests (backward_inputs in tests/helpers.py)
+    bwd = {}
+    for i, (rows, cols) in enumerate(BIAS_GRAD_SHAPES):
+        g = O.ref_normal(rows * cols, 0, 1, 40 + i, 0).reshape(rows, cols)
+        bwd[f"bias_grad_{rows}x{cols}"] = O.ref_bias_add_backward(g)
+    for i, (m, k, n) in enumerate(MATMUL_BWD_SHAPES):
+        a = O.ref_normal(m * k, 0, 1, 60 + i, 0).reshape(m, k)
+        b = O.ref_normal(k * n, 0, 1, 60 + i, m * k).reshape(k, n)
+        g = O.ref_normal(m * n, 0, 1, 60 + i, m * k + k * n).reshape(m, n)
+        da, db = O.ref_matmul_backward(a, b, g)
+        bwd[f"matmul_{m}x{k}x{n}_da"] = da
+        bwd[f"matmul_{m}x{k}x{n}_db"] = db
+    np.savez_compressed(os.path.join(HERE, "backward_cases.npz"), **bwd)
     print("wrote", sorted(os.listdir(HERE)))
 
 

@@ -105,3 +105,19 @@ def attention_inputs():
     d["k2"] = O.normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 27, 0).reshape(4, lq2, 32)
     d["v2"] = O.normal(4 * lq2 * 32, 0, 1 / np.sqrt(32), 28, 0).reshape(4, lq2, 32)
     return d
+
+
+def backward_inputs():
+    """Inputs of tests/golden/backward_cases.npz, regenerated with the oracle's Philox."""
+    import sys
+    sys.path.insert(0, GOLDEN)
+    from make_golden import BIAS_GRAD_SHAPES, MATMUL_BWD_SHAPES
+    d = {}
+    for i, (rows, cols) in enumerate(BIAS_GRAD_SHAPES):
+        d[f"bias_grad_{rows}x{cols}"] = O.normal(rows * cols, 0, 1, 40 + i, 0).reshape(rows, cols)
+    for i, (m, k, n) in enumerate(MATMUL_BWD_SHAPES):
+        d[f"matmul_{m}x{k}x{n}"] = (
+            O.normal(m * k, 0, 1, 60 + i, 0).reshape(m, k),
+            O.normal(k * n, 0, 1, 60 + i, m * k).reshape(k, n),
+            O.normal(m * n, 0, 1, 60 + i, m * k + k * n).reshape(m, n))
+    return d

@@ -132,3 +132,31 @@ def test_softmax_and_attention_restatements_match_reference():
                                rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(O.attention(a["q2"], a["k2"], a["v2"], None, True),
                                g["attention_causal_64"], rtol=1e-5, atol=1e-6)
+
+
+def test_backward_restatements_match_golden():
+    """bias_add's bias gradient (row-order float sums) and matmul's backward products, restated,
+    equal the reference's autograd results bit for bit (tests/golden/backward_cases.npz)."""
+    from helpers import backward_inputs
+
+    g = golden("backward_cases.npz")
+    inp = backward_inputs()
+    for name, arr in inp.items():
+        if name.startswith("bias_grad"):
+            np.testing.assert_array_equal(O.bias_grad(arr), g[name], err_msg=name)
+        else:
+            a, b, grad = arr
+            da, db = O.matmul_backward(a, b, grad)
+            np.testing.assert_array_equal(da, g[name + "_da"], err_msg=name)
+            np.testing.assert_array_equal(db, g[name + "_db"], err_msg=name)
+
+
+@pytest.mark.skipif(O.reference() is None, reason="reference library not built here")
+def test_bias_grad_restatement_on_ragged_and_empty_shapes():
+    rng = np.random.default_rng(11)
+    for rows, cols in [(7, 1), (129, 33), (5000, 3)]:
+        x = rng.standard_normal((rows, cols)).astype(np.float32) * 100
+        np.testing.assert_array_equal(O.bias_grad(x), O.ref_bias_add_backward(x),
+                                      err_msg=f"{rows}x{cols}")
+    # no rows: the loop adds nothing (the reference records no graph for an empty input)
+    np.testing.assert_array_equal(O.bias_grad(np.zeros((0, 5), np.float32)), np.zeros(5))
