@@ -44,7 +44,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--precision", choices=["3xtf32", "1xtf32"], default="3xtf32")
     p.add_argument("--impl", choices=["mine", "reference"], default="mine")
-    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "gemv"], default="c2")
+    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "gemv", "copy"], default="c2")
     p.add_argument("--prepacked", action="store_true",
                    help="c3: W1 and W2 split once before the timed region (pack_b), as the "
                         "reference's PackedB serves inference")
@@ -52,6 +52,9 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--size", type=int, default=8192,
                    help="c2 only: M = N = K per rank (profiling captures use a smaller case)")
+    p.add_argument("--view", choices=["transpose", "slice", "stepped"], default="transpose",
+                   help="copy only: the packed view (transposed; a column slice of a wider "
+                        "matrix, read as 16-byte rows; every other column, a gather)")
     p.add_argument("--mnk", type=str, default=None,
                    help="c2: 'M,N,K' per rank instead of --size; gemv: 'M,1,K' (profiling shapes)")
     return p.parse_args()
@@ -366,6 +369,43 @@ def main():
         def step():
             mf.gemm_strided_batched(Q, K, scale, None, 0.0, False, True, precision=args.precision)
             mf.gemm_strided_batched(P, V, precision=args.precision)
+    elif args.workload == "copy":
+        # Tensor::contiguous() of C2's transposed operand: what the unpatched reference does to
+        # B^T before every CUDA gemm with transB (through the host, src/core/tensor.cpp:224-229)
+        m = n = args.size
+        k = 1
+        scaling = "weak"
+        if args.view == "transpose":
+            wl = (f"copy: Tensor::contiguous() of an {m}x{n} transposed fp32 view (C2's B^T) on "
+                  f"the device")
+            Bsrc = torch.randn(n, m, device=device, generator=gen)
+            view = Bsrc.t()
+        elif args.view == "slice":
+            wl = f"copy: Tensor::contiguous() of columns 4..{n + 3} of an {m}x{n + 8} fp32 matrix"
+            Bsrc = torch.randn(m, n + 8, device=device, generator=gen)
+            view = Bsrc[:, 4:n + 4]
+        else:
+            wl = f"copy: Tensor::contiguous() of every other column of an {m}x{2 * n} fp32 matrix"
+            Bsrc = torch.randn(m, 2 * n, device=device, generator=gen)
+            view = Bsrc[:, ::2]
+        flops_rank = 0.0
+        unit = "GB/s"
+        h2d_bytes = 4 * Bsrc.numel()
+        d2h_bytes = 4 * m * n
+
+        def step():
+            mf.contiguous(view)
+
+        def e2e_factory():
+            hB = Bsrc.cpu().pin_memory()
+            hout = torch.empty(m, n, pin_memory=True)
+            dB = torch.empty_like(Bsrc)
+
+            def e2e_step():
+                dB.copy_(hB, non_blocking=True)
+                dview = dB.as_strided(view.shape, view.stride(), view.storage_offset())
+                hout.copy_(mf.contiguous(dview), non_blocking=True)
+            return e2e_step
     else:
         m, k = 65536, 8192
         if args.mnk:
@@ -430,7 +470,18 @@ def main():
     kern_per_step = kern_n / args.steps
     assert mf.device_status() == 0, "a kernel recorded a fault during the timed region"
 
-    if args.workload == "gemv":
+    if args.workload == "copy":
+        bytes_rank = 8.0 * m * n  # each element read once and written once
+        value = world * bytes_rank / (ms * 1e-3) / 1e9
+        achieved = bytes_rank / (kern_step_ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": profiled_traffic("copy", "f32"),
+                    "peak_source": f"{peaks['source']} hbm_gbs (STREAM-style copy)",
+                    "kernel": {"transpose": "copy_transpose_kernel"}.get(
+                        args.view, "copy_rows_kernel"),
+                    "algorithmic_bytes_per_launch": bytes_rank}
+    elif args.workload == "gemv":
         bytes_rank = 4.0 * (m * k + k + m)
         value = world * bytes_rank / (ms * 1e-3) / 1e9
         achieved = bytes_rank / (kern_step_ms * 1e-3) / 1e9
@@ -475,12 +526,33 @@ def main():
         torch.cuda.synchronize()
         e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps)
         barrier()
-        if args.workload == "gemv":
+        if args.workload in ("gemv", "copy"):
             e_val = world * bytes_rank / (e_ms * 1e-3) / 1e9
         else:
             e_val = world * flops_rank / (e_ms * 1e-3) / 1e12
+        # this box's host link, for reading e2e: one pinned 256 MiB copy each way, and both at once
+        hbuf = torch.empty(64 << 20, pin_memory=True)
+        dbuf = torch.empty(64 << 20, device=device)
+        link = {}
+        for what in ("h2d", "d2h"):
+            best = 0.0
+            for _ in range(3):
+                l0 = torch.cuda.Event(enable_timing=True)
+                l1 = torch.cuda.Event(enable_timing=True)
+                l0.record(stream)
+                if what == "h2d":
+                    dbuf.copy_(hbuf, non_blocking=True)
+                else:
+                    hbuf.copy_(dbuf, non_blocking=True)
+                l1.record(stream)
+                torch.cuda.synchronize()
+                best = max(best, hbuf.numel() * 4 / (l0.elapsed_time(l1) * 1e-3) / 1e9)
+            link[f"{what}_gbs"] = best
+        del hbuf, dbuf
+        bound_ms = max(h2d_bytes / (link["h2d_gbs"] * 1e9), d2h_bytes / (link["d2h_gbs"] * 1e9)) * 1e3
         e2e = {"value": e_val, "unit": unit, "h2d_bytes_per_step": h2d_bytes,
                "d2h_bytes_per_step": d2h_bytes, "ms_per_step": e_ms, "steps": e2e_steps,
+               "host_link": link, "link_bound_ms_per_step": bound_ms,
                "path": "mensurflow_b200 op on pinned host tensors (execution='gpu'): host -> "
                        "device copies, the C ABI kernels, device -> host copy of the result, "
                        "pipelined by row blocks, all inside the timed region"}
@@ -513,9 +585,25 @@ def main():
                             "sample": f"reference public gemm(+bias_add) on {rows} of 8192 rows "
                                       f"(B full), median of 3 timed calls, {per:.2f} s each"}
 
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "copy"
+            and args.view == "transpose"):
+        from oracle import oracle as O
+
+        if O.reference() is not None:
+            O.reference().mfref_set_threads(host_threads())
+            secs = O.ref_time_transpose_contiguous(m, n, 1, 3)
+            per = float(np.median(secs))
+            cpu_baseline = {"value": 8.0 * m * n / per / 1e9, "unit": "GB/s",
+                            "cores": int(O.reference().mfref_max_threads()), "kind": "reference",
+                            "sample": f"reference Tensor::contiguous() of the {m}x{n} transpose "
+                                      f"(cpu::transpose_f32), median of 3 calls, "
+                                      f"{per * 1e3:.1f} ms each"}
+
+    metric = {"gemv": "gemv HBM GB/s (65536x8192 fp32)",
+              "copy": "strided copy GB/s (Tensor::contiguous of a transposed 8192^2 fp32 view)"}
     if rank == 0:
         emit({
-            "metric": METRIC if args.workload != "gemv" else "gemv HBM GB/s (65536x8192 fp32)",
+            "metric": metric.get(args.workload, METRIC),
             "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "f32",

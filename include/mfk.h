@@ -212,6 +212,28 @@ int mfk_masked_softmax_f32(const float* scores, const uint8_t* keep, int64_t kee
 int mfk_where_f32(const uint8_t* cond, const float* x, const float* y, float* out, int64_t n,
                   void* stream);
 
+/* Tensor::contiguous() on the device: gathers the strided view x (element (i_0..i_{n-1}) at
+ * x[sum_d i_d * strides[d]], strides in elements, any sign, 0 for broadcast dims) into the
+ * row-major buffer out of the same shape. shape/strides are host arrays of ndim entries. Replaces
+ * the host round trip of non-CPU tensors in src/core/tensor.cpp:208-230 (copy_to_host into a
+ * std::vector, then copy_from_host) and matches the CPU path's cpu::strided_copy_f32 /
+ * cpu::transpose_f32 (src/backends/cpu/ops/movement/movement.cpp:12-67) byte for byte. After
+ * merging size-1 and contiguous neighbouring dims at most 12 dims may remain
+ * (MFK_ERR_UNSUPPORTED beyond). out must not overlap x. */
+int mfk_strided_copy_f32(const float* x, const int64_t* shape, const int64_t* strides,
+                         int32_t ndim, float* out, void* stream);
+
+/* out[i] = x[i] for n contiguous elements. Replaces the OpId::Copy kernel (CPU adapter:
+ * src/backends/cpu/backend.cpp:110-113 -> cpu::copy_f32; op: src/ops/blas.cpp:106-117). */
+int mfk_copy_f32(const float* x, float* out, int64_t n, void* stream);
+
+/* Tensor::to(device) between two CUDA devices: `bytes` from src on src_device to dst on
+ * dst_device, device to device over NVLink (a stream-ordered peer copy on `stream`), instead of
+ * the reference's staging through a host std::vector (src/core/tensor.cpp:193-206). The same
+ * device gives a device-to-device copy. */
+int mfk_copy_peer(void* dst, int32_t dst_device, const void* src, int32_t src_device,
+                  int64_t bytes, void* stream);
+
 /* Process-wide precision used when a descriptor says MFK_PRECISION_DEFAULT. The reference's
  * public signatures have no precision argument, so its adapters leave the default in place. */
 int mfk_set_default_precision(int32_t precision);

@@ -9,6 +9,8 @@ from .ops import (  # noqa: F401
     attention,
     bias_add,
     bias_grad,
+    contiguous,
+    copy,
     device_status,
     gelu,
     gemm,
@@ -26,12 +28,14 @@ from .ops import (  # noqa: F401
     relu,
     set_default_precision,
     softmax,
+    to,
     where,
 )
 
 __all__ = [
-    "MfkError", "PackedB", "build", "attention", "bias_add", "bias_grad", "device_status",
+    "MfkError", "PackedB", "build", "attention", "bias_add", "bias_grad", "contiguous",
+    "copy", "device_status",
     "gelu", "gemm", "gemm_prepacked", "gemm_strided_batched", "gemv", "get_default_precision",
     "linear", "linear_backward", "log_softmax", "matmul", "matmul_backward", "matvec", "pack_b",
-    "relu", "set_default_precision", "softmax", "where",
+    "relu", "set_default_precision", "softmax", "to", "where",
 ]

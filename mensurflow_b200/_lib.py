@@ -42,6 +42,9 @@ EXPORTED = (
     "mfk_softmax_f32",
     "mfk_masked_softmax_f32",
     "mfk_where_f32",
+    "mfk_strided_copy_f32",
+    "mfk_copy_f32",
+    "mfk_copy_peer",
     "mfk_set_default_precision",
     "mfk_get_default_precision",
     "mfk_device_status",
@@ -124,6 +127,10 @@ def lib() -> ctypes.CDLL:
             so.mfk_softmax_f32.argtypes = [vp, vp, i64, i64, i64, i32, vp]
             so.mfk_masked_softmax_f32.argtypes = [vp, vp, i64, i64, i32, vp, i64, i64, i64, vp]
             so.mfk_where_f32.argtypes = [vp, vp, vp, vp, i64, vp]
+            so.mfk_strided_copy_f32.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64),
+                                                i32, vp, vp]
+            so.mfk_copy_f32.argtypes = [vp, vp, i64, vp]
+            so.mfk_copy_peer.argtypes = [vp, i32, vp, i32, i64, vp]
             so.mfk_set_default_precision.argtypes = [i32]
             so.mfk_get_default_precision.restype = i32
             so.mfk_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]

@@ -17,6 +17,7 @@
 #include "mfk.h"
 
 #include "gemm_tc.cuh"
+#include "movement.cuh"
 #include "prep.cuh"
 #include "simt.cuh"
 
@@ -908,6 +909,136 @@ int mfk_where_f32(const uint8_t* cond, const float* x, const float* y, float* ou
     mfk::where_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         cond, x, y, out, n);
     MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+int launch_contig_copy(const float* x, float* out, int64_t n, const DeviceInfo* info,
+                       cudaStream_t stream) {
+    const int64_t max_blocks = int64_t(info->sm_count) * 8;
+    g_launches.fetch_add(1);
+    if (aligned16(x) && aligned16(out) && n % 4 == 0) {
+        const int64_t n4 = n / 4;
+        const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, max_blocks);
+        mfk::copy_contig_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(out), n4);
+    } else {
+        const int64_t blocks = std::min<int64_t>((n + 255) / 256, max_blocks);
+        mfk::copy_contig_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, out, n);
+    }
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mfk_strided_copy_f32(const float* x, const int64_t* shape, const int64_t* strides,
+                         int32_t ndim, float* out, void* stream_) {
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (ndim < 0 || (ndim > 0 && (shape == nullptr || strides == nullptr)))
+        return MFK_ERR_INVALID_ARGUMENT;
+    // Merge the view: drop size-1 dims, fold a dim into its outer neighbour when the pair is one
+    // evenly strided run. The output is row-major over the same shape either way.
+    mfk::CopyView v{};
+    int64_t numel = 1;
+    for (int d = 0; d < ndim; ++d) {
+        if (shape[d] < 0) return MFK_ERR_INVALID_ARGUMENT;
+        if (__builtin_mul_overflow(numel, shape[d], &numel)) return MFK_ERR_INVALID_ARGUMENT;
+    }
+    if (numel == 0) return MFK_OK;
+    if (x == nullptr || out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    for (int d = 0; d < ndim; ++d) {
+        if (shape[d] == 1) continue;
+        if (v.ndim > 0 && v.stride[v.ndim - 1] == strides[d] * shape[d]) {
+            v.shape[v.ndim - 1] *= shape[d];
+            v.stride[v.ndim - 1] = strides[d];
+            continue;
+        }
+        if (v.ndim == mfk::kMaxCopyDims) return MFK_ERR_UNSUPPORTED;
+        v.shape[v.ndim] = shape[d];
+        v.stride[v.ndim] = strides[d];
+        ++v.ndim;
+    }
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    if (v.ndim == 0) return launch_contig_copy(x, out, 1, info, stream);
+    if (v.ndim == 1 && v.stride[0] == 1) return launch_contig_copy(x, out, numel, info, stream);
+
+    const int n = v.ndim;
+    const int64_t L = v.shape[n - 1];
+    const int64_t rows = numel / L;
+    const int64_t max_blocks = int64_t(info->sm_count) * 8;
+    int p = -1;
+    if (v.stride[n - 1] != 1) {
+        for (int d = n - 2; d >= 0; --d) {
+            if (v.stride[d] == 1) {
+                p = d;
+                break;
+            }
+        }
+    }
+    g_launches.fetch_add(1);
+    TimedLaunch timed(stream);
+    if (p >= 0) {
+        const int64_t batch = rows / v.shape[p];
+        const int64_t tiles = ((L + mfk::kCopyTile - 1) / mfk::kCopyTile) *
+                              ((v.shape[p] + mfk::kCopyTile - 1) / mfk::kCopyTile) * batch;
+        const int64_t blocks = std::min<int64_t>(tiles, max_blocks);
+        mfk::copy_transpose_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            x, out, v, p, batch);
+    } else if (L < 32) {
+        const int64_t blocks = std::min<int64_t>((rows + 255) / 256, max_blocks);
+        mfk::copy_short_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            x, out, v, rows);
+    } else {
+        bool vec4 = v.stride[n - 1] == 1 && L % 4 == 0 && aligned16(x) && aligned16(out);
+        for (int d = 0; d + 1 < n; ++d) vec4 = vec4 && v.stride[d] % 4 == 0;
+        const int64_t pieces = (L + mfk::kCopyPiece - 1) / mfk::kCopyPiece;
+        const int64_t blocks = std::min<int64_t>((rows * pieces * 32 + 255) / 256, max_blocks);
+        if (vec4) {
+            mfk::copy_rows_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                x, out, v, rows);
+        } else {
+            mfk::copy_rows_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                x, out, v, rows);
+        }
+    }
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+int mfk_copy_f32(const float* x, float* out, int64_t n, void* stream) {
+    if (n < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (n == 0) return MFK_OK;
+    if (x == nullptr || out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    return launch_contig_copy(x, out, n, info, static_cast<cudaStream_t>(stream));
+}
+
+int mfk_copy_peer(void* dst, int32_t dst_device, const void* src, int32_t src_device,
+                  int64_t bytes, void* stream) {
+    if (bytes < 0 || dst_device < 0 || src_device < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (bytes == 0) return MFK_OK;
+    if (dst == nullptr || src == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    int count = 0;
+    MFK_CUDA(cudaGetDeviceCount(&count));
+    if (dst_device >= count || src_device >= count) return MFK_ERR_INVALID_ARGUMENT;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dst_device == src_device) {
+        MFK_CUDA(cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToDevice, s));
+    } else {
+        MFK_CUDA(cudaMemcpyPeerAsync(dst, dst_device, src, src_device, static_cast<size_t>(bytes), s));
+    }
     return MFK_OK;
 }
 

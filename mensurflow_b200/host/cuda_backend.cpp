@@ -277,6 +277,28 @@ void gemv_kernel(const OpArgs& args, Stream& stream) {
               "gemv");
 }
 
+// OpId::Copy: out = a packed copy of the input. The op hands over a contiguous input
+// (src/ops/blas.cpp:106-117); a strided input is gathered in the same launch, which is what
+// Tensor::contiguous() dispatches for a CUDA view once it routes through OpId::Copy instead of
+// the host (the patch in INTEGRATION.md; today src/core/tensor.cpp:224-229 stages through a host
+// vector). Same contract as the CPU adapter (src/backends/cpu/backend.cpp:110-113).
+void copy_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& x = args.inputs[0];
+    const Tensor& out = args.outputs[0];
+    if (x.is_contiguous()) {
+        check_mfk(mfk_copy_f32(TensorAccess::data<float>(x), TensorAccess::data<float>(out),
+                               out.numel(), s.raw()),
+                  "copy");
+        return;
+    }
+    const std::vector<std::int64_t> shape(x.shape().begin(), x.shape().end());
+    const std::vector<std::int64_t> strides(x.strides().begin(), x.strides().end());
+    check_mfk(mfk_strided_copy_f32(TensorAccess::data<float>(x), shape.data(), strides.data(),
+                                   x.dim(), TensorAccess::data<float>(out), s.raw()),
+              "contiguous");
+}
+
 // OpId::Matvec: contiguous a [m, k], x [k].
 void matvec_kernel(const OpArgs& args, Stream& stream) {
     auto& s = cuda(stream);
@@ -360,6 +382,7 @@ class CudaBackend final : public Backend {
         dispatcher.register_kernel(key(OpId::Softmax), softmax_kernel<0>);
         dispatcher.register_kernel(key(OpId::LogSoftmax), softmax_kernel<1>);
         dispatcher.register_kernel(key(OpId::Where), where_kernel);
+        dispatcher.register_kernel(key(OpId::Copy), copy_kernel);
 #ifdef MENSURFLOW_HAS_OPID_GEMM
         dispatcher.register_kernel(key(OpId::Gemm), gemm_kernel);
 #else

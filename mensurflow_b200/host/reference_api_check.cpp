@@ -4,6 +4,7 @@
 // not run on a GPU: gemm_strided_batched (the 19 API cases of tests/ops/gemm_batched_test.cpp),
 // attention (the cases of tests/ops/softmax_loss_test.cpp test_attention), softmax, bias_add,
 // relu and gelu. Prints one line per check and exits non-zero on the first mismatch.
+#include "core/dispatcher.hpp"
 #include "mensurflow/mensurflow.hpp"
 
 #include <cmath>
@@ -160,6 +161,37 @@ void check_elementwise(Device gpu) {
                   &mag);
 }
 
+// Device-side packing of views: the reference's public copy() on a CUDA tensor, and OpId::Copy
+// dispatched with a strided CUDA view as its input — the call Tensor::contiguous() makes once it
+// routes CUDA views through OpId::Copy instead of a host round trip — against
+// the CPU's Tensor::contiguous() of the same view. Copies are exact.
+void check_copy(Device gpu) {
+    const Tensor x = input({6, 7, 8}, 51);
+    const Tensor xg = x.to(gpu);
+    require_close(copy(xg, Execution::GPU), copy(x, Execution::CPU), 0.0, 0.0, "copy");
+    struct View {
+        const char* name;
+        Tensor (*make)(const Tensor&);
+    };
+    const View views[] = {
+        {"transpose", [](const Tensor& t) { return t.view({42, 8}).transpose(0, 1); }},
+        {"permute 2,0,1", [](const Tensor& t) { return t.permute({2, 0, 1}); }},
+        {"permute 1,2,0", [](const Tensor& t) { return t.permute({1, 2, 0}); }},
+        {"column slice", [](const Tensor& t) { return t.slice(2, 1, 7); }},
+        {"stepped slices", [](const Tensor& t) { return t.slice(0, 1, 6, 2).slice(2, 0, 8, 3); }},
+        {"expand", [](const Tensor& t) { return t.slice(0, 0, 1).expand({4, 6, 7, 8}); }},
+        {"transpose + slice", [](const Tensor& t) { return t.transpose(0, 1).slice(2, 3, 4); }},
+    };
+    for (const View& v : views) {
+        const Tensor view_g = v.make(xg);
+        Tensor out = Tensor::empty(view_g.shape(), DType::F32, gpu);
+        detail::OpArgs args{{view_g}, {out}};
+        detail::dispatch(detail::OpId::Copy, args, Execution::GPU);
+        require_close(out, v.make(x).contiguous(), 0.0, 0.0,
+                      std::string("contiguous on the device: ") + v.name);
+    }
+}
+
 } // namespace
 
 int main() {
@@ -172,6 +204,7 @@ int main() {
         check_batched(gpu);
         check_attention(gpu);
         check_elementwise(gpu);
+        check_copy(gpu);
         std::cout << "reference_api_check passed (" << checks << " checks on " << to_string(gpu)
                   << ")\n";
         return 0;

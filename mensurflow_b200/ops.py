@@ -62,6 +62,71 @@ def _kernel_for(op: str, t: torch.Tensor):
         raise NotImplementedError(f"{op}: these kernels run on CUDA devices only")
 
 
+def contiguous(x: torch.Tensor) -> torch.Tensor:
+    """Tensor::contiguous() on the device (src/core/tensor.cpp:208-230): a contiguous tensor is
+    returned as it is; a strided view (transposed, permuted, sliced with steps, expanded) is
+    gathered into a new row-major tensor on the same device by one kernel
+    (mfk_strided_copy_f32), where the reference stages non-CPU views through a host vector."""
+    _require(x, "contiguous", "x")
+    if x.is_contiguous():
+        return x
+    _kernel_for("contiguous", x)
+    out = torch.empty(tuple(x.shape), dtype=x.dtype, device=x.device)
+    nd = x.dim()
+    shape = (ctypes.c_int64 * max(nd, 1))(*x.shape)
+    strides = (ctypes.c_int64 * max(nd, 1))(*x.stride())
+    with torch.cuda.device(x.device):
+        check(_lib.lib().mfk_strided_copy_f32(x.data_ptr(), shape, strides, nd, out.data_ptr(),
+                                              _stream()), "contiguous")
+    return out
+
+
+def copy(x: torch.Tensor) -> torch.Tensor:
+    """A packed copy, as mensurflow::copy (src/ops/blas.cpp:106-117): a new tensor of x's shape
+    on x's device that never shares x's storage. A strided x is gathered in the same launch (the
+    reference packs it with contiguous() first and then copies again)."""
+    _require(x, "copy", "x")
+    _kernel_for("copy", x)
+    if not x.is_contiguous():
+        return contiguous(x)
+    out = torch.empty(tuple(x.shape), dtype=x.dtype, device=x.device)
+    if x.numel() == 0:
+        return out
+    with torch.cuda.device(x.device):
+        check(_lib.lib().mfk_copy_f32(x.data_ptr(), out.data_ptr(), x.numel(), _stream()), "copy")
+    return out
+
+
+def to(x: torch.Tensor, device) -> torch.Tensor:
+    """Tensor::to(device) (src/core/tensor.cpp:193-206). The same device returns x itself; a
+    move between two CUDA devices is a device-to-device copy over NVLink (mfk_copy_peer) of the
+    packed tensor, ordered after x's producers on x's device and before later work on the
+    target's current stream, where the reference stages it through a host vector. A move to or
+    from the host is a plain host copy (the reference's copy_to_host / copy_from_host)."""
+    _require(x, "to", "x")
+    target = torch.device(device)
+    if target.type == "cuda" and target.index is None:
+        target = torch.device("cuda", torch.cuda.current_device())
+    if target == x.device:
+        return x
+    if target.type != "cuda" or x.device.type != "cuda":
+        return x.to(target).contiguous() if target.type == "cpu" else x.contiguous().to(target)
+    _kernel_for("to", x)
+    src = contiguous(x)
+    out = torch.empty(tuple(x.shape), dtype=x.dtype, device=target)
+    if x.numel() == 0:
+        return out
+    src_stream = torch.cuda.current_stream(x.device)
+    with torch.cuda.device(x.device):
+        check(_lib.lib().mfk_copy_peer(out.data_ptr(), target.index, src.data_ptr(),
+                                       x.device.index, src.numel() * src.element_size(),
+                                       src_stream.cuda_stream), "to")
+    done = torch.cuda.Event()
+    done.record(src_stream)
+    torch.cuda.current_stream(target).wait_event(done)
+    return out
+
+
 def set_default_precision(precision: str) -> None:
     """Process-wide GEMM precision ("3xtf32", the default, or "1xtf32")."""
     check(_lib.lib().mfk_set_default_precision(_PRECISIONS[precision]), "set_default_precision")
@@ -190,7 +255,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch
                                transpose_b, bias, activation, precision, out, chunks)
     _kernel_for("gemm", a)
     if bias is not None:
-        bias = bias.contiguous()
+        bias = contiguous(bias)
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=a.device)
     elif tuple(out.shape) != (m, n) or out.stride(1) != 1:
@@ -296,7 +361,7 @@ def gemm_prepacked(a: torch.Tensor, packed: PackedB, alpha: float = 1.0,
     if activation not in _ACTS:
         raise ValueError(f"gemm_prepacked: unknown activation {activation!r}")
     if bias is not None:
-        bias = bias.contiguous()
+        bias = contiguous(bias)
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=a.device)
     elif tuple(out.shape) != (m, n) or out.stride(1) != 1:
@@ -349,7 +414,7 @@ def bias_grad(grad: torch.Tensor) -> torch.Tensor:
     _require(grad, "bias_grad", "grad", 2)
     _kernel_for("bias_grad", grad)
     rows, cols = grad.shape
-    g = grad if grad.stride(1) == 1 and (rows <= 1 or grad.stride(0) >= cols) else grad.contiguous()
+    g = grad if grad.stride(1) == 1 and (rows <= 1 or grad.stride(0) >= cols) else contiguous(grad)
     out = torch.empty(cols, dtype=torch.float32, device=grad.device)
     ld = g.stride(0) if rows > 1 else cols
     check(_lib.lib().mfk_bias_grad_f32(_ptr(g) if g.numel() else None, rows, cols, ld,
@@ -465,7 +530,7 @@ def gemm_strided_batched(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0,
         c_off = _odometer_offsets(initial, batch_shape)
         even = batch <= 1 or bool(np.all(np.diff(c_off) == c_off[1] - c_off[0]))
         if not even:
-            initial = initial.contiguous()  # the reference packs c the same way (blas.cpp:361)
+            initial = contiguous(initial)  # the reference packs c the same way (blas.cpp:361)
             c_off = _odometer_offsets(initial, batch_shape)
         desc.c_in = initial.data_ptr()
         desc.c_in_rs, desc.c_in_cs = initial.stride(-2), initial.stride(-1)
@@ -492,9 +557,9 @@ def gemv(a: torch.Tensor, x: torch.Tensor, alpha: float = 1.0, y: Optional[torch
         raise ValueError("gemv: output length does not match matrix dimensions")
     _kernel_for("gemv", a)
     if a.stride(1) != 1 or (rows > 1 and a.stride(0) < cols):
-        a = a.contiguous()
+        a = contiguous(a)
     out = torch.empty(n_out, dtype=torch.float32, device=a.device)
-    y0 = y.contiguous() if y is not None else None
+    y0 = contiguous(y) if y is not None else None
     check(_lib.lib().mfk_gemv_f32(a.data_ptr(), rows, cols, max(a.stride(0), cols),
                                   1 if transpose_a else 0, x.data_ptr(), x.stride(0) or 1,
                                   float(alpha), float(beta), _ptr(y0), out.data_ptr(), _stream()),
@@ -515,7 +580,7 @@ def matvec(a: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
 
 def _bias_act(x: torch.Tensor, bias: Optional[torch.Tensor], act: int, op: str) -> torch.Tensor:
     _kernel_for(op, x)
-    x = x.contiguous()
+    x = contiguous(x)
     out = torch.empty_like(x)
     cols = x.shape[-1] if x.dim() > 0 else 1
     rows = x.numel() // cols if cols else 0
@@ -533,7 +598,7 @@ def bias_add(x: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
         raise ValueError(f"bias_add: expected x [batch, features] and bias [features], got "
                          f"{tuple(x.shape)} and {tuple(bias.shape)}")
     _same("bias_add", x, bias)
-    return _bias_act(x, bias.contiguous(), _lib.ACT_NONE, "bias_add")
+    return _bias_act(x, contiguous(bias), _lib.ACT_NONE, "bias_add")
 
 
 def relu(x: torch.Tensor) -> torch.Tensor:
@@ -559,7 +624,7 @@ def _softmax(x: torch.Tensor, axis: int, log: bool, op: str) -> torch.Tensor:
     if not 0 <= ax < extent:
         raise ValueError(f"{op}: axis {axis} is out of range for a {rank}-d tensor")
     _kernel_for(op, x)
-    x = x.contiguous()
+    x = contiguous(x)
     shape = tuple(x.shape) if rank else (1,)
     outer = int(np.prod(shape[:ax])) if ax else 1
     inner = int(np.prod(shape[ax + 1:])) if ax + 1 < len(shape) else 1
@@ -597,8 +662,8 @@ def where(condition: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> torch.Te
     except RuntimeError as e:
         raise ValueError(f"where: {e}")
     _kernel_for("where", x)
-    xx = x.expand(shape).contiguous()
-    yy = y.expand(shape).contiguous()
+    xx = contiguous(x.expand(shape))
+    yy = contiguous(y.expand(shape))
     cc = condition.expand(shape).contiguous()
     out = torch.empty(shape, dtype=torch.float32, device=x.device)
     check(_lib.lib().mfk_where_f32(cc.data_ptr(), xx.data_ptr(), yy.data_ptr(), out.data_ptr(),

@@ -116,6 +116,10 @@ def reference():
                 so.mfref_attention.argtypes = [_ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int,
                                                _ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int,
                                                ctypes.c_int, _f32, _ptr, _ptr, _ptr]
+                so.mfref_contiguous_view.argtypes = [_ptr, _ptr, ctypes.c_int, _ptr, _ptr, _ptr,
+                                                     _ptr, _ptr, ctypes.c_int, _ptr, _ptr]
+                so.mfref_time_transpose_contiguous.argtypes = [_i64, _i64, ctypes.c_int,
+                                                               ctypes.c_int, _ptr]
                 _ref = so
     return _ref
 
@@ -421,6 +425,92 @@ class RefGemmBench:
 def ref_time_gemv(rows, cols, seed, warmup, reps):
     secs = np.zeros(reps, np.float64)
     _check_ref(reference().mfref_time_gemv(rows, cols, seed, warmup, reps, _p(secs)))
+    return secs
+
+
+def view_recipe_shape(base_shape, order, slices, expand=None):
+    """Shape of base.permute(order) sliced by `slices` ((start, end, step) per dim) and expanded."""
+    if expand is not None:
+        return tuple(expand)
+    shape = []
+    for d, (start, end, step) in enumerate(slices):
+        size = end - start
+        shape.append(0 if size <= 0 else (size + step - 1) // step)
+    return tuple(shape)
+
+
+def view_recipe_strided(base_shape, order, slices, expand=None):
+    """(offset, shape, strides) in elements of the recipe's view over a contiguous base, with the
+    reference's view arithmetic: permute reorders (shape, strides) (src/core/tensor.cpp permute),
+    slice moves the offset by start*stride and multiplies the stride by step, expand gives
+    broadcast dims stride 0 (leading new dims included)."""
+    nd = len(base_shape)
+    base_strides = [1] * nd
+    for d in range(nd - 2, -1, -1):
+        base_strides[d] = base_strides[d + 1] * base_shape[d + 1]
+    shape = [base_shape[o] for o in order]
+    strides = [base_strides[o] for o in order]
+    offset = 0
+    for d, (start, end, step) in enumerate(slices):
+        size = max(0, end - start)
+        offset += start * strides[d] if size > 0 else 0
+        shape[d] = 0 if size == 0 else (size + step - 1) // step
+        strides[d] *= step
+    if expand is not None:
+        lead = len(expand) - nd
+        strides = [0] * lead + [0 if (shape[d] == 1 and expand[lead + d] != 1) else strides[d]
+                                for d in range(nd)]
+        shape = list(expand)
+    return offset, tuple(shape), tuple(strides)
+
+
+def strided_copy(buf, offset, shape, strides):
+    """Restatement of cpu::strided_copy_f32 (src/backends/cpu/ops/movement/movement.cpp:12-42):
+    output row r (all dims but the innermost, innermost outer dim fastest) starts at the input
+    offset sum_d coord_d*strides[d]; its elements are read at unit stride when the innermost
+    stride is 1 (one memcpy per row in the reference), else one by one. transpose_f32 (:44-67)
+    gives the same values for a transposed matrix."""
+    buf = np.asarray(buf, np.float32).reshape(-1)
+    n = int(np.prod(shape)) if len(shape) else 1
+    out = np.empty(n, np.float32)
+    if n == 0:
+        return out.reshape(shape)
+    nd = len(shape)
+    row = shape[-1] if nd else 1
+    rows = n // row
+    cols = np.arange(row, dtype=np.int64) * (strides[-1] if nd else 0)
+    for r in range(rows):
+        src, index = offset, r
+        for d in range(nd - 2, -1, -1):
+            src += (index % shape[d]) * strides[d]
+            index //= shape[d]
+        out[r * row:(r + 1) * row] = buf[src + cols]
+    return out.reshape(shape)
+
+
+def ref_contiguous_view(x, order, slices, expand=None):
+    """The reference's Tensor::contiguous() of x.permute(order).slice(...)[.expand(...)]."""
+    x = np.ascontiguousarray(x, np.float32)
+    nd = x.ndim
+    base = np.array(x.shape, np.int64)
+    o = np.array(order, np.int32)
+    st = np.array([s[0] for s in slices], np.int64)
+    en = np.array([s[1] for s in slices], np.int64)
+    sp = np.array([s[2] for s in slices], np.int64)
+    ex = None if expand is None else np.array(expand, np.int64)
+    shape = view_recipe_shape(x.shape, order, slices, expand)
+    out = np.empty(shape, np.float32)
+    oshape = np.zeros(16, np.int64)
+    _check_ref(reference().mfref_contiguous_view(
+        _p(x), _p(base), nd, _p(o), _p(st), _p(en), _p(sp), _p(ex),
+        0 if ex is None else len(expand), _p(out), _p(oshape)))
+    assert tuple(int(v) for v in oshape[:len(shape)]) == tuple(shape)
+    return out
+
+
+def ref_time_transpose_contiguous(rows, cols, warmup, reps):
+    secs = np.zeros(reps, np.float64)
+    _check_ref(reference().mfref_time_transpose_contiguous(rows, cols, warmup, reps, _p(secs)))
     return secs
 
 

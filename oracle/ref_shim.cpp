@@ -303,4 +303,50 @@ int mfref_time_gemv(std::int64_t rows, std::int64_t cols, std::uint64_t seed, in
     });
 }
 
+// A strided view built with the reference's public view ops, then made contiguous by
+// Tensor::contiguous() (src/core/tensor.cpp:208-230 -> cpu::transpose_f32 for a transposed
+// matrix, cpu::strided_copy_f32 otherwise): x is a contiguous host tensor of base_shape (nd
+// dims); the view is x.permute(order), then slice(d, start[d], end[d], step[d]) for every d,
+// then expand(expand_shape) when expand_shape is non-null (out_nd dims). `out` receives the
+// contiguous result, `out_shape` its shape (nd, or out_nd after expand).
+int mfref_contiguous_view(const float* x, const std::int64_t* base_shape, int nd,
+                          const int* order, const std::int64_t* start, const std::int64_t* end,
+                          const std::int64_t* step, const std::int64_t* expand_shape, int out_nd,
+                          float* out, std::int64_t* out_shape) {
+    return guarded([&] {
+        Tensor t = host_tensor(x, make_shape(base_shape, nd));
+        t = t.permute(std::vector<int>(order, order + nd));
+        for (int d = 0; d < nd; ++d) {
+            t = t.slice(d, start[d], end[d], step[d]);
+        }
+        if (expand_shape != nullptr) {
+            t = t.expand(make_shape(expand_shape, out_nd));
+        }
+        const Tensor c = t.contiguous();
+        for (int d = 0; d < c.dim(); ++d) {
+            out_shape[d] = c.shape()[d];
+        }
+        copy_out(c, out);
+    });
+}
+
+// Times the reference's Tensor::contiguous() of a transposed [rows, cols] matrix (the view of a
+// contiguous [cols, rows] tensor), the CPU path cpu::transpose_f32.
+int mfref_time_transpose_contiguous(std::int64_t rows, std::int64_t cols, int warmup, int reps,
+                                    double* seconds) {
+    return guarded([&] {
+        const Tensor base = uniform({cols, rows}, -1.0f, 1.0f, 5, 0, Execution::CPU);
+        const Tensor view = base.transpose(0, 1);
+        for (int i = 0; i < warmup; ++i) {
+            view.contiguous();
+        }
+        for (int i = 0; i < reps; ++i) {
+            const double t0 = now();
+            const Tensor r = view.contiguous();
+            seconds[i] = now() - t0;
+            (void)r;
+        }
+    });
+}
+
 } // extern "C"

@@ -184,6 +184,17 @@ def main():
         bwd[f"matmul_{m}x{k}x{n}_da"] = da
         bwd[f"matmul_{m}x{k}x{n}_db"] = db
     np.savez_compressed(os.path.join(HERE, "backward_cases.npz"), **bwd)
+
+    # Tensor::contiguous() of the views in tests/helpers.py COPY_CASES (src/core/tensor.cpp:208-230
+    # -> cpu::transpose_f32 / cpu::strided_copy_f32)
+    sys.path.insert(0, os.path.dirname(HERE))
+    from helpers import COPY_CASES, copy_case  # noqa: E402
+
+    cpy = {}
+    for i, case in enumerate(COPY_CASES):
+        x, full = copy_case(i)
+        cpy[case[0]] = O.ref_contiguous_view(x, case[2], full, case[4])
+    np.savez_compressed(os.path.join(HERE, "copy_cases.npz"), **cpy)
     print("wrote", sorted(os.listdir(HERE)))
 
 

@@ -121,3 +121,45 @@ def backward_inputs():
             O.normal(k * n, 0, 1, 60 + i, m * k).reshape(k, n),
             O.normal(m * n, 0, 1, 60 + i, m * k + k * n).reshape(m, n))
     return d
+
+
+# Strided views packed by Tensor::contiguous(): name, base shape (a contiguous tensor), permute
+# order, slices {dim: (start, end, step)} applied after the permute, expand shape (or None), and
+# the input ("iota" as the reference's tests/core tests use, else seeded normal). The first four
+# are the views of the reference's tests/core/transfer_test.cpp:50-62 and view_test.cpp:80-100.
+COPY_CASES = [
+    ("transfer_test transpose", (3, 4), (1, 0), {}, None, "iota"),
+    ("transfer_test every other column", (3, 4), (0, 1), {1: (0, 4, 2)}, None, "iota"),
+    ("view_test permute", (2, 3, 4), (2, 0, 1), {}, None, "iota"),
+    ("view_test transpose then slice", (2, 3, 4), (1, 0, 2), {2: (3, 4, 1)}, None, "iota"),
+    ("transpose 257x129", (129, 257), (1, 0), {}, None, "normal"),
+    ("transpose 1024x1024", (1024, 1024), (1, 0), {}, None, "normal"),
+    ("permute rows 0,2,1,3", (3, 20, 30, 64), (0, 2, 1, 3), {}, None, "normal"),
+    ("permute 3,1,2,0", (5, 6, 7, 40), (3, 1, 2, 0), {}, None, "normal"),
+    ("aligned column slice", (64, 100), (0, 1), {1: (8, 72, 1)}, None, "normal"),
+    ("unaligned column slice", (64, 100), (0, 1), {1: (3, 70, 1)}, None, "normal"),
+    ("stepped in both dims", (50, 80), (0, 1), {0: (1, 50, 3), 1: (2, 80, 2)}, None, "normal"),
+    ("expand leading and size-1", (1, 7, 48), (0, 1, 2), {}, (5, 3, 7, 48), "normal"),
+    ("expand innermost", (6, 1), (0, 1), {}, (6, 40), "normal"),
+    ("short rows", (200, 9, 5), (0, 1, 2), {2: (0, 3, 1)}, None, "normal"),
+    ("single element", (4, 5), (0, 1), {0: (2, 3, 1), 1: (3, 4, 1)}, None, "normal"),
+    ("empty", (4, 5), (0, 1), {0: (2, 2, 1)}, None, "normal"),
+    ("batched transpose with slice", (8, 33, 65), (0, 2, 1), {1: (1, 65, 1)}, None, "normal"),
+    ("5-D permute", (3, 4, 5, 6, 7), (4, 2, 0, 3, 1), {}, None, "normal"),
+    ("stepped columns of a whole matrix", (64, 200), (0, 1), {1: (0, 200, 2)}, None, "normal"),
+    ("long aligned rows", (3, 9000), (0, 1), {1: (4, 8996, 1)}, None, "normal"),
+]
+
+
+def copy_case(i):
+    """(input array, full slice list) of COPY_CASES[i]; the slice list has (start, end, step)
+    for every dim of the permuted view."""
+    name, base, order, slices, expand, kind = COPY_CASES[i]
+    n = int(np.prod(base))
+    if kind == "iota":
+        x = np.arange(n, dtype=np.float32).reshape(base)
+    else:
+        x = O.normal(n, 0, 1, 70 + i, 0).reshape(base)
+    permuted = [base[o] for o in order]
+    full = [slices.get(d, (0, permuted[d], 1)) for d in range(len(base))]
+    return x, full

@@ -143,3 +143,37 @@ def test_no_cpu_fallback_when_library_missing(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.lib()
+
+
+def test_strided_copy_argument_errors_before_launch():
+    so = _lib.lib()
+    i64x = ctypes.c_int64 * 13
+    shape = i64x(3, -1)
+    strides = i64x(1, 1)
+    assert so.mfk_strided_copy_f32(None, shape, strides, 2, None, None) == \
+        _lib.MFK_ERR_INVALID_ARGUMENT
+    assert so.mfk_strided_copy_f32(None, shape, strides, -1, None, None) == \
+        _lib.MFK_ERR_INVALID_ARGUMENT
+    # an empty view copies nothing and needs no device
+    shape = i64x(3, 0)
+    assert so.mfk_strided_copy_f32(None, shape, strides, 2, None, None) == _lib.MFK_OK
+    # 13 dims that no merge can reduce (a reversed permutation of a 2 x ... x 2 tensor)
+    shape = i64x(*([2] * 13))
+    strides = i64x(*[1 << d for d in range(13)])
+    assert so.mfk_strided_copy_f32(ctypes.c_void_p(16), shape, strides, 13,
+                                   ctypes.c_void_p(16), None) == _lib.MFK_ERR_UNSUPPORTED
+    assert so.mfk_copy_f32(None, None, -1, None) == _lib.MFK_ERR_INVALID_ARGUMENT
+    assert so.mfk_copy_f32(None, None, 0, None) == _lib.MFK_OK
+    assert so.mfk_copy_peer(None, 0, None, 0, -1, None) == _lib.MFK_ERR_INVALID_ARGUMENT
+    assert so.mfk_copy_peer(None, 0, None, 1, 0, None) == _lib.MFK_OK
+
+
+def test_contiguous_and_to_refuse_cpu_tensors_like_the_dispatcher():
+    x = torch.zeros(3, 4).t()
+    with pytest.raises(NotImplementedError):
+        mf.contiguous(x)
+    with pytest.raises(NotImplementedError):
+        mf.copy(torch.zeros(3))
+    y = torch.zeros(3, 4)
+    assert mf.contiguous(y) is y  # already contiguous: returned as is, as the reference does
+    assert mf.to(y, "cpu") is y

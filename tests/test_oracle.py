@@ -160,3 +160,18 @@ def test_bias_grad_restatement_on_ragged_and_empty_shapes():
                                       err_msg=f"{rows}x{cols}")
     # no rows: the loop adds nothing (the reference records no graph for an empty input)
     np.testing.assert_array_equal(O.bias_grad(np.zeros((0, 5), np.float32)), np.zeros(5))
+
+
+def test_strided_copy_restatement_matches_reference_views():
+    """oracle.strided_copy (cpu::strided_copy_f32 restated) over the reference's view arithmetic
+    reproduces the reference's Tensor::contiguous() on every COPY_CASES view, bit for bit."""
+    from helpers import COPY_CASES, copy_case
+
+    gold = golden("copy_cases.npz")
+    for i, case in enumerate(COPY_CASES):
+        x, full = copy_case(i)
+        off, shape, strides = O.view_recipe_strided(x.shape, case[2], full, case[4])
+        got = O.strided_copy(x, off, shape, strides)
+        want = gold[case[0]]
+        assert got.shape == want.shape, case[0]
+        assert np.array_equal(got, want), case[0]

@@ -3,7 +3,8 @@
 mensurflow_b200/host/Makefile compiles the unmodified reference library with this repository's
 CUDA backend (mensurflow_b200/host/cuda_backend.cpp, which calls the sm_100a kernels through
 include/mfk.h) in place of its cuBLAS backend, and links the reference's matmul_test,
-matvec_test and elementwise_ops_test against it. Those programs check values on every device
+matvec_test, elementwise_ops_test (tests/ops/) and transfer_test, view_test (tests/core/:
+Tensor::to, contiguous and views) against it. Those programs check values on every device
 whose dispatcher has the kernel (tests/ops/matmul_test.cpp:97-100, matvec_test.cpp:69-72,
 elementwise_ops_test.cpp has_bias), so on a GPU box they run their CPU checks and then the same
 checks on cuda:0. reference_api_check is this repository's own program over the same library: it
@@ -21,7 +22,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("name", ["matmul_test", "matvec_test", "elementwise_ops_test",
-                                  "reference_api_check"])
+                                  "transfer_test", "view_test", "reference_api_check"])
 def test_reference_program_passes_on_b200(cuda, name):
     path = os.path.join(BUILD, name)
     if not os.path.exists(path):
@@ -39,3 +40,4 @@ def test_reference_program_passes_on_b200(cuda, name):
         # gemm_strided_batched, attention and softmax, which the reference's programs do not run
         # on a GPU
         assert "on cuda:0" in out and "attention both" in out, out[-2000:]
+        assert "contiguous on the device: permute 2,0,1" in out, out[-2000:]
