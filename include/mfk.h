@@ -129,6 +129,32 @@ int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream);
 #define MFK_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
 int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream);
 
+/* A GEMM split by row blocks over several GPUs of this process, optionally gathered into one
+ * device's buffer in the same kernels. Rank r (of nranks) computes its rows with per_rank[r] (every
+ * pointer on devices[r]) on streams[r] (NULL: that device's default stream). With gather == 0
+ * each rank writes its own per_rank[r].c. With gather != 0, per_rank[r].c and .ldc are ignored:
+ * rank r's epilogue stores its rows straight into `gathered` (an [sum of m, n] buffer with row
+ * stride ld_gathered on devices[root]) at row offset sum_{q<r} per_rank[q].m — the ranks on other
+ * GPUs write over NVLink (peer access is enabled here), so the gather needs no extra kernel or
+ * collective — and streams[root] waits for every rank, so work queued on it after this call sees
+ * the whole C. The reference has no multi-device path (its GEMM runs on one device); this is the
+ * row-block partition plus the gather that a single-device result needs, in place of an NCCL
+ * all-gather of C. Returns once every launch is queued; the caller's current device is kept. */
+int mfk_sharded_gemm_f32(const mfk_gemm_desc* per_rank, int32_t nranks, const int32_t* devices,
+                         void* const* streams, int32_t gather, int32_t root, float* gathered,
+                         int64_t ld_gathered);
+
+/* Device memory shared between processes (one process per GPU), so a rank's GEMM can write its
+ * rows into another rank's buffer over NVLink: mfk_ipc_get_handle returns the IPC handle of the
+ * allocation holding `ptr` (MFK_IPC_HANDLE_BYTES bytes into `handle`) and ptr's byte offset in it;
+ * mfk_ipc_open_handle maps a handle from another process on the current device (peer access
+ * enabled) and returns the allocation's base; mfk_ipc_close_handle unmaps it. No counterpart in
+ * the reference (single process). */
+#define MFK_IPC_HANDLE_BYTES 64
+int mfk_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
+int mfk_ipc_open_handle(const void* handle, void** base);
+int mfk_ipc_close_handle(void* base);
+
 /* gemm_strided_batched on CUDA. Replaces the OpId::GemmBatched kernel (CPU adapter:
  * src/backends/cpu/backend.cpp:239-293 -> cpu::gemm_batched_f32_parallel, gemm_batched.cpp:58)
  * and so both batched GEMMs of attention (src/ops/attention.cpp:69, :97). desc->m/n/k describe

@@ -22,6 +22,7 @@ MFK_ERR_NO_DEVICE = 5
 MFK_ERR_DEVICE_FAULT = 6
 MFK_ERR_SCRATCH_LIMIT = 7
 NOALLOC_SCRATCH_BYTES = 64 * 1024 * 1024
+IPC_HANDLE_BYTES = 64
 
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_GELU_TANH = 0, 1, 2, 3
 PRECISION_DEFAULT, PRECISION_3XTF32, PRECISION_1XTF32 = -1, 0, 1
@@ -31,6 +32,10 @@ EXPORTED = (
     "mfk_gemm_f32",
     "mfk_gemm_f32_noalloc",
     "mfk_gemm_strided_batched_f32",
+    "mfk_sharded_gemm_f32",
+    "mfk_ipc_get_handle",
+    "mfk_ipc_open_handle",
+    "mfk_ipc_close_handle",
     "mfk_pack_b_f32",
     "mfk_packed_b_shape",
     "mfk_packed_b_free",
@@ -114,6 +119,12 @@ def lib() -> ctypes.CDLL:
             so.mfk_gemm_f32_noalloc.argtypes = [ctypes.POINTER(GemmDesc), vp]
             so.mfk_gemm_strided_batched_f32.argtypes = [ctypes.POINTER(GemmDesc),
                                                         ctypes.POINTER(BatchDesc), vp]
+            so.mfk_sharded_gemm_f32.argtypes = [ctypes.POINTER(GemmDesc), i32,
+                                                ctypes.POINTER(i32), ctypes.POINTER(vp), i32,
+                                                i32, vp, i64]
+            so.mfk_ipc_get_handle.argtypes = [vp, vp, ctypes.POINTER(i64)]
+            so.mfk_ipc_open_handle.argtypes = [vp, ctypes.POINTER(vp)]
+            so.mfk_ipc_close_handle.argtypes = [vp]
             so.mfk_pack_b_f32.argtypes = [vp, i64, i64, i64, i64, i32, vp,
                                           ctypes.POINTER(ctypes.c_void_p)]
             so.mfk_packed_b_shape.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64),

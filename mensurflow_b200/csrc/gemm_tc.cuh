@@ -76,6 +76,7 @@ struct GemmArgs {
     int act;
     int tma_store;     // 1: C is written by TMA stores through shared memory (tmC is valid)
     int raw_hi;        // ASPLIT: the MMA reads raw A as hi (truncating), write only lo
+    int c_peer;        // C lies in another GPU's memory: the epilogue's stores cross NVLink
 };
 
 // CG: CTAs per MMA (1 or 2). BN: N of one MMA (columns of the tile). Per CTA: kBM rows of A,
@@ -618,6 +619,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     using C = TcConfig<CG, BN, SPLIT3, ATMEM>;
     constexpr int kHalf = BN / (C::kEpiWarpsC / 4);  // columns per warp
     constexpr int kChunks = kHalf / kEpiCols;
+    static_assert(kChunks % 2 == 0, "the peer-store path writes chunks in pairs");
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int ew = warp % 4;                            // TMEM lane quarter this warp may access
@@ -688,6 +690,14 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                         bulk_commit();
                     }
                     box ^= 1;
+                } else if (g.c_peer) {
+                    // stage the chunk (box ci & 1); the pair is written below as 128-byte rows
+                    const uint32_t buf = box0 + (ci & 1) * C::kEpiBoxBytes;
+#pragma unroll
+                    for (int q = 0; q < kEpiCols / 4; ++q) {
+                        st_shared_v4(buf + lane * (kEpiCols * 4) + ((q ^ ((lane >> 1) & 3)) << 4),
+                                     v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    }
                 } else if (row_ok) {
                     if (col0 + kEpiCols <= g.n && vec_out) {
 #pragma unroll
@@ -702,6 +712,40 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                         }
                     }
                 }
+            }
+            if (g.c_peer && (ci & 1)) {
+                // C in another GPU's memory: every request crosses NVLink, so the two staged
+                // chunks (32 columns) go out as full 128-byte row segments — eight lanes per row,
+                // four rows per store instruction — instead of one 16-byte piece per lane.
+                const int pair0 = col0 - kEpiCols;
+                __syncwarp();
+                if (pair0 < g.n && row0 < g.m) {
+                    const int c4 = lane & 7;
+#pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        const int r = it * 4 + (lane >> 3);
+                        const int q = c4 & 3;
+                        const float4 val = ld_shared_v4(box0 + (c4 >> 2) * C::kEpiBoxBytes +
+                                                        r * (kEpiCols * 4) +
+                                                        ((q ^ ((r >> 1) & 3)) << 4));
+                        const int grow = row0 + r;
+                        const int gcol = pair0 + c4 * 4;
+                        if (grow < g.m) {
+                            float* dst = g.c + static_cast<long long>(tc.b) * g.c_bs +
+                                         static_cast<long long>(grow) * g.ldc + gcol;
+                            if (gcol + 4 <= g.n && vec_out) {
+                                *reinterpret_cast<float4*>(dst) = val;
+                            } else {
+                                const float e4[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    if (gcol + j < g.n) dst[j] = e4[j];
+                                }
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
             }
             if (ci + 1 < kChunks) tmem_ld_wait();
         }
@@ -721,6 +765,9 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     }
     // Stores must have finished reading shared memory (and landed) before the CTA exits.
     if (g.tma_store && lane == 0) bulk_wait<0>();
+    // Stores into a peer GPU's memory are performed at system scope before the kernel ends, so
+    // whatever the other GPU orders after this kernel (an event wait, a collective) sees them.
+    if (g.c_peer) __threadfence_system();
     __syncwarp();
 }
 

@@ -594,12 +594,24 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     g.group_m = cg == 2 ? 8 : 12;
     g.num_tiles = static_cast<long long>(batch) * g.tiles_m * g.tiles_n;
 
-    // C through TMA stores when its layout allows (16-byte aligned rows and matrices).
+    // C through TMA stores when its layout allows (16-byte aligned rows and matrices) and it lies
+    // in this GPU's memory. C on another GPU (the gather target of a sharded product, reached over
+    // NVLink) is written with plain stores from the epilogue: no tensor map covers peer memory.
+    bool c_local = true;
+    {
+        cudaPointerAttributes pa{};
+        if (cudaPointerGetAttributes(&pa, d->c) == cudaSuccess) {
+            c_local = pa.type != cudaMemoryTypeDevice || pa.device == dev;
+        } else {
+            cudaGetLastError();
+        }
+    }
     CUtensorMap mc;
     std::memset(&mc, 0, sizeof(mc));
-    const bool c_ok = aligned16(d->c) && d->ldc % 4 == 0 && (batch == 1 || g.c_bs % 4 == 0) &&
+    const bool c_ok = c_local && aligned16(d->c) && d->ldc % 4 == 0 && (batch == 1 || g.c_bs % 4 == 0) &&
                       d->ldc < (int64_t(1) << 37) && g.c_bs >= 0 && g.c_bs < (int64_t(1) << 37);
     g.tma_store = (c_ok && make_store_map(&mc, d->c, d->n, d->m, batch, d->ldc, g.c_bs)) ? 1 : 0;
+    g.c_peer = c_local ? 0 : 1;
 
     // 3xTF32 with A read in place: the kernel splits A in shared memory.
     const bool asplit = split3 && A.direct;
@@ -648,6 +660,115 @@ int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream) {
         scratch.ptr = static_cast<uint8_t*>(info->noalloc_scratch);
     }
     return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream), &scratch);
+}
+
+int mfk_sharded_gemm_f32(const mfk_gemm_desc* per_rank, int32_t nranks, const int32_t* devices,
+                         void* const* streams, int32_t gather, int32_t root, float* gathered,
+                         int64_t ld_gathered) {
+    if (per_rank == nullptr || devices == nullptr || streams == nullptr || nranks < 1)
+        return MFK_ERR_INVALID_ARGUMENT;
+    int count = 0;
+    MFK_CUDA(cudaGetDeviceCount(&count));
+    for (int r = 0; r < nranks; ++r) {
+        if (devices[r] < 0 || devices[r] >= count) return MFK_ERR_INVALID_ARGUMENT;
+        const int rc = check_desc(&per_rank[r]);
+        if (rc != MFK_OK) return rc;
+        if (per_rank[r].n != per_rank[0].n) return MFK_ERR_INVALID_ARGUMENT;
+    }
+    if (gather) {
+        if (root < 0 || root >= nranks || gathered == nullptr || ld_gathered < per_rank[0].n)
+            return MFK_ERR_INVALID_ARGUMENT;
+    }
+    int caller_device = 0;
+    MFK_CUDA(cudaGetDevice(&caller_device));
+    struct Restore {
+        int dev;
+        ~Restore() { cudaSetDevice(dev); }
+    } restore{caller_device};
+    const int root_dev = gather ? devices[root] : 0;
+    int64_t row0 = 0;
+    for (int r = 0; r < nranks; ++r) {
+        mfk_gemm_desc d = per_rank[r];
+        MFK_CUDA(cudaSetDevice(devices[r]));
+        if (gather) {
+            d.c = gathered + row0 * ld_gathered;
+            d.ldc = ld_gathered;
+            if (devices[r] != root_dev) {
+                int can = 0;
+                MFK_CUDA(cudaDeviceCanAccessPeer(&can, devices[r], root_dev));
+                if (!can) {
+                    t_cuda_error = "the gather target's GPU is not reachable as a peer";
+                    return MFK_ERR_UNSUPPORTED;
+                }
+                const cudaError_t e = cudaDeviceEnablePeerAccess(root_dev, 0);
+                if (e == cudaErrorPeerAccessAlreadyEnabled) {
+                    cudaGetLastError();
+                } else if (e != cudaSuccess) {
+                    return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+                }
+            }
+        }
+        const int rc = run_gemm(&d, nullptr, static_cast<cudaStream_t>(streams[r]), nullptr);
+        if (rc != MFK_OK) return rc;
+        row0 += d.m;
+    }
+    if (gather) {
+        // The gathered C is complete on the root's stream once every rank's GEMM has finished.
+        for (int r = 0; r < nranks; ++r) {
+            if (r == root || streams[r] == streams[root]) continue;
+            MFK_CUDA(cudaSetDevice(devices[r]));
+            cudaEvent_t ev;
+            MFK_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+            cudaError_t e = cudaEventRecord(ev, static_cast<cudaStream_t>(streams[r]));
+            if (e == cudaSuccess) {
+                cudaSetDevice(root_dev);
+                e = cudaStreamWaitEvent(static_cast<cudaStream_t>(streams[root]), ev, 0);
+            }
+            cudaEventDestroy(ev);
+            if (e != cudaSuccess) return cuda_fail(e, "cross-device stream wait");
+        }
+    }
+    return MFK_OK;
+}
+
+int mfk_ipc_get_handle(const void* ptr, void* handle, int64_t* offset) {
+    if (ptr == nullptr || handle == nullptr || offset == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    static PFN_cuMemGetAddressRange_v3020 range_fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) !=
+                cudaSuccess || q != cudaDriverEntryPointSuccess) {
+            return static_cast<PFN_cuMemGetAddressRange_v3020>(nullptr);
+        }
+        return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+    }();
+    if (range_fn == nullptr) return MFK_ERR_UNSUPPORTED;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+        t_cuda_error = "cuMemGetAddressRange: not a device allocation";
+        return MFK_ERR_INVALID_ARGUMENT;
+    }
+    cudaIpcMemHandle_t h;
+    MFK_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    static_assert(sizeof(h) == MFK_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+    return MFK_OK;
+}
+
+int mfk_ipc_open_handle(const void* handle, void** base) {
+    if (handle == nullptr || base == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    MFK_CUDA(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess));
+    return MFK_OK;
+}
+
+int mfk_ipc_close_handle(void* base) {
+    if (base == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    MFK_CUDA(cudaIpcCloseMemHandle(base));
+    return MFK_OK;
 }
 
 int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc* batch,

@@ -177,3 +177,22 @@ def test_contiguous_and_to_refuse_cpu_tensors_like_the_dispatcher():
     y = torch.zeros(3, 4)
     assert mf.contiguous(y) is y  # already contiguous: returned as is, as the reference does
     assert mf.to(y, "cpu") is y
+
+
+def test_sharded_argument_checks_without_a_device():
+    from mensurflow_b200 import sharded
+
+    so = _lib.lib()
+    descs = (_lib.GemmDesc * 2)()
+    devs = (ctypes.c_int32 * 2)(0, 0)
+    streams = (ctypes.c_void_p * 2)()
+    assert so.mfk_sharded_gemm_f32(descs, 0, devs, streams, 0, 0, None, 0) == \
+        _lib.MFK_ERR_INVALID_ARGUMENT
+    assert so.mfk_sharded_gemm_f32(None, 2, devs, streams, 0, 0, None, 0) == \
+        _lib.MFK_ERR_INVALID_ARGUMENT
+    assert so.mfk_ipc_get_handle(None, None, None) == _lib.MFK_ERR_INVALID_ARGUMENT
+    assert so.mfk_ipc_open_handle(None, None) == _lib.MFK_ERR_INVALID_ARGUMENT
+    assert so.mfk_ipc_close_handle(None) == _lib.MFK_ERR_INVALID_ARGUMENT
+    # gather="peer" needs the mapped buffer of C
+    with pytest.raises(ValueError):
+        sharded.sharded_gemm(torch.zeros(4, 3), torch.zeros(3, 2), 4, gather="peer")
