@@ -168,8 +168,7 @@ def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activa
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, pin_memory=True)
     compute = torch.cuda.current_stream(dev)
-    copy_in = torch.cuda.Stream(dev)
-    copy_out = torch.cuda.Stream(dev)
+    copy_in, copy_out = _copy_streams(dev)
     copy_in.wait_stream(compute)
     with torch.cuda.stream(copy_in):
         d_b = b.to(dev, non_blocking=True)
@@ -212,6 +211,16 @@ def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activa
             t.record_stream(copy_in)
     copy_out.synchronize()
     return out
+
+
+_COPY_STREAMS = {}
+
+
+def _copy_streams(dev: torch.device):
+    """The two copy streams of the host-tensor path on `dev` (made once per device)."""
+    if dev not in _COPY_STREAMS:
+        _COPY_STREAMS[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _COPY_STREAMS[dev]
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch.Tensor] = None,
