@@ -52,6 +52,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--size", type=int, default=8192,
                    help="c2 only: M = N = K per rank (profiling captures use a smaller case)")
+    p.add_argument("--heads", type=int, default=512,
+                   help="c4 only: batch x heads (512 in the config; profiling captures use fewer)")
     p.add_argument("--view", choices=["transpose", "slice", "stepped"], default="transpose",
                    help="copy only: the packed view (transposed; a column slice of a wider "
                         "matrix, read as 16-byte rows; every other column, a gather)")
@@ -367,14 +369,14 @@ def main():
             h = mf.linear(X, W1, b1, "gelu", precision=args.precision)
             mf.linear(h, W2, b2, precision=args.precision)
     elif args.workload == "c4":
-        heads_total, seq, dh = 32 * 16, 2048, 128
+        heads_total, seq, dh = args.heads, 2048, 128
         if heads_total % world:
-            raise SystemExit("c4: world size must divide 512")
+            raise SystemExit("c4: world size must divide the number of heads")
         bh = heads_total // world                # batch x heads split over ranks
         m, n, k = seq, seq, dh
         scaling = "strong"
         scale = float(1.0 / dh ** 0.5)
-        wl = (f"C4: attention GEMMs S = Q@K^T/sqrt(128) and O = P@V, batch*heads=512 split "
+        wl = (f"C4: attention GEMMs S = Q@K^T/sqrt(128) and O = P@V, batch*heads={heads_total} split "
               f"over ranks ({bh} per rank), seq 2048, head_dim 128; P is a stand-in of S's shape "
               f"(softmax is not on the timed path)")
         std = 1.0 / dh ** 0.5

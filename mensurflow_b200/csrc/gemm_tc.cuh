@@ -77,6 +77,18 @@ struct GemmArgs {
     int tma_store;     // 1: C is written by TMA stores through shared memory (tmC is valid)
     int raw_hi;        // ASPLIT: the MMA reads raw A as hi (truncating), write only lo
     int c_peer;        // C lies in another GPU's memory: the epilogue's stores cross NVLink
+    // Stream-K tail (sk_units > 0): tiles [0, dp_tiles) go whole to the units in turn; the
+    // k-iterations of tiles [dp_tiles, num_tiles) are split evenly over all sk_units units
+    // (unit u: sk_q + 1 iterations if u < sk_r, else sk_q). The unit holding a split tile's first
+    // k-blocks finishes it: every other part writes its raw accumulator to its unit's slot of
+    // sk_part and counts itself in sk_count; the finisher waits for the count, sums the parts in
+    // k order and runs the epilogue.
+    int sk_units;
+    long long dp_tiles;
+    long long sk_q;
+    int sk_r;
+    float* sk_part;    // [unit][CG][kBM * BN] floats
+    int* sk_count;     // [(num_tiles - dp_tiles) * CG * epilogue warps], zero at launch
 };
 
 // CG: CTAs per MMA (1 or 2). BN: N of one MMA (columns of the tile). Per CTA: kBM rows of A,
@@ -251,6 +263,59 @@ __device__ __forceinline__ long long tile_step() {
     return gridDim.x / CG;
 }
 
+// One piece of a unit's work: k-blocks [kb0, kb1) of tile `tile`.
+struct Work {
+    long long tile;
+    int kb0, kb1;
+};
+
+// First stream-K iteration of unit u, and the unit that owns iteration `it`.
+__device__ __forceinline__ long long sk_start(const GemmArgs& g, long long u) {
+    return u * g.sk_q + min(u, static_cast<long long>(g.sk_r));
+}
+
+__device__ __forceinline__ long long sk_unit_of(const GemmArgs& g, long long it) {
+    const long long big = static_cast<long long>(g.sk_r) * (g.sk_q + 1);
+    if (it < big || g.sk_q == 0) return it / (g.sk_q + 1);
+    return g.sk_r + (it - big) / g.sk_q;
+}
+
+// The same sequence of work for every role of a CTA: this unit's share of the stream-K
+// iterations (cut at tile boundaries) first, then its whole tiles — so the summing of a split
+// tile's parts in the epilogue overlaps the MMAs of the whole tiles that follow.
+template <int CG>
+struct WorkIter {
+    long long t, it, it_end;
+    __device__ __forceinline__ explicit WorkIter(const GemmArgs& g) {
+        t = first_tile<CG>();
+        it = it_end = 0;
+        if (g.sk_units > 0) {
+            const long long u = blockIdx.x / CG;
+            it = sk_start(g, u);
+            it_end = sk_start(g, u + 1);
+        }
+    }
+    __device__ __forceinline__ bool next(const GemmArgs& g, Work& w) {
+        if (it < it_end) {
+            const long long tr = it / g.num_kb;
+            w.tile = g.dp_tiles + tr;
+            w.kb0 = static_cast<int>(it - tr * g.num_kb);
+            w.kb1 = static_cast<int>(min(static_cast<long long>(g.num_kb), w.kb0 + (it_end - it)));
+            it += w.kb1 - w.kb0;
+            return true;
+        }
+        const long long dp_end = g.sk_units > 0 ? g.dp_tiles : g.num_tiles;
+        if (t < dp_end) {
+            w.tile = t;
+            w.kb0 = 0;
+            w.kb1 = g.num_kb;
+            t += tile_step<CG>();
+            return true;
+        }
+        return false;
+    }
+};
+
 // ASPLIT (3xTF32 only): A arrives as raw fp32 in the A_hi slot, completing on this CTA's own
 // a_full barrier, and the converter warps write hi and lo (in shared memory, or for ATMEM into
 // tensor memory); B arrives pre-split.
@@ -267,13 +332,14 @@ __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap
     constexpr uint32_t kFullBytes = ASPLIT ? 2 * C::kBBytes : C::kStageBytes;
     int stage = 0;
     uint32_t phase = 0;
-    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
-        const TileCoord tc = tile_coord(g, t);
+    WorkIter<CG> wi(g);
+    for (Work w; wi.next(g, w);) {
+        const TileCoord tc = tile_coord(g, w.tile);
         const int za = g.a_batch_bcast ? 0 : tc.b;
         const int zb = g.b_batch_bcast ? 0 : tc.b;
         const int ya = tc.tm * C::kTileM + static_cast<int>(rank) * kBM;
         const int yb = tc.tn * BN + static_cast<int>(rank) * C::kBRows;
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, kErrProducerWait)) return;
             uint8_t* s = stages + stage * C::kStageBytes;
             uint8_t* s_ahi = s;
@@ -326,8 +392,9 @@ __device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, u
     const int lane = threadIdx.x % 32;
     int stage = 0;
     uint32_t phase = 0;
-    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+    WorkIter<CG> wi(g);
+    for (Work w; wi.next(g, w);) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
             if (!mbar_wait(&a_full[stage], phase, kErrConvertWait)) return;
             float4* hi = reinterpret_cast<float4*>(stages + stage * C::kStageBytes);
             float4* lo = reinterpret_cast<float4*>(stages + stage * C::kStageBytes + C::kABytes +
@@ -391,8 +458,11 @@ __device__ __forceinline__ void tc_convert_tmem(const GemmArgs& g, uint8_t* stag
     const int q = warp % 4;
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    const long long total = (g.num_tiles - first_tile<CG>() + tile_step<CG>() - 1) /
-                            tile_step<CG>() * g.num_kb;
+    long long total = 0;  // k-blocks in this CTA's whole sequence of work
+    {
+        WorkIter<CG> wi(g);
+        for (Work w; wi.next(g, w);) total += w.kb1 - w.kb0;
+    }
     // k-block i of this CTA's sequence uses stage i % kStages and slot i % kASlots
     for (long long i = group; i < total; i += 2) {
         {
@@ -459,11 +529,12 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
     int slot = 0;             // ATMEM: the TMEM ring slot holding this k-block's A (hi, lo)
     uint32_t tphase = 0;
     const uint32_t stage0 = smem_u32(stages);
-    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
+    WorkIter<CG> wi(g);
+    for (Work w; wi.next(g, w);) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kErrMmaWait)) return;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
             if (!mbar_wait(&full[stage], phase, kErrMmaWait)) return;
             if constexpr (ATMEM) {
                 if (!mbar_wait(&converted[slot], tphase, kErrMmaWait)) return;
@@ -485,7 +556,7 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
                     const uint64_t dbl = smem_desc(b_lo + koff, 16, 1024, kSwizzle128B);
                     const uint32_t tah = ta + ks * 8;
                     const uint32_t tal = tah + 32;
-                    const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
+                    const uint32_t accumulate = (kb > w.kb0 || ks > 0) ? 1u : 0u;
                     if constexpr (CG == 1) {
                         mma_tf32_ts(d_tmem, tal, dbh, idesc, accumulate);
                         mma_tf32_ts(d_tmem, tah, dbl, idesc, 1u);
@@ -513,7 +584,7 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
                     const uint32_t koff = ks * 32;  // 8 tf32 = 32 bytes along the swizzled row
                     const uint64_t dah = smem_desc(a_hi + koff, 16, 1024, kSwizzle128B);
                     const uint64_t dbh = smem_desc(b_hi + koff, 16, 1024, kSwizzle128B);
-                    const uint32_t accumulate = (kb > 0 || ks > 0) ? 1u : 0u;
+                    const uint32_t accumulate = (kb > w.kb0 || ks > 0) ? 1u : 0u;
                     if constexpr (SPLIT3) {
                         const uint64_t dal = smem_desc(a_lo + koff, 16, 1024, kSwizzle128B);
                         const uint64_t dbl = smem_desc(b_lo + koff, 16, 1024, kSwizzle128B);
@@ -555,6 +626,66 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
             acc_phase ^= 1u;
         }
     }
+}
+
+// This warp's block of unit u's stream-K slot (kBM x BN floats per CTA rank): warp (half, ew)'s
+// chunk ci is a 2 KB block at ((half*kChunks + ci)*4 + ew) * 512 floats, stored as four 512-byte
+// rows of float4 (float4 q of lane l at q*32 + l), so each warp instruction moves 512 contiguous
+// bytes.
+template <int CG, int BN>
+__device__ __forceinline__ float4* sk_part_block(const GemmArgs& g, long long u, uint32_t rank,
+                                                 int half, int ew, int ci, int kChunks) {
+    float* base = g.sk_part + (u * CG + rank) * static_cast<long long>(kBM * BN);
+    return reinterpret_cast<float4*>(
+        base + ((static_cast<long long>(half) * kChunks + ci) * 4 + ew) * 512);
+}
+
+// The finisher of stream-K tile tr (unit u_first, which holds the first k-blocks) replaces its
+// own part in TMEM with the sum over every part, added in k order (its own first), so the
+// result does not depend on timing; the regular epilogue then reads the tile from TMEM as
+// usual. Chunk by chunk: the own part from TMEM, the others' loads of a pair in flight together.
+template <int CG, int BN, int kChunks>
+__device__ __forceinline__ void sk_fixup_tmem(const GemmArgs& g, uint32_t tbase,
+                                              long long u_first, long long u_last, uint32_t rank,
+                                              int half, int ew, int lane) {
+    constexpr int kGroup = 2;
+#pragma unroll 1
+    for (int ci = 0; ci < kChunks; ++ci) {
+        uint32_t own[kEpiCols];
+        tmem_ld_issue_32x32b_x16(tbase + ci * kEpiCols, own);
+        tmem_ld_wait();
+        float sum[kEpiCols];
+#pragma unroll
+        for (int j = 0; j < kEpiCols; ++j) sum[j] = __uint_as_float(own[j]);
+#pragma unroll 1
+        for (long long v0 = u_first + 1; v0 <= u_last; v0 += kGroup) {
+            float4 part[kGroup][kEpiCols / 4];
+#pragma unroll
+            for (int p = 0; p < kGroup; ++p) {
+                if (v0 + p <= u_last) {
+                    const float4* src = sk_part_block<CG, BN>(g, v0 + p, rank, half, ew, ci, kChunks);
+#pragma unroll
+                    for (int q = 0; q < kEpiCols / 4; ++q) part[p][q] = __ldcg(src + q * 32 + lane);
+                }
+            }
+#pragma unroll
+            for (int p = 0; p < kGroup; ++p) {
+                if (v0 + p <= u_last) {
+#pragma unroll
+                    for (int q = 0; q < kEpiCols / 4; ++q) {
+                        sum[4 * q] = __fadd_rn(sum[4 * q], part[p][q].x);
+                        sum[4 * q + 1] = __fadd_rn(sum[4 * q + 1], part[p][q].y);
+                        sum[4 * q + 2] = __fadd_rn(sum[4 * q + 2], part[p][q].z);
+                        sum[4 * q + 3] = __fadd_rn(sum[4 * q + 3], part[p][q].w);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kEpiCols; ++j) own[j] = __float_as_uint(sum[j]);
+        tmem_st_32x32b_x16(tbase + ci * kEpiCols, own);
+    }
+    tmem_st_wait();
 }
 
 // The epilogue of one kEpiCols-column chunk of a thread's row: alpha, beta*C_in, bias,
@@ -638,8 +769,11 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     int box = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (long long t = first_tile<CG>(); t < g.num_tiles; t += tile_step<CG>()) {
-        const TileCoord tc = tile_coord(g, t);
+    const int wid = warp - C::kEpiWarp0C;
+    const long long me = blockIdx.x / CG;
+    WorkIter<CG> wi(g);
+    for (Work w; wi.next(g, w);) {
+        const TileCoord tc = tile_coord(g, w.tile);
         if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) break;
         tc_fence_after();
         const int row0 = tc.tm * C::kTileM + static_cast<int>(rank) * kBM + ew * 32;
@@ -652,6 +786,69 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                               : nullptr;
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
                                static_cast<uint32_t>(acc * BN + half * kHalf);
+        // A stream-K part of a tile. Parts after the first k-blocks: this warp's raw accumulator
+        // goes to the unit's slot and is counted; the tile's first part (its unit reaches the
+        // tile last, at the end of its share) waits for the count, then sums all parts.
+        if (w.kb0 != 0 || w.kb1 != g.num_kb) {
+            const long long tr = w.tile - g.dp_tiles;
+            const long long u_first = sk_unit_of(g, tr * g.num_kb);
+            const long long u_last = sk_unit_of(g, (tr + 1) * g.num_kb - 1);
+            int* count = &g.sk_count[(tr * CG + rank) * C::kEpiWarpsC + wid];
+            if (w.kb0 != 0) {
+#pragma unroll 1
+                for (int ci = 0; ci < kChunks; ci += 2) {
+                    uint32_t r0[kEpiCols], r1[kEpiCols];
+                    tmem_ld_issue_32x32b_x16(tbase + ci * kEpiCols, r0);
+                    tmem_ld_issue_32x32b_x16(tbase + (ci + 1) * kEpiCols, r1);
+                    tmem_ld_wait();
+                    float4* d0 = sk_part_block<CG, BN>(g, me, rank, half, ew, ci, kChunks);
+                    float4* d1 = sk_part_block<CG, BN>(g, me, rank, half, ew, ci + 1, kChunks);
+#pragma unroll
+                    for (int q = 0; q < kEpiCols / 4; ++q) {
+                        __stcg(d0 + q * 32 + lane,
+                               make_float4(__uint_as_float(r0[4 * q]), __uint_as_float(r0[4 * q + 1]),
+                                           __uint_as_float(r0[4 * q + 2]), __uint_as_float(r0[4 * q + 3])));
+                        __stcg(d1 + q * 32 + lane,
+                               make_float4(__uint_as_float(r1[4 * q]), __uint_as_float(r1[4 * q + 1]),
+                                           __uint_as_float(r1[4 * q + 2]), __uint_as_float(r1[4 * q + 3])));
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(count, 1);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (CG == 1) {
+                        mbar_arrive(&acc_empty[acc]);
+                    } else {
+                        mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+                    }
+                }
+                if (++acc == C::kAccStages) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+                continue;
+            }
+            // the finisher: every later part of the tile has been written (bounded wait)
+            if (lane == 0) {
+                const int want = static_cast<int>(u_last - u_first);
+                if (atomicAdd(count, 0) < want) {
+                    const uint64_t start = global_timer();
+                    while (atomicAdd(count, 0) < want) {
+                        if (error_raised() || global_timer() - start > MFK_WAIT_LIMIT_NS) {
+                            raise_error(kErrEpilogueWait);
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+                }
+                __threadfence();
+            }
+            __syncwarp();
+            sk_fixup_tmem<CG, BN, kChunks>(g, tbase, u_first, u_last, rank, half, ew, lane);
+        }
         // Two register sets: the next chunk's TMEM load is in flight while this one is used.
         uint32_t ra[kEpiCols], rb[kEpiCols];
         tmem_ld_issue_32x32b_x16(tbase, ra);

@@ -249,8 +249,9 @@ constexpr int64_t kInKernelSplitMaxN = 384;
 // set-up flags.
 template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM = false>
 int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
-              const CUtensorMap& b1, const CUtensorMap& cmap, const GemmArgs& g, DeviceInfo* info,
-              int slot, cudaStream_t stream) {
+              const CUtensorMap& b1, const CUtensorMap& cmap, const GemmArgs& g_in,
+              DeviceInfo* info, int slot, cudaStream_t stream, bool allow_sk) {
+    GemmArgs g = g_in;
     using C = mfk::TcConfig<CG, BN, SPLIT3, ATMEM>;
     auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3, ASPLIT, ATMEM>;
     cudaLaunchConfig_t cfg = {};
@@ -285,7 +286,48 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
             info->smem_set[slot] = true;
         }
     }
-    const long long units = std::min<long long>(g.num_tiles, info->resident_units[slot]);
+    const long long resident = info->resident_units[slot];
+    long long units = std::min<long long>(g.num_tiles, resident);
+    // Stream-K tail: when the last wave of tiles would leave many units idle (under 92% of the
+    // units busy on average), the tiles of that wave are shared by k-iterations across every
+    // unit instead. Each extra part of a tile costs one round trip of a kBM x BN accumulator
+    // through L2, so the share per unit must be at least four k-blocks. All units are resident
+    // at once (the grid is the occupancy), so a tile's finisher never waits on a unit that has
+    // not started. Measured on B200, it pays in 3xTF32 when whole waves come first (the summing
+    // of split tiles overlaps their MMAs: 4096 x 4096 x 1024, 127.5 -> 118.5 us) or when the
+    // tiles fill at most half the units (1024^3: 39.4 -> 33.8 us), and not otherwise: with every
+    // SM streaming tf32 operands, 1xTF32 is short of L2 bandwidth (4096 x 1024 x 4096: 53 -> 63
+    // us), and a tail that is the whole problem leaves the summing exposed (138 -> 145 us).
+    struct SkWorkspace {
+        void* p = nullptr;
+        cudaStream_t s;
+        ~SkWorkspace() {
+            if (p) cudaFreeAsync(p, s);
+        }
+    } sk{nullptr, stream};
+    if (allow_sk && resident > 0 && g.num_tiles % resident != 0 && g.num_tiles < 16 * resident) {
+        const long long waves = g.num_tiles / resident;
+        const long long rem = g.num_tiles % resident;
+        const double busy = static_cast<double>(g.num_tiles) /
+                            static_cast<double>((waves + 1) * resident);
+        const long long iters = rem * g.num_kb;
+        if (SPLIT3 && busy < 0.92 && iters >= 4 * resident &&
+            (waves >= 1 || 2 * g.num_tiles <= resident)) {
+            const size_t part_bytes =
+                static_cast<size_t>(resident) * CG * mfk::kBM * BN * sizeof(float);
+            const size_t count_bytes = static_cast<size_t>(rem) * CG * C::kEpiWarpsC * sizeof(int);
+            MFK_CUDA(cudaMallocAsync(&sk.p, part_bytes + count_bytes, stream));
+            MFK_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(sk.p) + part_bytes, 0, count_bytes,
+                                     stream));
+            g.sk_units = static_cast<int>(resident);
+            g.dp_tiles = waves * resident;
+            g.sk_q = iters / resident;
+            g.sk_r = static_cast<int>(iters % resident);
+            g.sk_part = static_cast<float*>(sk.p);
+            g.sk_count = reinterpret_cast<int*>(static_cast<uint8_t*>(sk.p) + part_bytes);
+            units = resident;
+        }
+    }
     cfg.gridDim = dim3(static_cast<unsigned>(units * CG), 1, 1);
     {
         TimedLaunch timed(stream);
@@ -617,22 +659,22 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     const bool asplit = split3 && A.direct;
     g.raw_hi = raw_hi ? 1 : 0;
     if (cg == 2 && BN == 256) {
-        if (asplit) return launch_tc<2, 256, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 6, stream);
-        return split3 ? launch_tc<2, 256, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 0, stream)
-                      : launch_tc<2, 256, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 1, stream);
+        if (asplit) return launch_tc<2, 256, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 6, stream, fixed == nullptr);
+        return split3 ? launch_tc<2, 256, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 0, stream, fixed == nullptr)
+                      : launch_tc<2, 256, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 1, stream, fixed == nullptr);
     }
     // N <= 128 with A split in place: the split goes to tensor memory (ATMEM), which leaves
     // shared memory to the B tiles and the raw A stages.
     if (cg == 2) {
         if (asplit) {
-            return launch_tc<2, 128, true, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 9, stream);
+            return launch_tc<2, 128, true, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 9, stream, fixed == nullptr);
         }
-        return split3 ? launch_tc<2, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 2, stream)
-                      : launch_tc<2, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 3, stream);
+        return split3 ? launch_tc<2, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 2, stream, fixed == nullptr)
+                      : launch_tc<2, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 3, stream, fixed == nullptr);
     }
-    if (asplit) return launch_tc<1, 128, true, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 10, stream);
-    return split3 ? launch_tc<1, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 4, stream)
-                  : launch_tc<1, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 5, stream);
+    if (asplit) return launch_tc<1, 128, true, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 10, stream, fixed == nullptr);
+    return split3 ? launch_tc<1, 128, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 4, stream, fixed == nullptr)
+                  : launch_tc<1, 128, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 5, stream, fixed == nullptr);
 }
 
 }  // namespace

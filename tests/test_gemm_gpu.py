@@ -426,3 +426,51 @@ def test_host_tensors_with_gpu_execution(cuda, trans):
     with pytest.raises(NotImplementedError):
         mf.gemm(ha, hb, transpose_a=ta, transpose_b=tb)  # "auto" on host data: no CPU kernel here
     no_fault()
+
+
+# Shapes whose last wave of tiles would leave most SM pairs idle, so the kernel shares that
+# wave's k-iterations across every unit (stream-K tail) and sums the parts of a tile in k order:
+# (m, n, k, batch). Covers the pre-split kernel (n > 384), the in-kernel split of A in shared
+# memory (128 < n <= 384) and in tensor memory (n <= 128), the one-CTA kernel (m <= 128), a
+# batch, and the C3 MLP shapes.
+STREAM_K_SHAPES = [(1024, 1024, 1024, 1), (1024, 300, 2048, 1), (2048, 128, 2048, 1),
+                   (100, 1000, 4096, 1), (300, 260, 800, 3), (4096, 4096, 1024, 1),
+                   (4096, 1024, 4096, 1)]
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("shape", STREAM_K_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_tail(cuda, shape, precision):
+    """Seeded inputs against the oracle within the path's bound, with the full epilogue (alpha,
+    beta*C, bias, GELU) applied to the summed parts; the same call twice gives the same bits
+    (the parts are summed in a fixed order, whichever unit finishes last); and quarter-integer
+    inputs stay exact."""
+    m, n, k, batch = shape
+    rng = np.random.default_rng(m + 7 * n + 13 * k + batch)
+    a = rng.standard_normal((batch, m, k)).astype(np.float32)
+    b = rng.standard_normal((batch, k, n)).astype(np.float32)
+    c = rng.standard_normal((batch, m, n)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    ta, tb, tc, tbias = dev(a, cuda), dev(b, cuda), dev(c, cuda), dev(bias, cuda)
+    for i in range(batch):
+        got = mf.gemm(ta[i], tb[i], 0.5, tc[i], 1.0, bias=tbias, activation="gelu",
+                      precision=precision)
+        again = mf.gemm(ta[i], tb[i], 0.5, tc[i], 1.0, bias=tbias, activation="gelu",
+                        precision=precision)
+        assert torch.equal(got, again), "stream-K parts summed in a run-dependent order"
+        want = O.activation(O.gemm(a[i], b[i], 0.5, c[i], 1.0, bias=bias), "gelu")
+        mag = 0.5 * O.abs_product(a[i], b[i]) + np.abs(c[i]) + np.abs(bias)[None, :]
+        rel, ab = tol(precision)
+        assert_close(host(got), want, 1.2 * mag, (rel, ab + 4e-7), f"{shape} [{i}]")
+    if batch > 1:
+        got = mf.gemm_strided_batched(ta, tb, 0.5, tc, 1.0, precision=precision)
+        for i in range(batch):
+            want = O.gemm(a[i], b[i], 0.5, c[i], 1.0)
+            mag = 0.5 * O.abs_product(a[i], b[i]) + np.abs(c[i])
+            assert_close(host(got[i]), want, mag, tol(precision), f"{shape} batched [{i}]")
+    # exact inputs: every partial sum is exact, so the parts add up to the reference's bits
+    qa = (rng.integers(-16, 17, (m, k)) / 4).astype(np.float32)
+    qb = (rng.integers(-16, 17, (k, n)) / 4).astype(np.float32)
+    np.testing.assert_array_equal(host(mf.matmul(dev(qa, cuda), dev(qb, cuda),
+                                                 precision=precision)), O.gemm(qa, qb))
+    no_fault()
