@@ -2,16 +2,20 @@
 """Benchmark of the B200 fp32 GEMM path (the reference's `gemm` + `bias_add` on CUDA).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--precision 3xtf32|1xtf32]
-                    [--impl mine|reference] [--workload c2|c5|gemv]
+                    [--impl mine|reference] [--workload c2|c3|c4|c5|gemv|copy]
 
 Workload ("C2"): per rank, C = 0.5 * A @ B^T + 1.0 * C_in + bias with
 A, B, C_in [8192, 8192] ~ N(0, 1) and bias [8192] ~ U(-0.1, 0.1), fp32 in HBM, one fused call
 per step (3xTF32 by default). Under torchrun every rank owns one 8192-row block of an
 M = 8192*N problem with B and bias replicated, so per-GPU work is fixed ("scaling": "weak") and
 there is no collective on the data path. `value` is the whole-job TFLOP/s (2*M*N*K per step
-summed over ranks, divided by the max-over-ranks device time). The other workloads: `c5`
-(32768 x 32768 x 8192, row blocks split over the ranks: strong scaling) and `gemv`
-(65536 x 8192, HBM-bound).
+summed over ranks, divided by the max-over-ranks device time). The other workloads: `c3` (the
+two-layer MLP forward, `--prepacked` for pre-split weights), `c4` (the two attention GEMMs,
+batch x heads split over the ranks; `--heads` for smaller profiling cases), `c5` (32768 x 32768
+x 8192, row blocks split over the ranks: strong scaling; at N > 1 the gather of C to rank 0 fused
+into the GEMM is timed against NCCL's all-gather), `gemv` (65536 x 8192, HBM-bound) and `copy`
+(Tensor::contiguous of an 8192^2 view on the device, `--view transpose|slice|stepped`).
+Every workload reports the reference's own CPU path on a bounded sample as `cpu_baseline`.
 
 `--impl reference` times the reference's own CPU implementation (the unmodified library built
 from its sources into oracle/_ref) on a bounded row sample of the same workload; rank 0 only.
@@ -190,6 +194,50 @@ def cpu_gemm_sample(m_full, n, k, target_s, reps, warmup=1):
     secs = list(bench.run(0.5, 1.0, True, reps))
     bench.close()
     return secs, rows, "reference", cores
+
+
+def reference_cpu_baseline(args, m, n, k):
+    """The reference's own CPU path (the unmodified library in oracle/_ref, public API, all host
+    threads) on a bounded sample of the workload, in the workload's unit."""
+    from oracle import oracle as O
+
+    ref = O.reference()
+    if ref is None:
+        return None
+    ref.mfref_set_threads(host_threads())
+    cores = int(ref.mfref_max_threads())
+    if args.workload == "c3":
+        secs = O.ref_time_mlp(4096, 1024, 4096, 2, 1, 3)
+        per = float(statistics.median(secs))
+        return {"value": 2.0 * 2 * 4096 * 1024 * 4096 / per / 1e12, "unit": "TFLOP/s",
+                "cores": cores, "kind": "reference",
+                "sample": f"the whole C3 forward (matmul, bias_add, gelu, matmul, bias_add) on "
+                          f"the reference's public API, median of 3 calls, {per * 1e3:.1f} ms each"}
+    if args.workload == "c4":
+        heads = 8
+        secs = O.ref_time_attention_gemms(heads, 2048, 128, 3, 1, 3)
+        per = float(statistics.median(secs))
+        return {"value": 2.0 * 2 * heads * 2048 * 2048 * 128 / per / 1e12, "unit": "TFLOP/s",
+                "cores": cores, "kind": "reference",
+                "sample": f"{heads} of 512 heads: the two gemm_strided_batched calls, median of 3, "
+                          f"{per * 1e3:.1f} ms each"}
+    if args.workload == "c5":
+        rows = 512
+        bench = O.RefGemmBench(rows, 32768, 8192, False, 4)
+        bench.run(1.0, 0.0, False, 1)
+        secs = list(bench.run(1.0, 0.0, False, 3))
+        bench.close()
+        per = float(statistics.median(secs))
+        return {"value": 2.0 * rows * 32768 * 8192 / per / 1e12, "unit": "TFLOP/s",
+                "cores": cores, "kind": "reference",
+                "sample": f"{rows} of 32768 rows of A/C (B full), median of 3 gemm calls, "
+                          f"{per:.2f} s each"}
+    rows = 16384
+    secs = O.ref_time_gemv(rows, 8192, 4, 1, 5)
+    per = float(statistics.median(secs))
+    return {"value": 4.0 * (rows * 8192 + 8192 + rows) / per / 1e9, "unit": "GB/s",
+            "cores": cores, "kind": "reference",
+            "sample": f"{rows} of 65536 rows of A, median of 5 gemv calls, {per * 1e3:.1f} ms each"}
 
 
 def run_reference_arm(args):
@@ -651,6 +699,10 @@ def main():
                             "sample": f"reference Tensor::contiguous() of the {m}x{n} transpose "
                                       f"(cpu::transpose_f32), median of 3 calls, "
                                       f"{per * 1e3:.1f} ms each"}
+
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and cpu_baseline is None
+            and args.workload in ("c3", "c4", "c5", "gemv") and not args.mnk):
+        cpu_baseline = reference_cpu_baseline(args, m, n, k)
 
     metric = {"gemv": "gemv HBM GB/s (65536x8192 fp32)",
               "copy": "strided copy GB/s (Tensor::contiguous of a transposed 8192^2 fp32 view)"}

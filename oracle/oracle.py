@@ -116,6 +116,10 @@ def reference():
                 so.mfref_attention.argtypes = [_ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int,
                                                _ptr, _ptr, ctypes.c_int, _ptr, _ptr, ctypes.c_int,
                                                ctypes.c_int, _f32, _ptr, _ptr, _ptr]
+                so.mfref_time_mlp.argtypes = [_i64, _i64, _i64, _u64, ctypes.c_int,
+                                              ctypes.c_int, _ptr]
+                so.mfref_time_attention_gemms.argtypes = [_i64, _i64, _i64, _u64, ctypes.c_int,
+                                                          ctypes.c_int, _ptr]
                 so.mfref_contiguous_view.argtypes = [_ptr, _ptr, ctypes.c_int, _ptr, _ptr, _ptr,
                                                      _ptr, _ptr, ctypes.c_int, _ptr, _ptr]
                 so.mfref_time_transpose_contiguous.argtypes = [_i64, _i64, ctypes.c_int,
@@ -425,6 +429,19 @@ class RefGemmBench:
 def ref_time_gemv(rows, cols, seed, warmup, reps):
     secs = np.zeros(reps, np.float64)
     _check_ref(reference().mfref_time_gemv(rows, cols, seed, warmup, reps, _p(secs)))
+    return secs
+
+
+def ref_time_mlp(rows, d_in, d_hid, seed, warmup, reps):
+    secs = np.zeros(reps, np.float64)
+    _check_ref(reference().mfref_time_mlp(rows, d_in, d_hid, seed, warmup, reps, _p(secs)))
+    return secs
+
+
+def ref_time_attention_gemms(heads, seq, dh, seed, warmup, reps):
+    secs = np.zeros(reps, np.float64)
+    _check_ref(reference().mfref_time_attention_gemms(heads, seq, dh, seed, warmup, reps,
+                                                      _p(secs)))
     return secs
 
 

@@ -10,6 +10,7 @@
 //   bias_add / relu/gelu  include/mensurflow/ops/elementwise.hpp:43,56,62
 //   backward of bias_add and matmul, through the reference's autograd (Tensor::backward)
 //   uniform / normal      include/mensurflow/ops/random.hpp:20,25
+//   Tensor::contiguous of views (permute / slice / expand), include/mensurflow/tensor.hpp
 // Used by tests/golden/make_golden.py (fixtures), by tests that pin the C restatement in
 // oracle/mf_oracle.c against the reference, and by bench.py's CPU-baseline and reference arms.
 // Every entry returns 0 on success and -1 on a C++ exception (text in mfref_last_error()).
@@ -18,6 +19,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -299,6 +301,66 @@ int mfref_time_gemv(std::int64_t rows, std::int64_t cols, std::uint64_t seed, in
             const Tensor r = gemv(a, x, 1.0f, nullptr, 0.0f, false, Execution::CPU);
             seconds[i] = now() - t0;
             (void)r;
+        }
+    });
+}
+
+// Times the reference's two-layer MLP forward on CPU inputs made once:
+// y = bias_add(matmul(gelu(bias_add(matmul(x, w1), b1)), w2), b2), x ~ N(0, 1), w1 / w2
+// Xavier-uniform, zero biases, with the public ops a user would call.
+int mfref_time_mlp(std::int64_t rows, std::int64_t d_in, std::int64_t d_hid, std::uint64_t seed,
+                   int warmup, int reps, double* seconds) {
+    return guarded([&] {
+        const float lim = std::sqrt(6.0f / static_cast<float>(d_in + d_hid));
+        const Tensor x = normal({rows, d_in}, 0.0f, 1.0f, seed, 0, Execution::CPU);
+        const Tensor w1 = uniform({d_in, d_hid}, -lim, lim, seed, std::uint64_t(rows * d_in),
+                                  Execution::CPU);
+        const Tensor w2 = uniform({d_hid, d_in}, -lim, lim, seed,
+                                  std::uint64_t(rows * d_in + d_in * d_hid), Execution::CPU);
+        const Tensor b1 = Tensor::zeros({d_hid});
+        const Tensor b2 = Tensor::zeros({d_in});
+        auto step = [&] {
+            const Tensor h = gelu(bias_add(matmul(x, w1, Execution::CPU), b1, Execution::CPU),
+                                  false, Execution::CPU);
+            return bias_add(matmul(h, w2, Execution::CPU), b2, Execution::CPU);
+        };
+        for (int i = 0; i < warmup; ++i) {
+            step();
+        }
+        for (int i = 0; i < reps; ++i) {
+            const double t0 = now();
+            const Tensor y = step();
+            seconds[i] = now() - t0;
+            (void)y;
+        }
+    });
+}
+
+// Times the reference's two batched GEMMs of attention on `heads` matrices:
+// S = gemm_strided_batched(q, k, 1/sqrt(dh), transpose_b) and O = gemm_strided_batched(S, v),
+// q, k, v ~ N(0, 1/sqrt(dh)) (S stands in for the softmax weights: same shape, same work).
+int mfref_time_attention_gemms(std::int64_t heads, std::int64_t seq, std::int64_t dh,
+                               std::uint64_t seed, int warmup, int reps, double* seconds) {
+    return guarded([&] {
+        const float sd = 1.0f / std::sqrt(static_cast<float>(dh));
+        const std::uint64_t n = std::uint64_t(heads * seq * dh);
+        const Tensor q = normal({heads, seq, dh}, 0.0f, sd, seed, 0, Execution::CPU);
+        const Tensor k = normal({heads, seq, dh}, 0.0f, sd, seed, n, Execution::CPU);
+        const Tensor v = normal({heads, seq, dh}, 0.0f, sd, seed, 2 * n, Execution::CPU);
+        auto step = [&] {
+            const Tensor sc = gemm_strided_batched(q, k, sd, nullptr, 0.0f, false, true,
+                                                   Execution::CPU);
+            return gemm_strided_batched(sc, v, 1.0f, nullptr, 0.0f, false, false,
+                                        Execution::CPU);
+        };
+        for (int i = 0; i < warmup; ++i) {
+            step();
+        }
+        for (int i = 0; i < reps; ++i) {
+            const double t0 = now();
+            const Tensor o = step();
+            seconds[i] = now() - t0;
+            (void)o;
         }
     });
 }
