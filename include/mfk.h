@@ -60,6 +60,7 @@ typedef enum mfk_precision {
 #define MFK_DEVERR_MMA_TIMEOUT 0x2u
 #define MFK_DEVERR_EPILOGUE_TIMEOUT 0x4u
 #define MFK_DEVERR_CONVERT_TIMEOUT 0x8u
+#define MFK_DEVERR_SELFTEST_TIMEOUT 0x10u
 
 /* One GEMM: c = act(alpha * op(A) op(B) + beta * c_in + bias).
  * op(A) is m x k with element (i, p) at a[i*a_rs + p*a_cs]; op(B) is k x n with element (p, j)
@@ -269,6 +270,14 @@ int32_t mfk_get_default_precision(void);
  * device to finish its work. *bits receives MFK_DEVERR_* bits; returns MFK_OK, or
  * MFK_ERR_DEVICE_FAULT when bits were set, or MFK_ERR_CUDA. */
 int mfk_device_status(uint32_t* bits, int32_t clear);
+
+/* Self-test of the failure path (no counterpart in the reference): one kernel waits, through the
+ * same bounded wait the GEMM pipeline uses, on a barrier that nothing completes, with a limit of
+ * limit_ns (at most the pipeline's own 2 s). The wait gives up, sets MFK_DEVERR_SELFTEST_TIMEOUT
+ * in the device error word and the kernel ends normally; *gave_up is 1 when it did. Synchronises
+ * the stream. Read (and clear) the error word with mfk_device_status afterwards; the context
+ * stays usable. */
+int mfk_selftest_wait_timeout(uint64_t limit_ns, uint32_t* gave_up, void* stream);
 
 /* Instrumentation (no counterpart in the reference's kernels; the reference times ops with
  * host-side trace spans in run_on, src/core/dispatcher.cpp:298-317, which cannot see device time).

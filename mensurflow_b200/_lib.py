@@ -56,6 +56,7 @@ EXPORTED = (
     "mfk_status_string",
     "mfk_last_cuda_error",
     "mfk_version",
+    "mfk_selftest_wait_timeout",
     "mfk_kernel_timer",
     "mfk_kernel_timer_read",
     "mfk_launch_count",
@@ -149,6 +150,8 @@ def lib() -> ctypes.CDLL:
             so.mfk_status_string.restype = ctypes.c_char_p
             so.mfk_last_cuda_error.restype = ctypes.c_char_p
             so.mfk_version.restype = i32
+            so.mfk_selftest_wait_timeout.argtypes = [ctypes.c_uint64,
+                                                     ctypes.POINTER(ctypes.c_uint32), vp]
             so.mfk_kernel_timer.argtypes = [i32]
             so.mfk_kernel_timer_read.argtypes = [ctypes.POINTER(ctypes.c_double),
                                                  ctypes.POINTER(ctypes.c_int64)]

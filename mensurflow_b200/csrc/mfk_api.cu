@@ -40,6 +40,9 @@ using mfk::GemmArgs;
 // address comes from cudaGetSymbolAddress, once per device (DeviceInfo::noalloc_scratch).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[MFK_NOALLOC_SCRATCH_BYTES];
 
+// Where the wait self-test kernel reports whether its wait gave up.
+static __device__ unsigned int g_selftest_flag;
+
 // A caller-fixed workspace used instead of the stream-ordered allocator.
 struct FixedScratch {
     uint8_t* ptr;
@@ -1229,6 +1232,25 @@ int mfk_device_status(uint32_t* bits, int32_t clear) {
     }
     *bits = v;
     return v != 0 ? MFK_ERR_DEVICE_FAULT : MFK_OK;
+}
+
+int mfk_selftest_wait_timeout(uint64_t limit_ns, uint32_t* gave_up, void* stream) {
+    if (gave_up == nullptr || limit_ns == 0 || limit_ns > MFK_WAIT_LIMIT_NS)
+        return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    void* flag_addr = nullptr;
+    MFK_CUDA(cudaGetSymbolAddress(&flag_addr, g_selftest_flag));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned int* flag = static_cast<unsigned int*>(flag_addr);
+    g_launches.fetch_add(1);
+    mfk::wait_selftest_kernel<<<1, 32, 0, s>>>(static_cast<unsigned long long>(limit_ns), flag);
+    MFK_CUDA(cudaGetLastError());
+    MFK_CUDA(cudaMemcpyAsync(gave_up, flag, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    MFK_CUDA(cudaStreamSynchronize(s));
+    return MFK_OK;
 }
 
 int mfk_kernel_timer(int32_t enable) {

@@ -69,8 +69,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Returns false (and leaves the error
-// word set) when the limit passes or another thread has already raised an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code) {
+// word set) when `limit_ns` passes or another thread has already raised an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code,
+                                          uint64_t limit_ns = MFK_WAIT_LIMIT_NS) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t start = global_timer();
@@ -78,7 +79,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
         if (mbar_try_wait(addr, parity)) return true;
         if ((spin & 255u) == 0u) {
             if (error_raised()) return false;
-            if (global_timer() - start > MFK_WAIT_LIMIT_NS) {
+            if (global_timer() - start > limit_ns) {
                 raise_error(code);
                 return false;
             }

@@ -364,4 +364,24 @@ __global__ void __launch_bounds__(kBgThreads) bias_grad_kernel(const float* __re
     if (warp == 0 && col_ok) out[col] = acc;
 }
 
+// ---- self-test of the bounded waits ---------------------------------------------------------
+// One CTA waits on an mbarrier that nothing will ever complete, through the same bounded wait
+// the GEMM pipeline uses, with a short limit: the wait gives up, records `kErrSelfTest` in the
+// device error word and the kernel returns normally, leaving the context usable.
+constexpr unsigned int kErrSelfTest = 1u << 4;
+
+__global__ void wait_selftest_kernel(unsigned long long limit_ns, unsigned int* gave_up) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // nothing arrives on `bar`, so phase 0 never completes
+        const bool done = mbar_wait(&bar, 0, kErrSelfTest, limit_ns);
+        *gave_up = done ? 0u : 1u;
+    }
+}
+
 }  // namespace mfk

@@ -99,3 +99,61 @@ def test_block_range_covers_rows_once():
             assert rows == list(range(total))
     with pytest.raises(ValueError):
         block_range(10, 2, 2)
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 holds the wrong number of rows: sharded_gemm rejects it on the host (ValueError)
+    and the rank leaves without joining the gather. Rank 0 reaches the gather, whose peer is
+    gone: the collective must end with an error within the process group's short timeout rather
+    than wait for ever."""
+    import datetime
+    import time
+
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    from mensurflow_b200 import sharded
+
+    m, n, k = 64, 16, 8
+    a = torch.randn(m, k)
+    b = torch.randn(n, k)
+    a_local = sharded.local_rows(a, world, rank)
+    if rank == 1:
+        try:
+            sharded.sharded_gemm(a_local[:-1], b, m, transpose_b=True, gather=True,
+                                 gemm_fn=oracle_gemm)
+            q.put((rank, "no error"))
+        except ValueError:
+            q.put((rank, "ValueError"))
+        q.close()
+        q.join_thread()
+        os._exit(0)  # leaves without the collective
+    t0 = time.time()
+    try:
+        sharded.sharded_gemm(a_local, b, m, transpose_b=True, gather=True, gemm_fn=oracle_gemm)
+        q.put((rank, "no error"))
+    except Exception as e:  # the collective's failure (timeout or closed connection)
+        q.put((rank, f"error after {time.time() - t0:.1f} s: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_makes_the_gather_fail_not_hang():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank is still waiting in the gather"
+    results = dict(q.get(timeout=10) for _ in procs)
+    assert results[1] == "ValueError"
+    assert results[0].startswith("error after"), results[0]
