@@ -24,14 +24,17 @@ def test_bounded_wait_gives_up_and_the_context_stays_usable(cuda):
     so = _lib.lib()
     assert mf.device_status() == 0
     gave_up = ctypes.c_uint32(7)
-    rc = so.mfk_selftest_wait_timeout(50_000_000, ctypes.byref(gave_up),
-                                      torch.cuda.current_stream().cuda_stream)
-    assert rc == _lib.MFK_OK
-    assert gave_up.value == 1
-    bits = ctypes.c_uint32(0)
-    assert so.mfk_device_status(ctypes.byref(bits), 0) == _lib.MFK_ERR_DEVICE_FAULT
-    assert bits.value == 0x10  # MFK_DEVERR_SELFTEST_TIMEOUT, nothing else
-    assert mf.device_status() == 0x10  # read and cleared
+    try:
+        rc = so.mfk_selftest_wait_timeout(50_000_000, ctypes.byref(gave_up),
+                                          torch.cuda.current_stream().cuda_stream)
+        assert rc == _lib.MFK_OK
+        assert gave_up.value == 1
+        bits = ctypes.c_uint32(0)
+        assert so.mfk_device_status(ctypes.byref(bits), 0) == _lib.MFK_ERR_DEVICE_FAULT
+        assert bits.value == 0x10  # MFK_DEVERR_SELFTEST_TIMEOUT, nothing else
+        assert mf.device_status() == 0x10  # read and cleared
+    finally:
+        mf.device_status()  # later kernels must not see the bit, whatever happened above
     assert mf.device_status() == 0  # cleared
     # the context is intact: a GEMM right after gives the oracle's result
     rng = np.random.default_rng(1)
