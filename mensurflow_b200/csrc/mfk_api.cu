@@ -241,10 +241,15 @@ bool tma_readable(const Operand& o, int64_t k) {
 }
 
 // 1xTF32 reads a readable operand in place. 3xTF32 needs it split: the pre-pass costs 12 bytes of
-// HBM traffic per element once, the in-kernel split of A (converter warps) costs shared-memory
-// bandwidth on every N-tile of the product. Measured on B200 the in-kernel split wins below
-// N ~ 360 (C4's P @ V, N = 128: 8.1 -> 5.6 ms) and loses above (C3 4096^2 x 1024: 0.19 -> 0.26 ms).
-constexpr int64_t kInKernelSplitMaxN = 384;
+// HBM traffic per element and a launch, the in-kernel split of A (converter warps, only lo written
+// where the tensor cores truncate) costs issue slots and shared-memory bandwidth on every N-tile
+// of the product, off the MMA's critical path. With the bit-arithmetic rounding and CTA-scope
+// arrives the in-kernel split of A wins at every width measured on B200 (pre-pass -> in-kernel):
+// C2 8192^3 3.89 -> 3.74 ms, 8192 x 4096 x 8192 2.25 -> 2.03 ms, 8192 x 1024 x 8192 0.64 -> 0.50
+// ms, C3's 4096 x 1024 x 4096 0.21 -> 0.17 ms, C4's S = QK^T 0.77 -> 0.73 ms per 128 heads (the
+// first build, with cvt.rna rounding and cluster-scope arrives, lost above N ~ 360). So A is split
+// in the kernel whenever TMA can read it where it lies; B, and an A it cannot read, are packed.
+constexpr int64_t kInKernelSplitMaxN = INT64_MAX;
 
 
 
@@ -528,12 +533,11 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     B.ptr += B.bl.shift;
 
     // Direct TMA reads when the layout allows; the maps are encoded now so that a layout the
-    // driver rejects falls back to packing instead of failing. In 3xTF32 only A of a small-N
-    // product is read in place (split inside the kernel); every other operand is packed as an
-    // explicitly rounded (hi, lo) pair. Reading raw fp32 as hi elsewhere (the tensor cores
-    // truncate) saves a third of the pre-pass but measured ~9% slower on the 8192^3 kernel under
-    // the power cap: the 13 low bits left in hi keep toggling through shared memory and the MMA
-    // datapath, where rounded hi has them zeroed.
+    // driver rejects falls back to packing instead of failing. In 3xTF32 A is read in place and
+    // split inside the kernel; B is packed as an explicitly rounded (hi, lo) pair (a pre-pass
+    // writing B's lo only, with raw B as hi, measured ~9% slower on the 8192^3 kernel under the
+    // power cap: the 13 low bits left in hi keep toggling through shared memory and the MMA
+    // datapath, where rounded hi has them zeroed).
     CUtensorMap ma0, ma1, mb0, mb1;
     auto direct_map = [&](Operand& o, int box_rows, CUtensorMap* m0, CUtensorMap* m1,
                           int* bcast) {

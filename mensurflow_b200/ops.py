@@ -227,7 +227,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch
          beta: float = 0.0, transpose_a: bool = False, transpose_b: bool = False, *,
          bias: Optional[torch.Tensor] = None, activation: Optional[str] = None,
          precision: Optional[str] = None, out: Optional[torch.Tensor] = None,
-         execution: str = "auto", chunks: int = 8) -> torch.Tensor:
+         execution: str = "auto", chunks: int = 32) -> torch.Tensor:
     """alpha * op(a) @ op(b) + beta * c, as mensurflow::gemm (blas.hpp:59, blas.cpp:234-262),
     in ONE kernel; `bias` and `activation` fuse the following bias_add/relu/gelu.
 
