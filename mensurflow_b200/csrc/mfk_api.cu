@@ -358,9 +358,9 @@ int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode
             for (int64_t i = 0; i < batch && offs_aligned; ++i) offs_aligned = o.bl.offsets[i] % 4 == 0;
         }
         if (offs_aligned) {
-            const int64_t total4 = o.rows * (Kp / 4) * batch;
-            const int64_t blocks = std::min<int64_t>((total4 + 255) / 256,
-                                                     static_cast<int64_t>(info->sm_count) * 16);
+            const int64_t rows = o.rows * batch;  // one warp per row, eight per block
+            const int64_t blocks = std::min<int64_t>((rows + 7) / 8,
+                                                     static_cast<int64_t>(info->sm_count) * 8);
             mfk::pack_kmajor_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
                 o.ptr, reinterpret_cast<const long long*>(o.dev_offsets), o.bl.stride, o.rs,
                 static_cast<int>(o.rows), static_cast<int>(k), static_cast<int>(Kp),

@@ -72,41 +72,54 @@ __global__ void __launch_bounds__(256) pack_kmajor_kernel(
 }
 
 // The same pass for an operand that is already K-major with 16-byte aligned rows and K % 4 == 0
-// (the common case: A row-major, or B read transposed): no transpose needed, so each thread
-// moves one float4 straight through, coalesced on both sides. Grid-stride over
-// rows x Kp/4 float4s of `batch` matrices.
+// (the common case: A row-major, or B read transposed): no transpose needed, so each float4 goes
+// straight through, coalesced on both sides. One warp per output row (grid-stride over the
+// batch x R rows; the row's source found with one division), lanes along the row's Kp/4 float4s,
+// two rows in flight per warp.
+__device__ __forceinline__ void pack_store4(float* hi, float* lo, long long i, float4 v, int mode) {
+    float4* h4 = reinterpret_cast<float4*>(hi) + i;
+    if (mode == kPackCopy) {
+        *h4 = v;
+    } else if (mode == kPackRound) {
+        *h4 = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+    } else {
+        float4 h, l;
+        split_tf32(v.x, h.x, l.x);
+        split_tf32(v.y, h.y, l.y);
+        split_tf32(v.z, h.z, l.z);
+        split_tf32(v.w, h.w, l.w);
+        *h4 = h;
+        reinterpret_cast<float4*>(lo)[i] = l;
+    }
+}
+
 __global__ void __launch_bounds__(256) pack_kmajor_vec4_kernel(
     const float* __restrict__ x, const long long* __restrict__ offsets, long long bstride,
     long long rs, int R, int K, int Kp, int batch, float* __restrict__ hi,
     float* __restrict__ lo, int mode) {
-    const long long per_row = Kp / 4;
-    const long long per_mat = static_cast<long long>(R) * per_row;
-    const long long total = per_mat * batch;
-    const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += step) {
-        const long long b = i / per_mat;
-        const long long rem = i - b * per_mat;
-        const long long r = rem / per_row;
-        const int p = static_cast<int>(rem - r * per_row) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (p < K) {
-            const long long base = offsets ? offsets[b] : b * bstride;
-            v = __ldcs(reinterpret_cast<const float4*>(x + base + r * rs + p));
-        }
-        float4* h4 = reinterpret_cast<float4*>(hi) + i;
-        if (mode == kPackCopy) {
-            *h4 = v;
-        } else if (mode == kPackRound) {
-            *h4 = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
-        } else {
-            float4 h, l;
-            split_tf32(v.x, h.x, l.x);
-            split_tf32(v.y, h.y, l.y);
-            split_tf32(v.z, h.z, l.z);
-            split_tf32(v.w, h.w, l.w);
-            *h4 = h;
-            reinterpret_cast<float4*>(lo)[i] = l;
+    const int lane = threadIdx.x % 32;
+    const int per_row = Kp / 4;
+    const long long rows = static_cast<long long>(batch) * R;
+    const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x / 32);
+    auto source = [&](long long row) {
+        const long long b = row / R;
+        const long long r = row - b * R;
+        return x + (offsets ? offsets[b] : b * bstride) + r * rs;
+    };
+    for (long long row0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+         row0 < rows; row0 += 2 * nwarps) {
+        const long long row1 = row0 + nwarps;
+        const float* s0 = source(row0);
+        const float* s1 = row1 < rows ? source(row1) : nullptr;
+#pragma unroll 4
+        for (int j = lane; j < per_row; j += 32) {
+            const int p = 4 * j;
+            const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 v0 = p < K ? __ldcs(reinterpret_cast<const float4*>(s0 + p)) : zero;
+            const float4 v1 =
+                (s1 != nullptr && p < K) ? __ldcs(reinterpret_cast<const float4*>(s1 + p)) : zero;
+            pack_store4(hi, lo, row0 * per_row + j, v0, mode);
+            if (s1 != nullptr) pack_store4(hi, lo, row1 * per_row + j, v1, mode);
         }
     }
 }

@@ -55,6 +55,33 @@ def test_c5_full_size(cuda):
     assert mf.device_status() == 0
 
 
+def test_c3_full_size_mlp(cuda):
+    """C3: y = gelu(X W1 + b1) W2 + b2 at batch 4096, X ~ N(0, 1), Xavier-uniform W1 [1024, 4096]
+    and W2 [4096, 1024], zero biases (the bench path: X and H split inside the GEMMs, the first
+    GEMM's tail wave shared by stream-K). Sampled rows of the whole chain against the oracle; the
+    bound for y adds the first GEMM's bound, carried through |W2| (GELU's slope is below 1.13)."""
+    rows_n, d_in, d_hid = 4096, 1024, 4096
+    g = torch.Generator(device=cuda).manual_seed(2)
+    lim = (6.0 / (d_in + d_hid)) ** 0.5
+    x = torch.randn(rows_n, d_in, device=cuda, generator=g)
+    w1 = (torch.rand(d_in, d_hid, device=cuda, generator=g) * 2 - 1) * lim
+    w2 = (torch.rand(d_hid, d_in, device=cuda, generator=g) * 2 - 1) * lim
+    b1 = torch.zeros(d_hid, device=cuda)
+    b2 = torch.zeros(d_in, device=cuda)
+    y = mf.linear(mf.linear(x, w1, b1, "gelu"), w2, b2)
+    rows = _rows(rows_n, 64, 6)
+    idx = torch.from_numpy(rows).to(cuda)
+    x_s = x[idx].cpu().numpy()
+    w1_h, w2_h = w1.cpu().numpy(), w2.cpu().numpy()
+    zeros_hid, zeros_in = np.zeros(d_hid, np.float32), np.zeros(d_in, np.float32)
+    h_s = O.activation(O.gemm(x_s, w1_h, bias=zeros_hid), "gelu").astype(np.float32)
+    want = O.gemm(h_s, w2_h, bias=zeros_in)
+    h_bound = 1.13 * (TOL_3X[0] * O.abs_product(x_s, w1_h) + TOL_3X[1])
+    mag = O.abs_product(np.abs(h_s), w2_h) + O.abs_product(h_bound, w2_h) / TOL_3X[0]
+    assert_close(y[idx].cpu().numpy(), want, mag, TOL_3X, "C3 full size")
+    assert mf.device_status() == 0
+
+
 def test_c4_full_size_attention_gemms(cuda):
     """C4: S = Q K^T / sqrt(128) and O = P V with batch*heads 512, seq 2048, head_dim 128."""
     bh, s, d = 512, 2048, 128
