@@ -66,6 +66,21 @@ def parse_args():
     return p.parse_args()
 
 
+# What each workload's end-to-end leg times (every copy is inside the timed region).
+E2E_PATHS = {
+    "c2": "the public gemm on pinned host tensors (execution='gpu'): host -> device copies, the C "
+          "ABI kernel, device -> host copy of C, pipelined by row blocks",
+    "c5": "the public gemm on pinned host tensors (execution='gpu'): host -> device copies, the C "
+          "ABI kernel, device -> host copy of C, pipelined by row blocks",
+    "c3": "pinned host X, W1, W2, b1, b2 copied in, the two fused linear calls, Y copied back "
+          "(one stream, not overlapped); with --prepacked the split weights stay resident and "
+          "only X and Y cross the host link",
+    "c4": "pinned host q, k, v copied in, the public attention op (S = QK^T/sqrt(d), causal masked "
+          "softmax, O = PV), O copied back (one stream, not overlapped)",
+    "default": "pinned host inputs copied in, the op, the result copied back (one stream)",
+}
+
+
 # ---- peaks ------------------------------------------------------------------------------------
 
 def load_peaks():
@@ -406,12 +421,44 @@ def main():
         b2 = torch.zeros(d_in, device=device)
         flops_rank = 2.0 * rows * d_in * d_hid * 2
         unit = "TFLOP/s"
-        h2d_bytes = d2h_bytes = 0
+        h2d_bytes = 4 * (X.numel() + W1.numel() + W2.numel() + d_hid + d_in)
+        d2h_bytes = 4 * rows * d_in
+        W1_dense, W2_dense = W1, W2
+
+        def e2e_factory():
+            # the forward from pinned host tensors: inputs and weights copied in every step, the
+            # output copied back, all on the caller's stream inside the timed region
+            hs = [t.cpu().pin_memory() for t in (X, W1_dense, W2_dense, b1, b2)]
+            ds = [torch.empty_like(t) for t in (X, W1_dense, W2_dense, b1, b2)]
+            hy = torch.empty(rows, d_in, pin_memory=True)
+
+            def e2e_step():
+                for d, h in zip(ds, hs):
+                    d.copy_(h, non_blocking=True)
+                hmid = mf.linear(ds[0], ds[1], ds[3], "gelu", precision=args.precision)
+                hy.copy_(mf.linear(hmid, ds[2], ds[4], precision=args.precision),
+                         non_blocking=True)
+            return e2e_step
 
         if args.prepacked:
             wl += "; W1, W2 pre-split once (pack_b) outside the timed region"
             W1 = mf.pack_b(W1, precision=args.precision)
             W2 = mf.pack_b(W2, precision=args.precision)
+            # inference with the split weights resident: only X comes in and Y goes out
+            h2d_bytes = 4 * X.numel()
+            packed1, packed2 = W1, W2
+
+            def e2e_factory():
+                hx = X.cpu().pin_memory()
+                dx = torch.empty_like(X)
+                hy = torch.empty(rows, d_in, pin_memory=True)
+
+                def e2e_step():
+                    dx.copy_(hx, non_blocking=True)
+                    hmid = mf.linear(dx, packed1, b1, "gelu", precision=args.precision)
+                    hy.copy_(mf.linear(hmid, packed2, b2, precision=args.precision),
+                             non_blocking=True)
+                return e2e_step
 
         def step():
             h = mf.linear(X, W1, b1, "gelu", precision=args.precision)
@@ -434,7 +481,23 @@ def main():
         P = torch.softmax(torch.randn(bh, seq, seq, device=device, generator=gen), -1)
         flops_rank = 2.0 * (2.0 * bh * seq * seq * dh)
         unit = "TFLOP/s"
-        h2d_bytes = d2h_bytes = 0
+        h2d_bytes = 4 * 3 * bh * seq * dh
+        d2h_bytes = 4 * bh * seq * dh
+
+        def e2e_factory():
+            # the whole attention op of the reference's API (S = QK^T/sqrt(d), causal masked
+            # softmax, O = PV) from pinned host q, k, v, the output copied back
+            hq, hk, hv = (t.cpu().pin_memory() for t in (Q, K, V))
+            dq, dk, dv = (torch.empty_like(t) for t in (Q, K, V))
+            ho = torch.empty(bh, seq, dh, pin_memory=True)
+
+            def e2e_step():
+                dq.copy_(hq, non_blocking=True)
+                dk.copy_(hk, non_blocking=True)
+                dv.copy_(hv, non_blocking=True)
+                ho.copy_(mf.attention(dq, dk, dv, causal=True, precision=args.precision),
+                         non_blocking=True)
+            return e2e_step
 
         def step():
             mf.gemm_strided_batched(Q, K, scale, None, 0.0, False, True, precision=args.precision)
@@ -623,9 +686,7 @@ def main():
         e2e = {"value": e_val, "unit": unit, "h2d_bytes_per_step": h2d_bytes,
                "d2h_bytes_per_step": d2h_bytes, "ms_per_step": e_ms, "steps": e2e_steps,
                "host_link": link, "link_bound_ms_per_step": bound_ms,
-               "path": "mensurflow_b200 op on pinned host tensors (execution='gpu'): host -> "
-                       "device copies, the C ABI kernels, device -> host copy of the result, "
-                       "pipelined by row blocks, all inside the timed region"}
+               "path": E2E_PATHS.get(args.workload, E2E_PATHS["default"])}
 
     allgather = None
     if gather_step is not None:
