@@ -680,14 +680,83 @@ def where(condition: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> torch.Te
     return out
 
 
+def _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks):
+    """Execution::GPU on host-resident q, k, v (as gemm's host path): the batch is cut into
+    chunks whose q, k, v stream in on one stream, are attended on the caller's stream and stream
+    back on a third, so the copies overlap each other and the math. q, k and v must share their
+    leading (batch) shape; a mask must broadcast over the batch (at most 2-D, or leading dims of
+    1). Returns a host tensor; the copies are complete when this returns."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lead = tuple(q.shape[:-2])
+    if tuple(k.shape[:-2]) != lead or tuple(v.shape[:-2]) != lead:
+        raise ValueError("attention: host tensors with execution='gpu' need q, k and v with the "
+                         "same batch shape")
+    if mask is not None and mask.dim() > 2 and any(s != 1 for s in mask.shape[:-2]):
+        raise ValueError("attention: host tensors with execution='gpu' take a mask that is the "
+                         "same for every batch entry")
+    queries, depth_v = q.shape[-2], v.shape[-1]
+    batch = int(np.prod(lead)) if lead else 1
+    q3 = q.reshape(batch, queries, q.shape[-1])
+    k3 = k.reshape(batch, k.shape[-2], k.shape[-1])
+    v3 = v.reshape(batch, v.shape[-2], depth_v)
+    if out is None:
+        out = torch.empty(lead + (queries, depth_v), dtype=torch.float32, pin_memory=True)
+    elif tuple(out.shape) != lead + (queries, depth_v) or out.device.type != "cpu":
+        raise ValueError("attention: out must be a host tensor of the result's shape")
+    o3 = out.view(batch, queries, depth_v)
+    compute = torch.cuda.current_stream(dev)
+    copy_in, copy_out = _copy_streams(dev)
+    copy_in.wait_stream(compute)
+    with torch.cuda.stream(copy_in):
+        d_mask = mask.to(dev, non_blocking=True) if mask is not None else None
+    nchunks = max(1, min(chunks, batch))
+    bounds = [round(i * batch / nchunks) for i in range(nchunks + 1)]
+    alive = []
+    for i in range(nchunks):
+        b0, b1 = bounds[i], bounds[i + 1]
+        if b1 <= b0:
+            continue
+        with torch.cuda.stream(copy_in):
+            dq = q3[b0:b1].to(dev, non_blocking=True)
+            dk = k3[b0:b1].to(dev, non_blocking=True)
+            dv = v3[b0:b1].to(dev, non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(copy_in)
+        compute.wait_event(ready)
+        o = attention(dq, dk, dv, d_mask, causal, scale, precision=precision)
+        done = torch.cuda.Event()
+        done.record(compute)
+        copy_out.wait_event(done)
+        with torch.cuda.stream(copy_out):
+            o3[b0:b1].copy_(o, non_blocking=True)
+        alive.extend((dq, dk, dv, o))
+    for t in alive + ([d_mask] if d_mask is not None else []):
+        t.record_stream(copy_out)
+        t.record_stream(copy_in)
+    copy_out.synchronize()
+    return out
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
               mask: Optional[torch.Tensor] = None, causal: bool = False, scale: float = 0.0, *,
-              precision: Optional[str] = None) -> torch.Tensor:
+              precision: Optional[str] = None, execution: str = "auto",
+              out: Optional[torch.Tensor] = None, chunks: int = 16) -> torch.Tensor:
     """Scaled dot-product attention as mensurflow::attention (attention.hpp:21,
     src/ops/attention.cpp:48-98): scores = scale * q @ k^T (batched GEMM, scale in alpha), entries
     outside `mask` (Bool, broadcast to the scores) and, with `causal`, above the diagonal set to
     -inf, softmax over the keys, then weights @ v. The masking is fused into the softmax pass
-    (one read and one write of the scores instead of the reference's where + softmax passes)."""
+    (one read and one write of the scores instead of the reference's where + softmax passes).
+
+    `execution` follows the reference's Execution: with host tensors "gpu" streams batch chunks
+    through the current CUDA device and returns a host tensor (`out`, if given, receives it)."""
+    if execution not in ("auto", "cpu", "gpu"):
+        raise ValueError(f"attention: unknown execution {execution!r}")
+    if (isinstance(q, torch.Tensor) and q.device.type == "cpu" and execution == "gpu" and
+            all(isinstance(t, torch.Tensor) and t.device.type == "cpu" and
+                t.dtype == torch.float32 and t.dim() >= 2 for t in (q, k, v))):
+        if mask is not None and (not isinstance(mask, torch.Tensor) or mask.dtype != torch.bool):
+            raise ValueError("attention: mask must be a defined Bool tensor")
+        return _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks)
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
         if t is None or not isinstance(t, torch.Tensor):
             raise ValueError(f"attention: undefined {name}")

@@ -109,3 +109,35 @@ def test_fused_mask_equals_where_then_softmax(cuda):
     assert rc == 0
     assert torch.equal(fused, composed)
     assert mf.device_status() == 0
+
+
+@pytest.mark.parametrize("chunks", [1, 4, 16])
+def test_attention_on_host_tensors(cuda, chunks):
+    """Execution::GPU on host-resident q, k, v: batch chunks stream through the device and the
+    result comes back as a host tensor; it equals the attention of the same tensors on the device
+    (each chunk is the same op on fewer batch entries) within the reference's 1e-4, with a 2-D
+    mask and the causal mask."""
+    rng = np.random.default_rng(12)
+    q = torch.from_numpy(rng.standard_normal((2, 5, 40, 16)).astype(np.float32) * 0.5)
+    k = torch.from_numpy(rng.standard_normal((2, 5, 56, 16)).astype(np.float32) * 0.5)
+    v = torch.from_numpy(rng.standard_normal((2, 5, 56, 24)).astype(np.float32))
+    mask = torch.from_numpy(rng.random((40, 56)) > 0.2)
+    hq, hk, hv = (t.pin_memory() for t in (q, k, v))
+    out = torch.empty(2, 5, 40, 24, pin_memory=True)
+    got = mf.attention(hq, hk, hv, mask, causal=True, execution="gpu", out=out, chunks=chunks)
+    assert got is out and got.device.type == "cpu"
+    want = mf.attention(q.to(cuda), k.to(cuda), v.to(cuda), mask.to(cuda), causal=True).cpu()
+    np.testing.assert_allclose(got.numpy(), want.numpy(), rtol=1e-4, atol=1e-6)
+    ref = O.attention(q.numpy(), k.numpy(), v.numpy(), mask.numpy(), causal=True)
+    np.testing.assert_allclose(got.numpy(), ref, rtol=1e-4, atol=1e-5)
+    assert mf.device_status() == 0
+
+
+def test_attention_on_host_tensors_argument_errors(cuda):
+    q = torch.zeros(2, 4, 8)
+    with pytest.raises(ValueError):
+        mf.attention(q, torch.zeros(3, 4, 8), torch.zeros(3, 4, 8), execution="gpu")
+    with pytest.raises(ValueError):  # a mask per batch entry
+        mf.attention(q, q, q, torch.ones(2, 4, 4, dtype=torch.bool), execution="gpu")
+    with pytest.raises(ValueError):
+        mf.attention(q, q, q, execution="tpu")
