@@ -474,3 +474,54 @@ def test_stream_k_tail(cuda, shape, precision):
     np.testing.assert_array_equal(host(mf.matmul(dev(qa, cuda), dev(qb, cuda),
                                                  precision=precision)), O.gemm(qa, qb))
     no_fault()
+
+
+# The shape tables of the reference's packed-GEMM test (tests/ops/gemm_packed_test.cpp): around
+# every micro-tile edge (:175-179), odd extras (:181-182), the threaded and large cases (:186,
+# :275), single rows (:380-381), narrow outputs (:400-403), and the strided-view shapes (:436-438).
+PACKED_TEST_SHAPES = [
+    (1, 1, 1), (1, 17, 3), (5, 15, 7), (6, 16, 1), (6, 16, 256), (7, 17, 257), (12, 32, 512),
+    (13, 33, 255), (167, 31, 20), (168, 16, 20), (169, 17, 300), (337, 49, 513), (40, 4080, 9),
+    (20, 4081, 17), (9, 8200, 5), (64, 64, 64), (100, 1, 100), (1, 100, 100),
+    (11, 7, 5), (13, 9, 17), (3, 23, 7), (5, 25, 9), (24, 48, 300), (25, 49, 301), (50, 50, 1100),
+    (200, 300, 100), (500, 70, 400), (37, 1000, 300), (1000, 37, 300),
+    (300, 300, 300), (97, 257, 901), (600, 100, 80),
+    (1, 1000, 37), (1, 37, 1000), (1, 2049, 515), (1, 5003, 301), (1, 7, 3), (1, 4096, 4),
+    (64, 10, 512), (65, 10, 515), (33, 1, 100), (7, 2, 9), (40, 15, 70), (3, 12, 2000),
+    (20, 5, 40000), (2000, 10, 300), (1001, 13, 77), (2, 3, 8), (2000, 64, 147), (3000, 40, 100),
+    (1500, 64, 30), (900, 100, 200), (5000, 16, 33), (600, 2000, 100), (700, 900, 250),
+    (32, 3000, 800), (64, 1500, 100),
+]
+STRIDED_TEST_SHAPES = [(1, 1, 1), (5, 15, 7), (13, 33, 255), (37, 50, 300), (169, 17, 300),
+                       (64, 64, 64), (200, 100, 70), (9, 200, 5)]
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_reference_packed_kernel_shapes(cuda, precision):
+    """Every shape of the reference's packed-GEMM test, on exact (quarter-integer) inputs: the
+    device result equals the oracle's bit for bit in both precisions."""
+    for i, (m, n, k) in enumerate(PACKED_TEST_SHAPES):
+        rng = np.random.default_rng(1000 + i)
+        a = (rng.integers(-16, 17, (m, k)) / 4).astype(np.float32)
+        b = (rng.integers(-16, 17, (k, n)) / 4).astype(np.float32)
+        got = host(mf.matmul(dev(a, cuda), dev(b, cuda), precision=precision))
+        np.testing.assert_array_equal(got, O.gemm(a, b), err_msg=f"{m}x{n}x{k}")
+    no_fault()
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+def test_reference_strided_view_shapes(cuda, precision):
+    """The strided shapes (gemm_packed_test.cpp:436-438) with A and B each stored plain or
+    transposed and read as views (the kernels take the strides as they are)."""
+    for i, (m, n, k) in enumerate(STRIDED_TEST_SHAPES):
+        rng = np.random.default_rng(2000 + i)
+        a = (rng.integers(-16, 17, (m, k)) / 4).astype(np.float32)
+        b = (rng.integers(-16, 17, (k, n)) / 4).astype(np.float32)
+        want = O.gemm(a, b)
+        for ta in (False, True):
+            for tb in (False, True):
+                av = dev(np.ascontiguousarray(a.T), cuda).t() if ta else dev(a, cuda)
+                bv = dev(np.ascontiguousarray(b.T), cuda).t() if tb else dev(b, cuda)
+                got = host(mf.matmul(av, bv, precision=precision))
+                np.testing.assert_array_equal(got, want, err_msg=f"{m}x{n}x{k} tA{ta} tB{tb}")
+    no_fault()
