@@ -79,15 +79,17 @@ struct GemmArgs {
     int c_peer;        // C lies in another GPU's memory: the epilogue's stores cross NVLink
     // Stream-K tail (sk_units > 0): tiles [0, dp_tiles) go whole to the units in turn; the
     // k-iterations of tiles [dp_tiles, num_tiles) are split evenly over all sk_units units
-    // (unit u: sk_q + 1 iterations if u < sk_r, else sk_q). The unit holding a split tile's first
-    // k-blocks finishes it: every other part writes its raw accumulator to its unit's slot of
-    // sk_part and counts itself in sk_count; the finisher waits for the count, sums the parts in
-    // k order and runs the epilogue.
+    // (unit u: sk_q + 1 iterations if u < sk_r, else sk_q). Every part of a split tile but the
+    // first writes its raw accumulator to its unit's slot 0 of sk_part and counts itself in
+    // sk_count. The unit holding the first k-blocks reaches the tile last; if the count is then
+    // complete it sums the parts in k order and runs the epilogue, else it writes its own part
+    // to slot 1 and counts itself too, and whichever part is counted last does the sum. No part
+    // ever waits for another.
     int sk_units;
     long long dp_tiles;
     long long sk_q;
     int sk_r;
-    float* sk_part;    // [unit][CG][kBM * BN] floats
+    float* sk_part;    // [unit][2 slots][CG][kBM * BN] floats
     int* sk_count;     // [(num_tiles - dp_tiles) * CG * epilogue warps], zero at launch
 };
 
@@ -628,27 +630,61 @@ __device__ __forceinline__ void tc_mma(const GemmArgs& g, uint32_t tmem_base, ui
     }
 }
 
-// This warp's block of unit u's stream-K slot (kBM x BN floats per CTA rank): warp (half, ew)'s
-// chunk ci is a 2 KB block at ((half*kChunks + ci)*4 + ew) * 512 floats, stored as four 512-byte
-// rows of float4 (float4 q of lane l at q*32 + l), so each warp instruction moves 512 contiguous
-// bytes.
+// This warp's block of unit u's stream-K slot `slot` (kBM x BN floats per CTA rank): warp
+// (half, ew)'s chunk ci is a 2 KB block at ((half*kChunks + ci)*4 + ew) * 512 floats, stored as
+// four 512-byte rows of float4 (float4 q of lane l at q*32 + l), so each warp instruction moves
+// 512 contiguous bytes.
 template <int CG, int BN>
-__device__ __forceinline__ float4* sk_part_block(const GemmArgs& g, long long u, uint32_t rank,
-                                                 int half, int ew, int ci, int kChunks) {
-    float* base = g.sk_part + (u * CG + rank) * static_cast<long long>(kBM * BN);
+__device__ __forceinline__ float4* sk_part_block(const GemmArgs& g, long long u, int slot,
+                                                 uint32_t rank, int half, int ew, int ci,
+                                                 int kChunks) {
+    float* base = g.sk_part + ((u * 2 + slot) * CG + rank) * static_cast<long long>(kBM * BN);
     return reinterpret_cast<float4*>(
         base + ((static_cast<long long>(half) * kChunks + ci) * 4 + ew) * 512);
 }
 
-// The finisher of stream-K tile tr (unit u_first, which holds the first k-blocks) replaces its
-// own part in TMEM with the sum over every part, added in k order (its own first), so the
-// result does not depend on timing; the regular epilogue then reads the tile from TMEM as
-// usual. Chunk by chunk: the own part from TMEM, the others' loads of a pair in flight together.
+// This warp's raw accumulator (TMEM, all chunks) into unit u's slot `slot`, then counted.
+// Returns the count before this part (so count + 1 parts are written).
+template <int CG, int BN, int kChunks>
+__device__ __forceinline__ int sk_write_part(const GemmArgs& g, uint32_t tbase, long long u,
+                                             int slot, uint32_t rank, int half, int ew, int lane,
+                                             int* count) {
+#pragma unroll 1
+    for (int ci = 0; ci < kChunks; ci += 2) {
+        uint32_t r0[kEpiCols], r1[kEpiCols];
+        tmem_ld_issue_32x32b_x16(tbase + ci * kEpiCols, r0);
+        tmem_ld_issue_32x32b_x16(tbase + (ci + 1) * kEpiCols, r1);
+        tmem_ld_wait();
+        float4* d0 = sk_part_block<CG, BN>(g, u, slot, rank, half, ew, ci, kChunks);
+        float4* d1 = sk_part_block<CG, BN>(g, u, slot, rank, half, ew, ci + 1, kChunks);
+#pragma unroll
+        for (int q = 0; q < kEpiCols / 4; ++q) {
+            __stcg(d0 + q * 32 + lane,
+                   make_float4(__uint_as_float(r0[4 * q]), __uint_as_float(r0[4 * q + 1]),
+                               __uint_as_float(r0[4 * q + 2]), __uint_as_float(r0[4 * q + 3])));
+            __stcg(d1 + q * 32 + lane,
+                   make_float4(__uint_as_float(r1[4 * q]), __uint_as_float(r1[4 * q + 1]),
+                               __uint_as_float(r1[4 * q + 2]), __uint_as_float(r1[4 * q + 3])));
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    int prev = 0;
+    if (lane == 0) prev = atomicAdd(count, 1);
+    return __shfl_sync(0xffffffffu, prev, 0);
+}
+
+// Replaces this warp's own part in TMEM with the sum over every part of the split tile, added
+// in k order (unit u_first's part first) so the bits do not depend on which part was counted
+// last; the regular epilogue then reads the tile from TMEM as usual. The parts of units after
+// u_first are in their slot 0, u_first's (when another unit sums) in its slot 1, this unit's
+// own in TMEM. Chunk by chunk, the other parts' loads of a pair in flight together.
 template <int CG, int BN, int kChunks>
 __device__ __forceinline__ void sk_fixup_tmem(const GemmArgs& g, uint32_t tbase,
-                                              long long u_first, long long u_last, uint32_t rank,
-                                              int half, int ew, int lane) {
+                                              long long u_first, long long u_last, long long me,
+                                              uint32_t rank, int half, int ew, int lane) {
     constexpr int kGroup = 2;
+    __threadfence();  // the parts counted before this point are visible
 #pragma unroll 1
     for (int ci = 0; ci < kChunks; ++ci) {
         uint32_t own[kEpiCols];
@@ -656,28 +692,40 @@ __device__ __forceinline__ void sk_fixup_tmem(const GemmArgs& g, uint32_t tbase,
         tmem_ld_wait();
         float sum[kEpiCols];
 #pragma unroll
-        for (int j = 0; j < kEpiCols; ++j) sum[j] = __uint_as_float(own[j]);
+        for (int j = 0; j < kEpiCols; ++j) sum[j] = 0.0f;
 #pragma unroll 1
-        for (long long v0 = u_first + 1; v0 <= u_last; v0 += kGroup) {
+        for (long long v0 = u_first; v0 <= u_last; v0 += kGroup) {
             float4 part[kGroup][kEpiCols / 4];
 #pragma unroll
             for (int p = 0; p < kGroup; ++p) {
-                if (v0 + p <= u_last) {
-                    const float4* src = sk_part_block<CG, BN>(g, v0 + p, rank, half, ew, ci, kChunks);
+                const long long v = v0 + p;
+                if (v <= u_last && v != me) {
+                    const float4* src = sk_part_block<CG, BN>(g, v, v == u_first ? 1 : 0, rank,
+                                                              half, ew, ci, kChunks);
 #pragma unroll
                     for (int q = 0; q < kEpiCols / 4; ++q) part[p][q] = __ldcg(src + q * 32 + lane);
                 }
             }
 #pragma unroll
             for (int p = 0; p < kGroup; ++p) {
-                if (v0 + p <= u_last) {
+                const long long v = v0 + p;
+                if (v <= u_last) {
+                    float val[kEpiCols];
+                    if (v == me) {
 #pragma unroll
-                    for (int q = 0; q < kEpiCols / 4; ++q) {
-                        sum[4 * q] = __fadd_rn(sum[4 * q], part[p][q].x);
-                        sum[4 * q + 1] = __fadd_rn(sum[4 * q + 1], part[p][q].y);
-                        sum[4 * q + 2] = __fadd_rn(sum[4 * q + 2], part[p][q].z);
-                        sum[4 * q + 3] = __fadd_rn(sum[4 * q + 3], part[p][q].w);
+                        for (int j = 0; j < kEpiCols; ++j) val[j] = __uint_as_float(own[j]);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < kEpiCols / 4; ++q) {
+                            val[4 * q] = part[p][q].x;
+                            val[4 * q + 1] = part[p][q].y;
+                            val[4 * q + 2] = part[p][q].z;
+                            val[4 * q + 3] = part[p][q].w;
+                        }
                     }
+#pragma unroll
+                    for (int j = 0; j < kEpiCols; ++j)
+                        sum[j] = v == u_first ? val[j] : __fadd_rn(sum[j], val[j]);
                 }
             }
         }
@@ -786,36 +834,29 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                               : nullptr;
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
                                static_cast<uint32_t>(acc * BN + half * kHalf);
-        // A stream-K part of a tile. Parts after the first k-blocks: this warp's raw accumulator
-        // goes to the unit's slot and is counted; the tile's first part (its unit reaches the
-        // tile last, at the end of its share) waits for the count, then sums all parts.
+        // A stream-K part of a tile (see GemmArgs::sk_units): either this warp sums the tile's
+        // parts and falls through to the regular epilogue, or it leaves its part for another
+        // unit and moves on. Nothing here waits for another unit.
         if (w.kb0 != 0 || w.kb1 != g.num_kb) {
             const long long tr = w.tile - g.dp_tiles;
             const long long u_first = sk_unit_of(g, tr * g.num_kb);
             const long long u_last = sk_unit_of(g, (tr + 1) * g.num_kb - 1);
+            const int others = static_cast<int>(u_last - u_first);  // parts besides one
             int* count = &g.sk_count[(tr * CG + rank) * C::kEpiWarpsC + wid];
+            bool sums = false;
             if (w.kb0 != 0) {
-#pragma unroll 1
-                for (int ci = 0; ci < kChunks; ci += 2) {
-                    uint32_t r0[kEpiCols], r1[kEpiCols];
-                    tmem_ld_issue_32x32b_x16(tbase + ci * kEpiCols, r0);
-                    tmem_ld_issue_32x32b_x16(tbase + (ci + 1) * kEpiCols, r1);
-                    tmem_ld_wait();
-                    float4* d0 = sk_part_block<CG, BN>(g, me, rank, half, ew, ci, kChunks);
-                    float4* d1 = sk_part_block<CG, BN>(g, me, rank, half, ew, ci + 1, kChunks);
-#pragma unroll
-                    for (int q = 0; q < kEpiCols / 4; ++q) {
-                        __stcg(d0 + q * 32 + lane,
-                               make_float4(__uint_as_float(r0[4 * q]), __uint_as_float(r0[4 * q + 1]),
-                                           __uint_as_float(r0[4 * q + 2]), __uint_as_float(r0[4 * q + 3])));
-                        __stcg(d1 + q * 32 + lane,
-                               make_float4(__uint_as_float(r1[4 * q]), __uint_as_float(r1[4 * q + 1]),
-                                           __uint_as_float(r1[4 * q + 2]), __uint_as_float(r1[4 * q + 3])));
-                    }
-                }
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) atomicAdd(count, 1);
+                // a later part: counted last means every other part is written
+                sums = sk_write_part<CG, BN, kChunks>(g, tbase, me, 0, rank, half, ew, lane,
+                                                      count) == others;
+            } else {
+                int done = 0;
+                if (lane == 0) done = atomicAdd(count, 0);
+                done = __shfl_sync(0xffffffffu, done, 0);
+                sums = done == others ||
+                       sk_write_part<CG, BN, kChunks>(g, tbase, me, 1, rank, half, ew, lane,
+                                                      count) == others;
+            }
+            if (!sums) {
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
@@ -831,23 +872,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                 }
                 continue;
             }
-            // the finisher: every later part of the tile has been written (bounded wait)
-            if (lane == 0) {
-                const int want = static_cast<int>(u_last - u_first);
-                if (atomicAdd(count, 0) < want) {
-                    const uint64_t start = global_timer();
-                    while (atomicAdd(count, 0) < want) {
-                        if (error_raised() || global_timer() - start > MFK_WAIT_LIMIT_NS) {
-                            raise_error(kErrEpilogueWait);
-                            break;
-                        }
-                        __nanosleep(64);
-                    }
-                }
-                __threadfence();
-            }
-            __syncwarp();
-            sk_fixup_tmem<CG, BN, kChunks>(g, tbase, u_first, u_last, rank, half, ew, lane);
+            sk_fixup_tmem<CG, BN, kChunks>(g, tbase, u_first, u_last, me, rank, half, ew, lane);
         }
         // Two register sets: the next chunk's TMEM load is in flight while this one is used.
         uint32_t ra[kEpiCols], rb[kEpiCols];

@@ -299,9 +299,9 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
     // Stream-K tail: when the last wave of tiles would leave many units idle (under 92% of the
     // units busy on average), the tiles of that wave are shared by k-iterations across every
     // unit instead. Each extra part of a tile costs one round trip of a kBM x BN accumulator
-    // through L2, so the share per unit must be at least four k-blocks. All units are resident
-    // at once (the grid is the occupancy), so a tile's finisher never waits on a unit that has
-    // not started. Measured on B200, it pays in 3xTF32 when whole waves come first (the summing
+    // through L2, so the share per unit must be at least four k-blocks. No part waits for
+    // another (the last part counted sums them), so GEMMs running at once on several streams
+    // cannot hold each other up. Measured on B200, it pays in 3xTF32 when whole waves come first (the summing
     // of split tiles overlaps their MMAs: 4096 x 4096 x 1024, 127.5 -> 118.5 us) or when the
     // tiles fill at most half the units (1024^3: 39.4 -> 33.8 us), and not otherwise: with every
     // SM streaming tf32 operands, 1xTF32 is short of L2 bandwidth (4096 x 1024 x 4096: 53 -> 63
@@ -322,7 +322,7 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
         if (SPLIT3 && busy < 0.92 && iters >= 4 * resident &&
             (waves >= 1 || 2 * g.num_tiles <= resident)) {
             const size_t part_bytes =
-                static_cast<size_t>(resident) * CG * mfk::kBM * BN * sizeof(float);
+                static_cast<size_t>(resident) * 2 * CG * mfk::kBM * BN * sizeof(float);
             const size_t count_bytes = static_cast<size_t>(rem) * CG * C::kEpiWarpsC * sizeof(int);
             MFK_CUDA(cudaMallocAsync(&sk.p, part_bytes + count_bytes, stream));
             MFK_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(sk.p) + part_bytes, 0, count_bytes,

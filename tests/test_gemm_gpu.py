@@ -525,3 +525,22 @@ def test_reference_strided_view_shapes(cuda, precision):
                 got = host(mf.matmul(av, bv, precision=precision))
                 np.testing.assert_array_equal(got, want, err_msg=f"{m}x{n}x{k} tA{ta} tB{tb}")
     no_fault()
+
+
+def test_stream_k_gemms_on_concurrent_streams(cuda):
+    """Stream-K GEMMs launched on two streams at once share the SMs, so not every CTA of one
+    launch need be resident while the other runs; no part of a split tile waits for another, so
+    every launch completes with the same bits and no bounded wait runs out."""
+    rng = np.random.default_rng(77)
+    a = dev(rng.standard_normal((1024, 1024)).astype(np.float32), cuda)
+    b = dev(rng.standard_normal((1024, 1024)).astype(np.float32), cuda)
+    want = mf.gemm(a, b)
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = []
+    for i in range(24):
+        with torch.cuda.stream(streams[i % 2]):
+            outs.append(mf.gemm(a, b))
+    torch.cuda.synchronize()
+    assert all(torch.equal(o, want) for o in outs)
+    no_fault()
