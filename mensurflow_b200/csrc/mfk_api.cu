@@ -301,11 +301,12 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
     // unit instead. Each extra part of a tile costs one round trip of a kBM x BN accumulator
     // through L2, so the share per unit must be at least four k-blocks. No part waits for
     // another (the last part counted sums them), so GEMMs running at once on several streams
-    // cannot hold each other up. Measured on B200, it pays in 3xTF32 when whole waves come first (the summing
-    // of split tiles overlaps their MMAs: 4096 x 4096 x 1024, 127.5 -> 118.5 us) or when the
-    // tiles fill at most half the units (1024^3: 39.4 -> 33.8 us), and not otherwise: with every
-    // SM streaming tf32 operands, 1xTF32 is short of L2 bandwidth (4096 x 1024 x 4096: 53 -> 63
-    // us), and a tail that is the whole problem leaves the summing exposed (138 -> 145 us).
+    // cannot hold each other up. Measured on B200 (kernel time, off -> on), it pays in 3xTF32
+    // when whole waves come first, so the summing of split tiles overlaps their MMAs (4096 x 4096
+    // x 1024: 129 -> 124 us), or when the tiles fill at most half the units (100 x 1000 x 4096:
+    // 98 -> 53 us; 1024 x 300 x 2048: 66 -> 46 us), and not otherwise: with every SM streaming
+    // tf32 operands 1xTF32 is short of L2 bandwidth (4096 x 1024 x 4096: 53 -> 63 us), and a tail
+    // that is the whole problem leaves the summing exposed (138 -> 145 us).
     struct SkWorkspace {
         void* p = nullptr;
         cudaStream_t s;
