@@ -90,7 +90,19 @@ struct GemmArgs {
     long long sk_q;
     int sk_r;
     float* sk_part;    // [unit][2 slots][CG][kBM * BN] floats
-    int* sk_count;     // [(num_tiles - dp_tiles) * CG * epilogue warps], zero at launch
+    int* sk_count;     // [(num_tiles - dp_tiles) * CG * epilogue warps], zero at launch; the
+                       // parts counted in bits 0-15, those that met an infinity from bit 16
+    // 3xTF32 with infinite operands (nonfinite_fixup_tmem). op(A)(i, p) of matrix z at
+    // ra[z*ra_bs + i*ra_rs + p] — A as the kernel reads it: raw where it is split in the kernel,
+    // else its packed hi — and op(B)(p, j) at rb[z*rb_bs + j*rb_rs + p], B's packed hi; both
+    // K-major with 16-byte aligned rows. ra is null outside 3xTF32. nf_word[i] == nf_tag[i] says
+    // a packing pass met an infinity (i = 0: this call's own passes, 1: a pre-split B).
+    const float* ra;
+    long long ra_rs, ra_bs;
+    const float* rb;
+    long long rb_rs, rb_bs;
+    const unsigned* nf_word[2];
+    unsigned nf_tag[2];
 };
 
 // CG: CTAs per MMA (1 or 2). BN: N of one MMA (columns of the tile). Per CTA: kBM rows of A,
@@ -388,12 +400,13 @@ __device__ __forceinline__ void tc_producer(const GemmArgs& g, const CUtensorMap
 // `converted` barrier.
 template <int CG, int BN, bool SPLIT3>
 __device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, uint64_t* a_full,
-                                           uint64_t* converted) {
+                                           uint64_t* converted, uint32_t* inf_seen) {
     using C = TcConfig<CG, BN, SPLIT3>;
     const int ct = threadIdx.x - kCvtWarp0 * 32;
     const int lane = threadIdx.x % 32;
     int stage = 0;
     uint32_t phase = 0;
+    bool inf = false;  // this thread has met an infinity in A (for the epilogue's fix-up)
     WorkIter<CG> wi(g);
     for (Work w; wi.next(g, w);) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
@@ -411,6 +424,7 @@ __device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, u
                     split_tf32(x.y, h.y, l.y);
                     split_tf32(x.z, h.z, l.z);
                     split_tf32(x.w, h.w, l.w);
+                    inf |= any_inf(x);
                     lo[i] = l;
                 }
             } else {
@@ -422,10 +436,12 @@ __device__ __forceinline__ void tc_convert(const GemmArgs& g, uint8_t* stages, u
                     split_tf32(x.y, h.y, l.y);
                     split_tf32(x.z, h.z, l.z);
                     split_tf32(x.w, h.w, l.w);
+                    inf |= any_inf(x);
                     hi[i] = h;
                     lo[i] = l;
                 }
             }
+            if (inf) *reinterpret_cast<volatile uint32_t*>(inf_seen) = 1u;
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -453,7 +469,8 @@ template <int CG, int BN>
 __device__ __forceinline__ void tc_convert_tmem(const GemmArgs& g, uint8_t* stages,
                                                 uint64_t* a_full, uint64_t* empty,
                                                 uint64_t* tfull, uint64_t* tempty,
-                                                uint32_t tmem_base, int group) {
+                                                uint32_t tmem_base, int group,
+                                                uint32_t* inf_seen) {
     using C = TcConfig<CG, BN, true, true>;
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -475,6 +492,7 @@ __device__ __forceinline__ void tc_convert_tmem(const GemmArgs& g, uint8_t* stag
             if (!mbar_wait(&a_full[stage], phase, kErrConvertWait)) return;
             const uint32_t rowp = smem_u32(stages + stage * C::kStageBytes) + row * 128;
             float x[32];
+            bool inf = false;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 const float4 v = ld_shared_v4(rowp + ((c ^ (row & 7)) << 4));
@@ -482,7 +500,10 @@ __device__ __forceinline__ void tc_convert_tmem(const GemmArgs& g, uint8_t* stag
                 x[4 * c + 1] = v.y;
                 x[4 * c + 2] = v.z;
                 x[4 * c + 3] = v.w;
+                inf |= any_inf(v);
             }
+            // raised before this k-block's arrival on tfull, so before the MMAs that read it
+            if (inf) *reinterpret_cast<volatile uint32_t*>(inf_seen) = 1u;
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);  // this warp's rows of A are read
             if (!mbar_wait(&tempty[slot], tphase ^ 1u, kErrConvertWait)) return;
@@ -648,7 +669,7 @@ __device__ __forceinline__ float4* sk_part_block(const GemmArgs& g, long long u,
 template <int CG, int BN, int kChunks>
 __device__ __forceinline__ int sk_write_part(const GemmArgs& g, uint32_t tbase, long long u,
                                              int slot, uint32_t rank, int half, int ew, int lane,
-                                             int* count) {
+                                             int* count, int add) {
 #pragma unroll 1
     for (int ci = 0; ci < kChunks; ci += 2) {
         uint32_t r0[kEpiCols], r1[kEpiCols];
@@ -670,7 +691,7 @@ __device__ __forceinline__ int sk_write_part(const GemmArgs& g, uint32_t tbase, 
     __threadfence();
     __syncwarp();
     int prev = 0;
-    if (lane == 0) prev = atomicAdd(count, 1);
+    if (lane == 0) prev = atomicAdd(count, add);
     return __shfl_sync(0xffffffffu, prev, 0);
 }
 
@@ -736,6 +757,59 @@ __device__ __forceinline__ void sk_fixup_tmem(const GemmArgs& g, uint32_t tbase,
     tmem_st_wait();
 }
 
+// Infinite operands in 3xTF32. An infinite x splits into hi = x and lo = 0, so a product
+// hi(a)*hi(b) + hi(a)*lo(b) + lo(a)*hi(b) with a = inf and b exact in tf32 (lo(b) = 0) holds
+// inf * 0 = NaN where the reference's fp32 product is an infinity. A dot product that meets an
+// infinity has a non-finite result that the order of its sum does not change (NaN if any term is
+// NaN or two infinite terms differ in sign, else the infinity), so each NaN accumulator of such a
+// tile is replaced by the plain fp32 dot product from the operands in memory, in tensor memory
+// before the epilogue reads it. Entries the tensor cores got right are not touched, and tiles
+// that cannot hold such an entry never come here (the flags the packing passes and the
+// converter warps raise on meeting an infinity).
+__device__ __forceinline__ float nonfinite_dot(const GemmArgs& g, int b, int row, int col) {
+    const float* a = g.ra + static_cast<long long>(b) * g.ra_bs + static_cast<long long>(row) * g.ra_rs;
+    const float* x = g.rb + static_cast<long long>(b) * g.rb_bs + static_cast<long long>(col) * g.rb_rs;
+    float acc = 0.0f;
+#pragma unroll 1
+    for (int p = 0; p < g.k; ++p) acc = fmaf(__ldg(a + p), __ldg(x + p), acc);
+    return acc;
+}
+
+// This warp's columns [colbase, colbase + kChunks*kEpiCols) of row `row` of the tile in tensor
+// memory at tbase: every NaN entry recomputed by nonfinite_dot and written back, one column at a
+// time (few registers live besides the epilogue's). Warp-uniform.
+template <int kChunks>
+__device__ __forceinline__ void nonfinite_fixup_tmem(const GemmArgs& g, uint32_t tbase, int b,
+                                                     int row, bool row_ok, int colbase) {
+#pragma unroll 1
+    for (int ci = 0; ci < kChunks; ++ci) {
+        const int col0 = colbase + ci * kEpiCols;
+        uint32_t nan_mask = 0;
+        {
+            uint32_t r[kEpiCols];
+            tmem_ld_issue_32x32b_x16(tbase + ci * kEpiCols, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < kEpiCols; ++j)
+                if (isnan(__uint_as_float(r[j]))) nan_mask |= 1u << j;
+        }
+        const int cols = g.n - col0;
+        if (!row_ok || cols <= 0) nan_mask = 0;
+        if (cols < kEpiCols) nan_mask &= (1u << max(cols, 0)) - 1u;
+        // the columns where some lane of the warp holds a NaN
+        for (uint32_t m = __reduce_or_sync(0xffffffffu, nan_mask); m != 0; m &= m - 1) {
+            const int j = __ffs(m) - 1;
+            const uint32_t taddr = tbase + ci * kEpiCols + j;
+            uint32_t v;
+            tmem_ld_issue_32x32b_x1(taddr, v);
+            tmem_ld_wait();
+            if (nan_mask & (1u << j)) v = __float_as_uint(nonfinite_dot(g, b, row, col0 + j));
+            tmem_st_32x32b_x1(taddr, v);
+        }
+    }
+    tmem_st_wait();
+}
+
 // The epilogue of one kEpiCols-column chunk of a thread's row: alpha, beta*C_in, bias,
 // activation, with the reference's rounding steps. The activation is applied in a separate pass
 // over the values so each unrolled loop stays short.
@@ -794,7 +868,7 @@ template <int CG, int BN, bool SPLIT3, bool ATMEM>
 __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap* tmC,
                                             uint8_t* epi_smem, uint32_t tmem_base,
                                             uint64_t* acc_full, uint64_t* acc_empty,
-                                            uint32_t rank) {
+                                            uint32_t rank, const uint32_t* inf_seen) {
     using C = TcConfig<CG, BN, SPLIT3, ATMEM>;
     constexpr int kHalf = BN / (C::kEpiWarpsC / 4);  // columns per warp
     constexpr int kChunks = kHalf / kEpiCols;
@@ -819,6 +893,12 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     uint32_t acc_phase = 0;
     const int wid = warp - C::kEpiWarp0C;
     const long long me = blockIdx.x / CG;
+    // a packing pass of this call met an infinity (written before the launch)
+    bool inf_packed = false;
+    if constexpr (SPLIT3) {
+        for (int i = 0; i < 2; ++i)
+            inf_packed |= g.ra != nullptr && g.nf_word[i] != nullptr && *g.nf_word[i] == g.nf_tag[i];
+    }
     WorkIter<CG> wi(g);
     for (Work w; wi.next(g, w);) {
         const TileCoord tc = tile_coord(g, w.tile);
@@ -834,28 +914,37 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                               : nullptr;
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
                                static_cast<uint32_t>(acc * BN + half * kHalf);
+        // 3xTF32: the k-blocks behind this accumulator may have met an infinity. The converters
+        // raise their flag before arriving for the k-block that held it, so before the MMAs this
+        // accumulator waited on.
+        bool inf_tile = false;
+        if constexpr (SPLIT3)
+            inf_tile = inf_packed || *reinterpret_cast<const volatile uint32_t*>(inf_seen) != 0u;
         // A stream-K part of a tile (see GemmArgs::sk_units): either this warp sums the tile's
         // parts and falls through to the regular epilogue, or it leaves its part for another
-        // unit and moves on. Nothing here waits for another unit.
+        // unit and moves on. Nothing here waits for another unit. Each part adds 1 to the
+        // tile's count, plus 1 << 16 if its k-blocks may have met an infinity.
         if (w.kb0 != 0 || w.kb1 != g.num_kb) {
             const long long tr = w.tile - g.dp_tiles;
             const long long u_first = sk_unit_of(g, tr * g.num_kb);
             const long long u_last = sk_unit_of(g, (tr + 1) * g.num_kb - 1);
             const int others = static_cast<int>(u_last - u_first);  // parts besides one
             int* count = &g.sk_count[(tr * CG + rank) * C::kEpiWarpsC + wid];
-            bool sums = false;
+            const int add = inf_tile ? 1 + (1 << 16) : 1;
+            int seen = 0;  // the count before this part's: the other parts written so far
             if (w.kb0 != 0) {
                 // a later part: counted last means every other part is written
-                sums = sk_write_part<CG, BN, kChunks>(g, tbase, me, 0, rank, half, ew, lane,
-                                                      count) == others;
+                seen = sk_write_part<CG, BN, kChunks>(g, tbase, me, 0, rank, half, ew, lane,
+                                                      count, add);
             } else {
-                int done = 0;
-                if (lane == 0) done = atomicAdd(count, 0);
-                done = __shfl_sync(0xffffffffu, done, 0);
-                sums = done == others ||
-                       sk_write_part<CG, BN, kChunks>(g, tbase, me, 1, rank, half, ew, lane,
-                                                      count) == others;
+                if (lane == 0) seen = atomicAdd(count, 0);
+                seen = __shfl_sync(0xffffffffu, seen, 0);
+                if ((seen & 0xffff) != others)
+                    seen = sk_write_part<CG, BN, kChunks>(g, tbase, me, 1, rank, half, ew, lane,
+                                                          count, add);
             }
+            const bool sums = (seen & 0xffff) == others;
+            inf_tile |= (seen >> 16) != 0;
             if (!sums) {
                 tc_fence_before();
                 __syncwarp();
@@ -873,6 +962,11 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                 continue;
             }
             sk_fixup_tmem<CG, BN, kChunks>(g, tbase, u_first, u_last, me, rank, half, ew, lane);
+        }
+        if constexpr (SPLIT3) {
+            if (g.ra != nullptr && __any_sync(0xffffffffu, inf_tile))
+                nonfinite_fixup_tmem<kChunks>(g, tbase, tc.b, row, row_ok,
+                                              tc.tn * BN + half * kHalf);
         }
         // Two register sets: the next chunk's TMEM load is in flight while this one is used.
         uint32_t ra[kEpiCols], rb[kEpiCols];
@@ -1017,7 +1111,8 @@ __global__ void __launch_bounds__(TcConfig<CG, BN, SPLIT3, ATMEM>::kThreads, 1)
     uint64_t* converted = a_full + C::kStages;
     uint64_t* tempty = converted + C::kStages;   // ATMEM: the MMAs reading a TMEM slot are done
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + (ATMEM ? C::kASlots : 0));
-    static_assert((3 * C::kStages + 2 * C::kAccStages + 1 + C::kASlots) * 8 + 4 <=
+    uint32_t* inf_seen = tmem_holder + 1;        // ASPLIT: the converters met an infinity in A
+    static_assert((3 * C::kStages + 2 * C::kAccStages + 1 + C::kASlots) * 8 + 8 <=
                       C::kBarrierBytes,
                   "barrier area too small");
 
@@ -1036,6 +1131,7 @@ __global__ void __launch_bounds__(TcConfig<CG, BN, SPLIT3, ATMEM>::kThreads, 1)
             mbar_init(&acc_empty[s], C::kEpiWarpsC * CG);  // every epilogue warp of the pair
         }
         mbar_init(drain, 1);
+        *inf_seen = 0u;
         if constexpr (ATMEM) {
             for (int s = 0; s < C::kStages; ++s) mbar_init(&a_full[s], 1);
             for (int s = 0; s < C::kASlots; ++s) {
@@ -1092,13 +1188,13 @@ __global__ void __launch_bounds__(TcConfig<CG, BN, SPLIT3, ATMEM>::kThreads, 1)
     } else if (ATMEM && ((warp >= kTmCvtWarp0 && warp < kTmCvtWarp0 + 4) || warp >= kTmCvtWarp1)) {
         if constexpr (ATMEM) {
             tc_convert_tmem<CG, BN>(g, stages, a_full, empty, converted, tempty, tmem_base,
-                                    warp >= kTmCvtWarp1 ? 1 : 0);
+                                    warp >= kTmCvtWarp1 ? 1 : 0, inf_seen);
         }
     } else if (!ATMEM && ASPLIT && warp >= kCvtWarp0 && warp < kCvtWarp0 + kCvtThreads / 32) {
-        tc_convert<CG, BN, SPLIT3>(g, stages, a_full, converted);
+        tc_convert<CG, BN, SPLIT3>(g, stages, a_full, converted, inf_seen);
     } else if (warp >= C::kEpiWarp0C && warp < C::kEpiWarp0C + C::kEpiWarpsC) {
         tc_epilogue<CG, BN, SPLIT3, ATMEM>(g, &tmC, epi_smem, tmem_base, acc_full, acc_empty,
-                                           rank);
+                                           rank, inf_seen);
     }
 
     tc_fence_before();

@@ -29,6 +29,7 @@ struct mfk_packed_b {
     int64_t k = 0, n = 0, kp = 0;
     int32_t precision = MFK_PRECISION_3XTF32;
     int device = 0;
+    unsigned* inf_word = nullptr;  // 3xTF32: 1 when the packing pass met an infinity in B
 };
 
 namespace {
@@ -55,6 +56,13 @@ std::atomic<int> g_default_precision{MFK_PRECISION_3XTF32};
 constexpr int kMaxDevices = 64;
 
 std::atomic<int64_t> g_launches{0};
+
+// Tags for the packing passes' infinity flag, one per GEMM call, never 0 (fresh memory reads 0).
+std::atomic<unsigned> g_inf_tag{0};
+unsigned next_inf_tag() {
+    unsigned t = g_inf_tag.fetch_add(1) + 1;
+    return t != 0 ? t : g_inf_tag.fetch_add(1) + 1;
+}
 
 // Optional CUDA-event pairs around the main kernel launch of each call (mfk_kernel_timer).
 struct KernelTimer {
@@ -350,7 +358,9 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
 // 3xTF32 split), zero in the columns k..Kp-1. o.dev_offsets must hold the per-matrix offsets on
 // the device when o.bl.offsets is set.
 int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode,
-                const DeviceInfo* info, cudaStream_t stream) {
+                const DeviceInfo* info, cudaStream_t stream, unsigned* inf_word = nullptr,
+                unsigned inf_tag = 0) {
+    if (mode != mfk::kPackSplit) inf_word = nullptr;
     if (o.cs == 1 && o.rs % 4 == 0 && k % 4 == 0 && aligned16(o.ptr) &&
         (o.dev_offsets != nullptr || o.bl.stride % 4 == 0)) {
         // already K-major and aligned: a straight vectorised pass
@@ -365,7 +375,7 @@ int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode
             mfk::pack_kmajor_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
                 o.ptr, reinterpret_cast<const long long*>(o.dev_offsets), o.bl.stride, o.rs,
                 static_cast<int>(o.rows), static_cast<int>(k), static_cast<int>(Kp),
-                static_cast<int>(batch), o.hi, o.lo, mode);
+                static_cast<int>(batch), o.hi, o.lo, mode, inf_word, inf_tag);
             g_launches.fetch_add(1);
             MFK_CUDA(cudaGetLastError());
             return MFK_OK;
@@ -384,7 +394,7 @@ int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode
         mfk::pack_kmajor_kernel<<<grid, dim3(32, 8), 0, stream>>>(
             src, offs, o.bl.stride, o.rs, o.cs, static_cast<int>(o.rows),
             static_cast<int>(k), static_cast<int>(Kp), o.hi + out_shift,
-            o.lo ? o.lo + out_shift : nullptr, mode, p_contig);
+            o.lo ? o.lo + out_shift : nullptr, mode, p_contig, inf_word, inf_tag);
         g_launches.fetch_add(1);
         MFK_CUDA(cudaGetLastError());
     }
@@ -575,6 +585,12 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     if (copies(B)) b_off = reserve(sizeof(float) * packed_elems(B) * copies(B));
     if (copies(A) && A.bl.offsets) ao_off = reserve(sizeof(int64_t) * batch);
     if (copies(B) && B.bl.offsets) bo_off = reserve(sizeof(int64_t) * batch);
+    // The packing passes' infinity flag (3xTF32): set to this call's tag when they meet one. A
+    // word left over from an earlier call holds another tag; a chance match only costs the
+    // kernel a scan for NaN accumulators.
+    const bool inf_flag = split3 && (copies(A) || copies(B));
+    const size_t inf_off = inf_flag ? reserve(sizeof(unsigned)) : 0;
+    const unsigned inf_tag = inf_flag ? next_inf_tag() : 0;
 
     uint8_t* ws = nullptr;
     if (bytes > 0 && fixed != nullptr) {
@@ -600,7 +616,7 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
                                      cudaMemcpyHostToDevice, stream));
         }
         return launch_pack(o, d->k, Kp, batch, split3 ? mfk::kPackSplit : mfk::kPackRound,
-                           info, stream);
+                           info, stream, reinterpret_cast<unsigned*>(ws + inf_off), inf_tag);
     };
     if (copies(A) && (rc = pack(A, a_off, ao_off)) != MFK_OK) return rc;
     if (copies(B) && (rc = pack(B, b_off, bo_off)) != MFK_OK) return rc;
@@ -634,6 +650,34 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
             return MFK_ERR_UNSUPPORTED;
         }
         g.b_batch_bcast = batch > 1 ? 1 : 0;
+    }
+    if (split3) {
+        // The operands as the kernel reads them, for the exact recomputation of entries an
+        // infinity turned into NaN (inf * 0 among the split products).
+        if (A.direct) {
+            g.ra = A.ptr;
+            g.ra_rs = A.rs;
+            g.ra_bs = A.bl.stride;
+        } else {
+            g.ra = A.hi;
+            g.ra_rs = Kp;
+            g.ra_bs = A.rows * Kp;
+        }
+        if (pb != nullptr) {
+            g.rb = pb->hi;
+            g.rb_rs = pb->kp;
+            g.rb_bs = 0;
+            g.nf_word[1] = pb->inf_word;
+            g.nf_tag[1] = 1u;
+        } else {
+            g.rb = B.hi;
+            g.rb_rs = Kp;
+            g.rb_bs = B.rows * Kp;
+        }
+        if (inf_flag) {
+            g.nf_word[0] = reinterpret_cast<const unsigned*>(ws + inf_off);
+            g.nf_tag[0] = inf_tag;
+        }
     }
 
     g.num_kb = static_cast<int>(Kp / mfk::kBK);
@@ -850,18 +894,28 @@ int mfk_pack_b_f32(const float* b, int64_t rsb, int64_t csb, int64_t k, int64_t 
     if (k > 0 && n > 0) {
         const bool split3 = p->precision == MFK_PRECISION_3XTF32;
         const size_t elems = static_cast<size_t>(n) * static_cast<size_t>(p->kp);
-        if (cudaMalloc(reinterpret_cast<void**>(&p->hi), sizeof(float) * elems * (split3 ? 2 : 1)) !=
-            cudaSuccess) {
+        const size_t panel_bytes = sizeof(float) * elems * (split3 ? 2 : 1);
+        if (cudaMalloc(reinterpret_cast<void**>(&p->hi), panel_bytes + 16) != cudaSuccess) {
             cudaGetLastError();
             delete p;
             return MFK_ERR_OUT_OF_MEMORY;
         }
         p->lo = split3 ? p->hi + elems : nullptr;
+        if (split3) {
+            p->inf_word = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(p->hi) + panel_bytes);
+            if (cudaMemsetAsync(p->inf_word, 0, sizeof(unsigned), stream) != cudaSuccess) {
+                cudaGetLastError();
+                cudaFree(p->hi);
+                delete p;
+                return MFK_ERR_CUDA;
+            }
+        }
         // op(B) element (p, j) at p*rsb + j*csb: K-major rows over j, row stride csb, depth rsb
         Operand o{b, csb, rsb, n, BatchLayout{}};
         o.hi = p->hi;
         o.lo = p->lo;
-        rc = launch_pack(o, k, p->kp, 1, split3 ? mfk::kPackSplit : mfk::kPackRound, info, stream);
+        rc = launch_pack(o, k, p->kp, 1, split3 ? mfk::kPackSplit : mfk::kPackRound, info, stream,
+                         p->inf_word, 1u);
         if (rc != MFK_OK) {
             cudaFree(p->hi);
             delete p;

@@ -225,6 +225,15 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
         : "memory");
 }
 
+// One 32-bit column, 32 lanes: load (issue only) and store.
+__device__ __forceinline__ void tmem_ld_issue_32x32b_x1(uint32_t taddr, uint32_t& r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x1(uint32_t taddr, uint32_t r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(r) : "memory");
+}
+
 // Wait until every tcgen05.st this thread issued has completed.
 __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -407,6 +416,13 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     const uint32_t lb = tf32_round_bits(__float_as_uint(x - __uint_as_float(hb)));
     hi = __uint_as_float(finite ? hb : (xb | ((xb & 0x007FFFFFu) ? 0x00400000u : 0u)));
     lo = __uint_as_float(finite ? lb : 0u);
+}
+
+// An infinity among the four values: the 3xTF32 split turns inf * 0 into NaN where the
+// reference has an infinity, so the passes that split operands flag what they meet.
+__device__ __forceinline__ bool any_inf(float4 v) {
+    const float inf = __int_as_float(0x7f800000);
+    return fabsf(v.x) == inf || fabsf(v.y) == inf || fabsf(v.z) == inf || fabsf(v.w) == inf;
 }
 
 // x rounded to tf32 (nearest, ties away from zero); a finite value that would round past the

@@ -20,11 +20,12 @@ enum PackMode : int {
 
 // op(X) of matrix b: element (r, p) at x[off(b) + r*rs + p*cs], with off(b) = offsets[b] when
 // offsets is non-null, else b*bstride. Writes hi/lo as [batch, R, Kp] row-major (row stride
-// Kp), zero in the padding columns K..Kp-1.
+// Kp), zero in the padding columns K..Kp-1. In kPackSplit mode an infinite element sets
+// *inf_word = inf_tag (when inf_word is non-null), for the GEMM's fix-up of inf * 0 terms.
 __global__ void __launch_bounds__(256) pack_kmajor_kernel(
     const float* __restrict__ x, const long long* __restrict__ offsets, long long bstride,
     long long rs, long long cs, int R, int K, int Kp, float* __restrict__ hi,
-    float* __restrict__ lo, int mode, int p_contig) {
+    float* __restrict__ lo, int mode, int p_contig, unsigned* inf_word, unsigned inf_tag) {
     __shared__ float tile[32][33];
     const int b = blockIdx.z;
     const int r0 = blockIdx.y * 32;
@@ -66,6 +67,7 @@ __global__ void __launch_bounds__(256) pack_kmajor_kernel(
                 split_tf32(v, h, l);
                 hi[o] = h;
                 lo[o] = l;
+                if (inf_word != nullptr && fabsf(v) == __int_as_float(0x7f800000)) *inf_word = inf_tag;
             }
         }
     }
@@ -96,7 +98,7 @@ __device__ __forceinline__ void pack_store4(float* hi, float* lo, long long i, f
 __global__ void __launch_bounds__(256) pack_kmajor_vec4_kernel(
     const float* __restrict__ x, const long long* __restrict__ offsets, long long bstride,
     long long rs, int R, int K, int Kp, int batch, float* __restrict__ hi,
-    float* __restrict__ lo, int mode) {
+    float* __restrict__ lo, int mode, unsigned* inf_word, unsigned inf_tag) {
     const int lane = threadIdx.x % 32;
     const int per_row = Kp / 4;
     const long long rows = static_cast<long long>(batch) * R;
@@ -120,6 +122,7 @@ __global__ void __launch_bounds__(256) pack_kmajor_vec4_kernel(
                 (s1 != nullptr && p < K) ? __ldcs(reinterpret_cast<const float4*>(s1 + p)) : zero;
             pack_store4(hi, lo, row0 * per_row + j, v0, mode);
             if (s1 != nullptr) pack_store4(hi, lo, row1 * per_row + j, v1, mode);
+            if (inf_word != nullptr && (any_inf(v0) || any_inf(v1))) *inf_word = inf_tag;
         }
     }
 }

@@ -544,3 +544,80 @@ def test_stream_k_gemms_on_concurrent_streams(cuda):
     torch.cuda.synchronize()
     assert all(torch.equal(o, want) for o in outs)
     no_fault()
+
+
+def _inf_operands(m, n, k, seed):
+    """Values exact in tf32 (lo = 0, so an infinity's partner lo gives inf * 0 in the split
+    products) with infinities placed to give +-inf, and NaN where inf meets 0 or two infinite
+    terms differ in sign."""
+    rng = np.random.default_rng(seed)
+    a = (rng.integers(-16, 17, (m, k)) / 4).astype(np.float32)
+    b = (rng.integers(-16, 17, (k, n)) / 4).astype(np.float32)
+    a[3, 5] = np.inf                      # row 3: +-inf, or NaN where b[5, j] == 0
+    a[m // 2, 2] = -np.inf
+    a[m // 2, 9] = np.inf                 # row m/2: -inf*b[2,j] + inf*b[9,j]
+    b[7, n - 1] = np.inf                  # column n-1: inf * a[i, 7]
+    return a, b
+
+
+def _assert_nonfinite_match(got, want):
+    special = ~np.isfinite(want)
+    assert special.any()
+    np.testing.assert_array_equal(np.isnan(got[special]), np.isnan(want[special]))
+    inf_want = np.isinf(want)
+    np.testing.assert_array_equal(got[inf_want], want[inf_want])
+    np.testing.assert_array_equal(got[~special], want[~special])  # exact inputs elsewhere
+
+
+# (m, n, k): A split in tensor memory (n <= 128), in shared memory, single-CTA tiles, stream-K
+# tails (1024 x 300 x 2048, 100 x 1000 x 4096), several waves
+INF_SHAPES = [(300, 64, 200), (300, 256, 200), (300, 640, 200), (100, 64, 70), (1024, 1024, 1024),
+              (1024, 300, 2048), (100, 1000, 4096)]
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("shape", INF_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_infinite_operands(cuda, precision, shape):
+    """Infinities in A and B give the reference's results on every kernel variant: +-inf where
+    the infinite products agree in sign, NaN where inf meets 0 or opposite infinities meet. In
+    3xTF32 an infinity's zero lo meets the other operand's hi and the tensor cores give NaN for
+    inf * 0; the kernel recomputes such entries exactly, flagged by the converter warps (A) and
+    the packing pass (B)."""
+    m, n, k = shape
+    a, b = _inf_operands(m, n, k, m * 5 + n + k)
+    want = O.gemm(a, b)
+    got = host(mf.matmul(dev(a, cuda), dev(b, cuda), precision=precision))
+    _assert_nonfinite_match(got, want)
+    no_fault()
+
+
+@pytest.mark.parametrize("route", ["packed_a", "prepacked_b", "batched", "epilogue"])
+def test_infinite_operands_routes(cuda, route):
+    """The same in 3xTF32 where A is packed by the pre-pass (transposed A), where B comes
+    pre-split (its flag is kept with the handle), in a batch (A broadcast, one infinity per
+    matrix), and with alpha, beta * C and bias applied to the recomputed entries."""
+    m, n, k = 300, 256, 200
+    a, b = _inf_operands(m, n, k, 11)
+    if route == "packed_a":
+        at = dev(np.ascontiguousarray(a.T), cuda)
+        got = host(mf.gemm(at, dev(b, cuda), transpose_a=True, precision="3xtf32"))
+        want = O.gemm(a, b)
+    elif route == "prepacked_b":
+        clean = np.where(np.isfinite(a), a, 1.0).astype(np.float32)  # infinities only in B
+        packed = mf.pack_b(dev(b, cuda), precision="3xtf32")
+        got = host(mf.gemm_prepacked(dev(clean, cuda), packed, precision="3xtf32"))
+        want = O.gemm(clean, b)
+    elif route == "batched":
+        bs = np.stack([b, np.where(np.isfinite(b), b, 0.0).astype(np.float32), b])
+        bs[1, 11, 3] = -np.inf
+        got = host(mf.gemm_strided_batched(dev(a, cuda), dev(bs, cuda), precision="3xtf32"))
+        want = np.stack([O.gemm(a, bs[i]) for i in range(3)])
+    else:
+        rng = np.random.default_rng(3)
+        c = (rng.integers(-8, 9, (m, n)) / 8).astype(np.float32)
+        bias = (rng.integers(-8, 9, n) / 8).astype(np.float32)
+        got = host(mf.gemm(dev(a, cuda), dev(b, cuda), 0.5, dev(c, cuda), 2.0,
+                           bias=dev(bias, cuda), precision="3xtf32"))
+        want = O.gemm(a, b, 0.5, c, 2.0, bias=bias)
+    _assert_nonfinite_match(got, want)
+    no_fault()
