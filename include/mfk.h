@@ -173,8 +173,11 @@ int mfk_gemm_strided_batched_f32(const mfk_gemm_desc* desc, const mfk_batch_desc
  * weights: rsb = n, csb = 1; weights stored [outputs, inputs]: rsb = 1, csb = k). b may be freed
  * or changed once the stream has run the pack. precision: MFK_PRECISION_3XTF32 / _1XTF32, or
  * DEFAULT for the library default at packing time. k == 0 or n == 0 gives an empty handle whose
- * products are zeros (plus beta*C_in and bias). The handle is released by mfk_packed_b_free
- * (device-synchronising; not while a product using it is in flight).
+ * products are zeros (plus beta*C_in and bias). The panels come from the device's stream-ordered
+ * memory pool, allocated on `stream` (a plain allocation while the stream is being captured), so
+ * the handle may be used on another stream only after that stream has waited for `stream`. The
+ * handle is released by mfk_packed_b_free (device-synchronising; not while a product using it is
+ * in flight).
  *
  * mfk_gemm_prepacked_f32: the mfk_gemm_f32 product with B taken from the handle: desc->b, b_rs and
  * b_cs are ignored; desc->k and desc->n must equal the handle's k and n, and the call must run

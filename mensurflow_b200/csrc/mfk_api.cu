@@ -30,6 +30,7 @@ struct mfk_packed_b {
     int32_t precision = MFK_PRECISION_3XTF32;
     int device = 0;
     unsigned* inf_word = nullptr;  // 3xTF32: 1 when the packing pass met an infinity in B
+    bool pooled = false;           // hi came from the stream-ordered pool (cudaMallocAsync)
 };
 
 namespace {
@@ -895,7 +896,18 @@ int mfk_pack_b_f32(const float* b, int64_t rsb, int64_t csb, int64_t k, int64_t 
         const bool split3 = p->precision == MFK_PRECISION_3XTF32;
         const size_t elems = static_cast<size_t>(n) * static_cast<size_t>(p->kp);
         const size_t panel_bytes = sizeof(float) * elems * (split3 ? 2 : 1);
-        if (cudaMalloc(reinterpret_cast<void**>(&p->hi), panel_bytes + 16) != cudaSuccess) {
+        // From the stream-ordered pool, which keeps freed blocks (a plain cudaMalloc of a large
+        // B costs milliseconds of host time); a plain allocation while the stream is captured.
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+            cudaGetLastError();
+            cap = cudaStreamCaptureStatusActive;
+        }
+        p->pooled = cap == cudaStreamCaptureStatusNone;
+        const cudaError_t alloc =
+            p->pooled ? cudaMallocAsync(reinterpret_cast<void**>(&p->hi), panel_bytes + 16, stream)
+                      : cudaMalloc(reinterpret_cast<void**>(&p->hi), panel_bytes + 16);
+        if (alloc != cudaSuccess) {
             cudaGetLastError();
             delete p;
             return MFK_ERR_OUT_OF_MEMORY;
@@ -905,8 +917,7 @@ int mfk_pack_b_f32(const float* b, int64_t rsb, int64_t csb, int64_t k, int64_t 
             p->inf_word = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(p->hi) + panel_bytes);
             if (cudaMemsetAsync(p->inf_word, 0, sizeof(unsigned), stream) != cudaSuccess) {
                 cudaGetLastError();
-                cudaFree(p->hi);
-                delete p;
+                mfk_packed_b_free(p);
                 return MFK_ERR_CUDA;
             }
         }
@@ -917,8 +928,7 @@ int mfk_pack_b_f32(const float* b, int64_t rsb, int64_t csb, int64_t k, int64_t 
         rc = launch_pack(o, k, p->kp, 1, split3 ? mfk::kPackSplit : mfk::kPackRound, info, stream,
                          p->inf_word, 1u);
         if (rc != MFK_OK) {
-            cudaFree(p->hi);
-            delete p;
+            mfk_packed_b_free(p);
             return rc;
         }
     }
@@ -941,7 +951,14 @@ int mfk_packed_b_free(mfk_packed_b* packed) {
         int cur = 0;
         const bool switch_dev = cudaGetDevice(&cur) == cudaSuccess && cur != packed->device;
         if (switch_dev) cudaSetDevice(packed->device);
-        if (cudaFree(packed->hi) != cudaSuccess) rc = MFK_ERR_CUDA;
+        if (packed->pooled) {
+            // nothing in flight reads it after the synchronisation: back to the pool at once
+            if (cudaDeviceSynchronize() != cudaSuccess ||
+                cudaFreeAsync(packed->hi, cudaStreamLegacy) != cudaSuccess)
+                rc = MFK_ERR_CUDA;
+        } else if (cudaFree(packed->hi) != cudaSuccess) {
+            rc = MFK_ERR_CUDA;
+        }
         if (switch_dev) cudaSetDevice(cur);
         cudaGetLastError();
     }

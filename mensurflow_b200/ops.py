@@ -178,6 +178,15 @@ def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activa
     # row blocks of op(A) are contiguous host slices only when A is not transposed
     nchunks = 1 if transpose_a or m < 512 else max(1, min(chunks, m // 256))
     bounds = [round(i * m / nchunks) // 128 * 128 for i in range(nchunks)] + [m]
+    # In 3xTF32 every product splits op(B) first; with several row blocks it is split once, as
+    # soon as it has arrived, and shared (bit-identical to splitting it for each block).
+    split_b = None
+    if nchunks > 1 and k > 0 and n > 0 and \
+            (get_default_precision() if precision in (None, "default") else precision) == "3xtf32":
+        b_ready = torch.cuda.Event()
+        b_ready.record(copy_in)
+        compute.wait_event(b_ready)
+        split_b = pack_b(right_d, precision="3xtf32")
     d_a = torch.empty_like(left, device=dev) if not transpose_a else None
     d_c = torch.empty((m, n), dtype=torch.float32, device=dev) if c is not None else None
     for i in range(nchunks):
@@ -197,8 +206,12 @@ def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activa
         ready = torch.cuda.Event()
         ready.record(copy_in)
         compute.wait_event(ready)
-        gemm(a_blk, right_d, alpha, c_blk, beta, False, False, bias=d_bias,
-             activation=activation, precision=precision, out=d_out[r0:r1])
+        if split_b is not None:
+            gemm_prepacked(a_blk, split_b, alpha, c_blk, beta, bias=d_bias,
+                           activation=activation, precision="3xtf32", out=d_out[r0:r1])
+        else:
+            gemm(a_blk, right_d, alpha, c_blk, beta, False, False, bias=d_bias,
+                 activation=activation, precision=precision, out=d_out[r0:r1])
         done = torch.cuda.Event()
         done.record(compute)
         copy_out.wait_event(done)
@@ -210,6 +223,8 @@ def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activa
             t.record_stream(copy_out)
             t.record_stream(copy_in)
     copy_out.synchronize()
+    if split_b is not None:
+        split_b.free()  # every product that read it has finished
     return out
 
 
