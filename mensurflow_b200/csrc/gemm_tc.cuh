@@ -972,10 +972,18 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
         uint32_t ra[kEpiCols], rb[kEpiCols];
         tmem_ld_issue_32x32b_x16(tbase, ra);
         tmem_ld_wait();
+        // Chunk pairs, the pair's two chunks unrolled (each with its own register set). With
+        // eight epilogue warps two copies of the chunk code instead of kChunks keep the epilogue
+        // within the instruction cache; the four-warp ATMEM epilogue, at its register limit,
+        // keeps every chunk unrolled.
+        constexpr int kPairUnroll = ATMEM ? kChunks / 2 : 1;
+#pragma unroll kPairUnroll
+        for (int cp = 0; cp < kChunks; cp += 2) {
 #pragma unroll
-        for (int ci = 0; ci < kChunks; ++ci) {
-            uint32_t (&r)[kEpiCols] = (ci & 1) ? rb : ra;
-            uint32_t (&rn)[kEpiCols] = (ci & 1) ? ra : rb;
+        for (int h = 0; h < 2; ++h) {
+            const int ci = cp + h;
+            uint32_t (&r)[kEpiCols] = h ? rb : ra;
+            uint32_t (&rn)[kEpiCols] = h ? ra : rb;
             if (ci + 1 < kChunks) tmem_ld_issue_32x32b_x16(tbase + (ci + 1) * kEpiCols, rn);
             const int col0 = tc.tn * BN + half * kHalf + ci * kEpiCols;
             if (col0 < g.n && row0 < g.m) {
@@ -1008,7 +1016,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                     box ^= 1;
                 } else if (g.c_peer) {
                     // stage the chunk (box ci & 1); the pair is written below as 128-byte rows
-                    const uint32_t buf = box0 + (ci & 1) * C::kEpiBoxBytes;
+                    const uint32_t buf = box0 + h * C::kEpiBoxBytes;
 #pragma unroll
                     for (int q = 0; q < kEpiCols / 4; ++q) {
                         st_shared_v4(buf + lane * (kEpiCols * 4) + ((q ^ ((lane >> 1) & 3)) << 4),
@@ -1029,7 +1037,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                     }
                 }
             }
-            if (g.c_peer && (ci & 1)) {
+            if (g.c_peer && h == 1) {
                 // C in another GPU's memory: every request crosses NVLink, so the two staged
                 // chunks (32 columns) go out as full 128-byte row segments — eight lanes per row,
                 // four rows per store instruction — instead of one 16-byte piece per lane.
@@ -1064,6 +1072,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                 __syncwarp();
             }
             if (ci + 1 < kChunks) tmem_ld_wait();
+        }
         }
         tc_fence_before();
         __syncwarp();
