@@ -765,7 +765,8 @@ __device__ __forceinline__ void sk_fixup_tmem(const GemmArgs& g, uint32_t tbase,
 // tile is replaced by the plain fp32 dot product from the operands in memory, in tensor memory
 // before the epilogue reads it. Entries the tensor cores got right are not touched, and tiles
 // that cannot hold such an entry never come here (the flags the packing passes and the
-// converter warps raise on meeting an infinity).
+// converter warps raise on meeting an infinity). B is read as its packed hi, which keeps every
+// sign, zero and infinity of B (only a denormal below 2^-136 truncates to zero).
 __device__ __forceinline__ float nonfinite_dot(const GemmArgs& g, int b, int row, int col) {
     const float* a = g.ra + static_cast<long long>(b) * g.ra_bs + static_cast<long long>(row) * g.ra_rs;
     const float* x = g.rb + static_cast<long long>(b) * g.rb_bs + static_cast<long long>(col) * g.rb_rs;
@@ -804,6 +805,7 @@ __device__ __forceinline__ void nonfinite_fixup_tmem(const GemmArgs& g, uint32_t
             tmem_ld_issue_32x32b_x1(taddr, v);
             tmem_ld_wait();
             if (nan_mask & (1u << j)) v = __float_as_uint(nonfinite_dot(g, b, row, col0 + j));
+            __syncwarp();  // the store below is warp-collective
             tmem_st_32x32b_x1(taddr, v);
         }
     }
