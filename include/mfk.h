@@ -138,7 +138,8 @@ int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream);
  * stride ld_gathered on devices[root]) at row offset sum_{q<r} per_rank[q].m — the ranks on other
  * GPUs write over NVLink (peer access is enabled here), so the gather needs no extra kernel or
  * collective — and streams[root] waits for every rank, so work queued on it after this call sees
- * the whole C. The reference has no multi-device path (its GEMM runs on one device); this is the
+ * the whole C; the ranks' writes in turn start only after the work queued on streams[root] before
+ * this call (a reader of the previous contents of `gathered`, for one). The reference has no multi-device path (its GEMM runs on one device); this is the
  * row-block partition plus the gather that a single-device result needs, in place of an NCCL
  * all-gather of C. Returns once every launch is queued; the caller's current device is kept. */
 int mfk_sharded_gemm_f32(const mfk_gemm_desc* per_rank, int32_t nranks, const int32_t* devices,

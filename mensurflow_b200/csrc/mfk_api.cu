@@ -781,6 +781,27 @@ int mfk_sharded_gemm_f32(const mfk_gemm_desc* per_rank, int32_t nranks, const in
         ~Restore() { cudaSetDevice(dev); }
     } restore{caller_device};
     const int root_dev = gather ? devices[root] : 0;
+    // one queue: the same stream on the same device (NULL is each device's own default stream)
+    auto same_queue = [&](int r, int q) {
+        return devices[r] == devices[q] && streams[r] == streams[q];
+    };
+    if (gather) {
+        // No rank writes into `gathered` before the work already queued on the root's stream
+        // (a reader of its previous contents, for one) has finished.
+        MFK_CUDA(cudaSetDevice(root_dev));
+        cudaEvent_t ready;
+        MFK_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+        struct DestroyEvent {
+            cudaEvent_t e;
+            ~DestroyEvent() { cudaEventDestroy(e); }
+        } ready_owner{ready};
+        MFK_CUDA(cudaEventRecord(ready, static_cast<cudaStream_t>(streams[root])));
+        for (int r = 0; r < nranks; ++r) {
+            if (same_queue(r, root)) continue;
+            MFK_CUDA(cudaSetDevice(devices[r]));
+            MFK_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(streams[r]), ready, 0));
+        }
+    }
     int64_t row0 = 0;
     for (int r = 0; r < nranks; ++r) {
         mfk_gemm_desc d = per_rank[r];
@@ -810,7 +831,7 @@ int mfk_sharded_gemm_f32(const mfk_gemm_desc* per_rank, int32_t nranks, const in
     if (gather) {
         // The gathered C is complete on the root's stream once every rank's GEMM has finished.
         for (int r = 0; r < nranks; ++r) {
-            if (r == root || streams[r] == streams[root]) continue;
+            if (same_queue(r, root)) continue;
             MFK_CUDA(cudaSetDevice(devices[r]));
             cudaEvent_t ev;
             MFK_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));

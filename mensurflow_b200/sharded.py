@@ -172,7 +172,10 @@ def sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, m_total: int, alpha: fl
     gather=False: returns this rank's rows. gather=True or "nccl": every rank receives the whole
     [m_total, N] C through NCCL's all-gather. gather="peer": this rank's GEMM writes its rows into
     `peer.buffer` on the root over NVLink (no collective on the data path); after a barrier on the
-    current streams the root holds C — the root gets the buffer back, the others None.
+    current streams the root holds C — the root gets the buffer back, the others None. The buffer
+    is reused by the next call: a barrier before the GEMMs keeps every rank from writing into it
+    until the root's current stream has finished the work queued before the call (reading the
+    previous C, for one); read it on another stream only after synchronising with that one.
 
     `gemm_fn` defaults to the B200 kernel (mensurflow_b200.ops.gemm); it is a parameter so the
     host logic can be exercised with CPU ranks."""
@@ -185,10 +188,12 @@ def sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, m_total: int, alpha: fl
     if gather == "peer":
         if peer is None or peer.rows != m_total:
             raise ValueError("sharded_gemm: gather='peer' needs the PeerRowGather of C")
+        # the root is done with the previous contents once every rank has reached this call
+        flag = torch.zeros(1, device=a_local.device)
+        dist.all_reduce(flag, group=group)
         gemm_into_peer(a_local, b, alpha, c_local, beta, transpose_b, peer.row_ptr(start),
                        peer.cols, bias=bias, activation=activation, precision=precision)
         # every rank's rows have landed once every rank's GEMM has finished
-        flag = torch.zeros(1, device=a_local.device)
         dist.all_reduce(flag, group=group)
         return peer.buffer if rank == peer.root else None
     if gemm_fn is None:
