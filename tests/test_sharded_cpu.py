@@ -157,3 +157,70 @@ def test_a_rank_that_leaves_makes_the_gather_fail_not_hang():
     results = dict(q.get(timeout=10) for _ in procs)
     assert results[1] == "ValueError"
     assert results[0].startswith("error after"), results[0]
+
+
+class _SharedRows:
+    """CPU stand-in for PeerRowGather: the root's buffer is shared memory every rank writes its
+    rows into; row_ptr() hands out the row index in place of a device address."""
+
+    def __init__(self, buffer, root, rank):
+        self.rows, self.cols = buffer.shape
+        self.root = root
+        self.shared = buffer
+        self.buffer = buffer if rank == root else None
+
+    def row_ptr(self, row):
+        return row
+
+
+def _reuse_worker(rank, world, port, buffer, q):
+    sys.path.insert(0, ROOT)
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mensurflow_b200 import sharded
+
+        peer = _SharedRows(buffer, 0, rank)
+
+        def rows_into_shared(a, b, alpha, c, beta, transpose_b, row0, ldc, *, bias=None,
+                             activation=None, precision=None):
+            peer.shared[row0:row0 + a.shape[0]] = oracle_gemm(a, b, alpha, c, beta, False,
+                                                              transpose_b)
+
+        sharded.gemm_into_peer = rows_into_shared
+        m, n, k = 48, 24, 16
+        g = torch.Generator().manual_seed(5)
+        a, b, c = torch.randn(m, k, generator=g), torch.randn(k, n, generator=g), torch.zeros(m, n)
+        start, stop = sharded.block_range(m, world, rank)
+        ok = True
+        for step in range(3):
+            full = sharded.sharded_gemm(a[start:stop], b, m, 1.0 + step, c[start:stop], 0.0,
+                                        gather="peer", peer=peer)
+            if rank == 0:
+                time.sleep(0.5)  # a slow reader: the other rank must not start the next step
+                ok = ok and torch.equal(full, oracle_gemm(a, b, 1.0 + step, None, 0.0, False,
+                                                          False))
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_gather_buffer_not_overwritten_while_the_root_reads():
+    """gather='peer' reuses the root's buffer from call to call: a rank must not write its next
+    rows while the root is still reading the previous C (the barrier before the GEMMs). The
+    root here reads slowly after each call; the other rank would overwrite its rows at once."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    buffer = torch.zeros(48, 24).share_memory_()
+    procs = [ctx.Process(target=_reuse_worker, args=(r, 2, port, buffer, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    results = dict(q.get(timeout=10) for _ in procs)
+    assert all(p.exitcode == 0 for p in procs)
+    assert results == {0: True, 1: True}
