@@ -175,3 +175,25 @@ def test_strided_copy_restatement_matches_reference_views():
         want = gold[case[0]]
         assert got.shape == want.shape, case[0]
         assert np.array_equal(got, want), case[0]
+
+
+@pytest.mark.skipif(O.reference() is None, reason="reference library not built here")
+@pytest.mark.parametrize("shape", [(300, 64, 200), (100, 1000, 70)])
+def test_restatement_matches_reference_on_infinite_operands(shape):
+    """The ±inf / NaN pattern the GPU tests hold the kernels to (tests/test_gemm_gpu.py,
+    test_infinite_operands*) is the restatement's: pinned here to the reference built from its
+    sources, entry for entry, with infinities that meet zeros, each other and finite values."""
+    m, n, k = shape
+    rng = np.random.default_rng(m + n + k)
+    a = (rng.integers(-16, 17, (m, k)) / 4).astype(np.float32)
+    b = (rng.integers(-16, 17, (k, n)) / 4).astype(np.float32)
+    a[3, 5] = np.inf
+    a[m // 2, 2] = -np.inf
+    a[m // 2, 9] = np.inf
+    b[7, n - 1] = np.inf
+    b[11, 0] = np.nan
+    want = O.ref_gemm(a, b)
+    got = O.gemm(a, b)
+    assert (~np.isfinite(want)).any()
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(want))
+    np.testing.assert_array_equal(got[~np.isnan(want)], want[~np.isnan(want)])
