@@ -115,9 +115,13 @@ int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream);
  * in device memory (a static __device__ array: every GPU that loads the library holds it until
  * the process exits). It calls no cudaMalloc/cudaFree or other allocating routine.
  *
- * Same descriptor, same arithmetic and same results as mfk_gemm_f32; the caller still provides
- * every input and the output. The operand copies must fit: 4 bytes x (number of copies) x
- * (rows of each packed operand) x k rounded up to 32. 3xTF32 packs B (n rows) twice, and A
+ * Same descriptor and the same error bound as mfk_gemm_f32 (3xTF32: |C - C_ref| <= 1e-5 *
+ * (|A||B|)_ij + 1e-6; 1xTF32: 2e-3 relative), but not always the same bits: this entry point
+ * never uses the stream-K schedule (whose partial tiles would need memory of their own), so on
+ * shapes where mfk_gemm_f32 shares the last wave's tiles by k-iterations the two sum in a
+ * different order. The caller still provides every input and the output. The operand copies
+ * must fit: 4 bytes x (number of copies) x (rows of each packed operand) x k rounded up to 32,
+ * plus 256 bytes per packed operand and one more word. 3xTF32 packs B (n rows) twice, and A
  * (m rows) twice only when TMA cannot read it where it lies (not K-major, or rows not 16-byte
  * aligned); 1xTF32 packs once only an operand TMA cannot read. Larger problems return
  * MFK_ERR_SCRATCH_LIMIT before anything is launched.

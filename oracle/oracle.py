@@ -331,6 +331,17 @@ def ref_gemm(a, b, alpha=1.0, c=None, beta=0.0, transpose_a=False, transpose_b=F
     return out
 
 
+def ref_matmul(a, b):
+    """The reference's public matmul (src/ops/blas.cpp:186-232) on the CPU."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    out = np.empty((m, n), np.float32)
+    _check_ref(reference().mfref_matmul(_p(a), m, k, _p(b), n, _p(out)))
+    return out
+
+
 def ref_gemm_strided_batched(a, b, alpha=1.0, c=None, beta=0.0, transpose_a=False,
                              transpose_b=False):
     a = np.ascontiguousarray(a, np.float32)

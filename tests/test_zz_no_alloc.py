@@ -3,9 +3,9 @@
 It exists for callers that cannot allocate device memory while they run (a host that reserves
 its whole memory plan up front, or a framework whose caching allocator owns the device); it
 keeps the tf32 operand copies in a fixed scratch array inside the library instead. Its results
-must match the allocating entry point (mfk_gemm_f32) on the same inputs, call after call — the
-scratch array keeps the previous call's contents, so two calls in a row with different inputs
-check that nothing stale leaks into a result.
+must meet the path's bound against both the allocating entry point (mfk_gemm_f32) and the oracle
+on the same inputs, call after call — the scratch array keeps the previous call's contents, so two
+calls in a row with different inputs check that nothing stale leaks into a result.
 
 The file is named to be collected last: a failure here leaves every other test already run.
 """
@@ -44,28 +44,44 @@ def _call(fn, desc):
     assert rc == _lib.MFK_OK, _lib.lib().mfk_status_string(rc).decode()
 
 
+# (m, n, k, transpose_a, transpose_b): A read in place with B packed (both layouts of B); A
+# transposed, so it is not K-major and is packed into the scratch array as well (two packed
+# operands plus the infinity flag word after them); and a shape whose last wave
+# mfk_gemm_f32 shares out by k-iterations (stream-K) while this entry point keeps whole tiles,
+# so the two entry points may differ in the last bits but both must meet the bound.
+CASES = [(700, 520, 1000, False, True), (700, 520, 1000, False, False),
+         (640, 384, 900, True, False), (1024, 300, 2048, False, False)]
+
+
 @pytest.mark.parametrize("precision,tol", [(_lib.PRECISION_3XTF32, TOL_3X),
                                            (_lib.PRECISION_1XTF32, TOL_1X)])
-@pytest.mark.parametrize("transpose_b", [True, False])
-def test_noalloc_matches_allocating_entry_point(cuda, precision, tol, transpose_b):
+@pytest.mark.parametrize("m,n,k,transpose_a,transpose_b", CASES)
+def test_noalloc_matches_allocating_entry_point(cuda, precision, tol, m, n, k, transpose_a,
+                                                transpose_b):
     so = _lib.lib()
-    m, n, k = 700, 520, 1000
     for call in range(2):  # two calls in a row, different inputs each time
         rng = np.random.default_rng(100 + call)
-        a = rng.standard_normal((m, k)).astype(np.float32)
+        a = rng.standard_normal((k, m) if transpose_a else (m, k)).astype(np.float32)
         b = rng.standard_normal((n, k) if transpose_b else (k, n)).astype(np.float32)
         c = rng.standard_normal((m, n)).astype(np.float32)
         bias = rng.uniform(-0.1, 0.1, n).astype(np.float32)
         ta, tb, tc, tbias = (torch.from_numpy(x).to(cuda) for x in (a, b, c, bias))
+        left = ta.t() if transpose_a else ta
         want = torch.full((m, n), float("nan"), device=cuda)
         got = torch.full((m, n), float("nan"), device=cuda)
-        _call(so.mfk_gemm_f32, _desc(ta, tb, tc, want, 0.5, 1.0, tbias, precision, transpose_b))
+        _call(so.mfk_gemm_f32,
+              _desc(left, tb, tc, want, 0.5, 1.0, tbias, precision, transpose_b))
         _call(so.mfk_gemm_f32_noalloc,
-              _desc(ta, tb, tc, got, 0.5, 1.0, tbias, precision, transpose_b))
+              _desc(left, tb, tc, got, 0.5, 1.0, tbias, precision, transpose_b))
         torch.cuda.synchronize()
-        mag = 0.5 * O.abs_product(a, b, False, transpose_b) + np.abs(c) + np.abs(bias)[None, :]
-        assert_close(got.cpu().numpy(), want.cpu().numpy(), mag, tol,
-                     f"no-alloc call {call + 1}")
+        got_h = got.cpu().numpy()
+        mag = (0.5 * O.abs_product(a, b, transpose_a, transpose_b) + np.abs(c) +
+               np.abs(bias)[None, :])
+        # against the allocating entry point ...
+        assert_close(got_h, want.cpu().numpy(), mag, tol, f"no-alloc call {call + 1}")
+        # ... and against the oracle (the reference's algorithm on the CPU)
+        oracle = O.gemm(a, b, 0.5, c, 1.0, transpose_a, transpose_b, bias=bias)
+        assert_close(got_h, oracle, mag, tol, f"no-alloc call {call + 1} vs the oracle")
     assert _lib.device_status() == 0
 
 
