@@ -17,8 +17,15 @@ into the GEMM is timed against NCCL's all-gather), `gemv` (65536 x 8192, HBM-bou
 (Tensor::contiguous of an 8192^2 view on the device, `--view transpose|slice|stepped`).
 Every workload reports the reference's own CPU path on a bounded sample as `cpu_baseline`.
 
+The default C2 line also carries `sustained` (the same step back to back for ~2.5 s, with its own
+clock record, against the sustained GEMM peak) and `c5` (the C5 strong-scaling GEMM at the same
+N: per-N step and kernel times, and at N > 1 NCCL's all-gather of C and the gather fused into the
+GEMM, with the GB/s into rank 0), so one SCALE run gives both the C2 weak and the C5 strong
+scaling. The JSON line is the last line of stdout.
+
 `--impl reference` times the reference's own CPU implementation (the unmodified library built
-from its sources into oracle/_ref) on a bounded row sample of the same workload; rank 0 only.
+from its sources into oracle/_ref, public gemm + bias_add, all host threads) on the whole C2
+problem every step; rank 0 only.
 """
 from __future__ import annotations
 
@@ -63,6 +70,12 @@ def parse_args():
                         "matrix, read as 16-byte rows; every other column, a gather)")
     p.add_argument("--mnk", type=str, default=None,
                    help="c2: 'M,N,K' per rank instead of --size; gemv: 'M,1,K' (profiling shapes)")
+    p.add_argument("--c5-steps", type=int, default=10,
+                   help="c2 at 8192: steps of the C5 strong-scaling leg reported as `c5` beside "
+                        "the C2 line (0 skips it)")
+    p.add_argument("--sustained-s", type=float, default=2.5,
+                   help="c2 at 8192: seconds of back-to-back steps for the `sustained` figure (0 "
+                        "skips it)")
     return p.parse_args()
 
 
@@ -271,27 +284,179 @@ def run_reference_arm(args):
         emit({"impl": "reference", "unavailable": "oracle/_ref/libmfref.so (the reference built "
               "from its sources) is not present on this machine"})
         return 0
+
     n = k = 8192
-    # each step is a bounded row sample sized to ~0.3 s so K steps end within minutes
-    res = cpu_gemm_sample(8192, n, k, target_s=0.3, reps=args.steps, warmup=args.warmup)
-    secs, rows, kind, cores = res
+    ref = O.reference()
+    ref.mfref_set_threads(host_threads())
+    cores = int(ref.mfref_max_threads())
+    # each step is the whole C2 problem (one 8192-row block; ~0.8 s on 16 host threads), on
+    # inputs the reference's own Philox factories made once
+    bench = O.RefGemmBench(8192, n, k, True, 1)
+    if args.warmup:
+        bench.run(0.5, 1.0, True, max(1, min(args.warmup, 3)))
+    secs = list(bench.run(0.5, 1.0, True, args.steps))
+    bench.close()
     per = statistics.median(secs)
-    flops = 2.0 * rows * n * k
+    flops = 2.0 * 8192 * n * k
     value = flops / per / 1e12
     emit({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (the reference's Philox normal/uniform)",
-        "config": {"workload": "C2 gemm 8192^3 alpha=0.5 beta=1 transB + bias_add, CPU row sample",
-                   "sample_rows": rows, "n": n, "k": k},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": kind,
-                         "sample": f"{rows} of 8192 rows of A/C_in (B, bias full), "
-                                   f"median of {len(secs)} timed calls"},
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (the reference's Philox normal/uniform)",
+        "config": {"workload": "C2: fused gemm C = 0.5*A@B^T + 1.0*C_in + bias, M=8192 N=8192 "
+                               "K=8192 per rank (the reference's public gemm + bias_add on the "
+                               "host CPU; at N > 1 GPUs the CPU's throughput is that of one "
+                               "8192-row block, whatever the number of blocks)",
+                   "precision": "fp32 (the reference's CPU packed GEMM)",
+                   "m_per_rank": 8192, "n": n, "k": k, "same_config": True},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+                         "sample": f"the whole C2 problem (all 8192 rows), median of "
+                                   f"{len(secs)} timed calls, {per:.2f} s each"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     })
     return 0
+
+
+# ---- legs reported beside the main line ------------------------------------------------------
+
+def time_back_to_back(step, seconds, ms_hint, stream, barrier, max_over_ranks, gpu_index):
+    """Steps run back to back for about `seconds` of device time (so the GPU settles under its
+    power cap), with their own clock record. Returns the sub-object of the JSON line."""
+    from mensurflow_b200 import _lib
+    import torch
+
+    n = max(10, int(seconds * 1e3 / max(ms_hint, 1e-3)) + 1)
+    clocks = ClockSampler(gpu_index)
+    clocks.start()
+    time.sleep(0.25)
+    _lib.kernel_timer(True)
+    _lib.kernel_timer_read()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    kern_ms, _ = _lib.kernel_timer_read()
+    _lib.kernel_timer(False)
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    kern = max_over_ranks(kern_ms / n)
+    return {"steps": n, "seconds": ms * n / 1e3, "ms_per_step": ms, "kernel_ms_per_step": kern,
+            "clocks": clk}
+
+
+def c5_strong_scaling(args, world, rank, device, gen, barrier, max_over_ranks, stream, peaks,
+                      dist):
+    """C5: 32768 x 32768 x 8192, alpha 1, beta 0, A and B uniform
+    [-1, 1), rows of A and C split over the ranks with B replicated (strong scaling: the total work
+    is fixed). Each rank writes its own slice; the gather of C to rank 0 is timed apart, both as
+    NCCL's all_gather_into_tensor and fused into the GEMM (each rank's epilogue stores its rows
+    into rank 0's buffer over NVLink)."""
+    import mensurflow_b200 as mf
+    from mensurflow_b200 import _lib
+    import torch
+
+    m_total, n, k = 32768, 32768, 8192
+    m = m_total // world
+    A = torch.rand(m, k, device=device, generator=gen) * 2 - 1
+    B = torch.rand(k, n, device=device, generator=gen) * 2 - 1
+    out = torch.empty(m, n, device=device)
+    flops = 2.0 * m_total * n * k
+
+    def step():
+        mf.gemm(A, B, 1.0, None, 0.0, out=out, precision=args.precision)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.25)
+    _lib.kernel_timer(True)
+    _lib.kernel_timer_read()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.c5_steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    kern_ms, _ = _lib.kernel_timer_read()
+    _lib.kernel_timer(False)
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.c5_steps)
+    kern = max_over_ranks(kern_ms / args.c5_steps)
+    per_product = 3.0 if args.precision == "3xtf32" else 1.0
+    peak = peaks["bf16_burst"] / 2.0 / per_product
+    res = {"workload": "C5: gemm 32768x32768x8192, alpha=1 beta=0, uniform[-1,1) inputs, rows "
+                       "of A and C split over the ranks, B replicated (strong scaling)",
+           "m_per_rank": m, "n": n, "k": k, "steps": args.c5_steps, "ms_per_step": ms,
+           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "scaling": "strong",
+           "kernel_ms_per_step": kern,
+           "per_gpu_kernel_frac": (flops / world) / (kern * 1e-3) / 1e12 / peak,
+           "clocks": clk, "parallelism": f"dp{world} row blocks, each rank writes its own slice"}
+    if world > 1:
+        from mensurflow_b200 import sharded
+
+        def t_steps(fn, reps=5):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            barrier()
+            h0 = torch.cuda.Event(enable_timing=True)
+            h1 = torch.cuda.Event(enable_timing=True)
+            h0.record(stream)
+            for _ in range(reps):
+                fn()
+            h1.record(stream)
+            torch.cuda.synchronize()
+            return max_over_ranks(h0.elapsed_time(h1) / reps)
+
+        g_ms = t_steps(lambda: sharded.gather_rows(out, m_total))
+        peer = sharded.PeerRowGather(m_total, n, device, root=0)
+        flag = torch.zeros(1, device=device)
+
+        def fused_step():
+            sharded.gemm_into_peer(A, B, 1.0, None, 0.0, False, peer.row_ptr(rank * m), n,
+                                   precision=args.precision)
+            dist.all_reduce(flag)
+
+        def barrier_step():
+            step()
+            dist.all_reduce(flag)
+
+        f_runs, b_runs = [], []
+        for _ in range(2):  # alternated, so clock drift under the power cap hits both alike
+            f_runs.append(t_steps(fused_step))
+            b_runs.append(t_steps(barrier_step))
+        f_ms, b_ms = min(f_runs), min(b_runs)
+        peer.close()
+        into_root = 4.0 * (m_total - m) * n
+        res.update({
+            "nccl_all_gather_ms": g_ms,
+            "nccl_all_gather_what": "NCCL all_gather_into_tensor of the C row blocks, alone",
+            "gathered": {
+                "ms_per_step": f_ms, "value": flops / (f_ms * 1e-3) / 1e12,
+                "gemm_with_step_barrier_ms": b_ms,
+                "bytes_into_rank0_per_step": into_root,
+                "gbs_into_rank0": into_root / (f_ms * 1e-3) / 1e9,
+                "what": "each rank's GEMM epilogue stores its rows into rank 0's C over NVLink "
+                        "(CUDA IPC mapping), then a 1-element all_reduce as the step barrier; "
+                        "rank 0 then holds the whole C"}})
+    del A, B, out
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---- my arm -----------------------------------------------------------------------------------
@@ -311,7 +476,6 @@ def main():
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    os.environ["NCCL_DEBUG"] = "WARN"  # keep rank 0's stdout to the one JSON line
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
@@ -822,10 +986,34 @@ def main():
             and args.workload in ("c3", "c4", "c5", "gemv") and not args.mnk):
         cpu_baseline = reference_cpu_baseline(args, m, n, k)
 
+    # the same step back to back for a few seconds: the figure under the power cap, against the
+    # sustained GEMM peak
+    sustained = None
+    if args.sustained_s > 0 and args.workload == "c2" and not args.mnk and args.size == 8192:
+        sustained = time_back_to_back(step, args.sustained_s, ms, stream, barrier,
+                                      max_over_ranks, local)
+        sus_achieved = flops_rank / (sustained["kernel_ms_per_step"] * 1e-3) / 1e12
+        sustained.update({
+            "value": world * flops_rank / (sustained["ms_per_step"] * 1e-3) / 1e12,
+            "unit": unit, "kernel_achieved": sus_achieved,
+            "frac_of_sustained_peak": sus_achieved / peak_sustained,
+            "sustained_peak": peak_sustained,
+            "peak_source": f"{peaks['source']} bf16 sustained {peaks['bf16_sustained']} "
+                           f"TFLOP/s / 2 (TF32) / {int(per_product)} ({args.precision})"})
+
+    # C5 strong scaling beside the C2 line (same line at every N, so the 1 -> 8 GPU scaling of
+    # the sharded GEMM is read from SCALE's per-N `c5` objects)
+    c5 = None
+    if args.c5_steps > 0 and args.workload == "c2" and not args.mnk and args.size == 8192 \
+            and 32768 % world == 0:
+        c5 = c5_strong_scaling(args, world, rank, device, gen, barrier, max_over_ranks, stream,
+                               peaks, dist)
+
     metric = {"gemv": "gemv HBM GB/s (65536x8192 fp32)",
               "copy": "strided copy GB/s (Tensor::contiguous of a transposed 8192^2 fp32 view)"}
+    line = None
     if rank == 0:
-        emit({
+        line = {
             "metric": metric.get(args.workload, METRIC),
             "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
@@ -835,10 +1023,13 @@ def main():
                        "k": k, "parallelism": f"dp{world} row-block shards, no collective",
                        "l2": l2_note},
             "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu_baseline,
-            "e2e": e2e, "clocks": clk, "allgather": allgather,
-        })
+            "e2e": e2e, "clocks": clk, "allgather": allgather, "sustained": sustained, "c5": c5,
+        }
     if world > 1:
         dist.destroy_process_group()
+    # the JSON line last on stdout, after anything NCCL prints while the group shuts down
+    if line is not None:
+        emit(line)
     return 0
 
 

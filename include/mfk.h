@@ -262,6 +262,35 @@ int mfk_strided_copy_f32(const float* x, const int64_t* shape, const int64_t* st
  * src/backends/cpu/backend.cpp:110-113 -> cpu::copy_f32; op: src/ops/blas.cpp:106-117). */
 int mfk_copy_f32(const float* x, float* out, int64_t n, void* stream);
 
+/* Elementwise out[i] = x[i] op y[i] over n contiguous elements, one IEEE fp32 operation per
+ * element (round to nearest, no contraction), bit-identical to the CPU backend's add_f32 / sub_f32
+ * / mul_f32 / div_f32 (src/backends/cpu/backend.cpp:865-868, via binary_kernel :595-598). Replaces
+ * the reference's CUDA Add/Sub/Mul kernels, which composed a copy with cublasSaxpy and used
+ * cublasSdgmm (src/backends/cuda/backend.cpp:160-191), and adds Div, which it lacked. The op layer
+ * expands and packs broadcast inputs first (src/ops/elementwise.cpp:158-225). out may be x or
+ * y. */
+typedef enum mfk_binary_op {
+    MFK_BINARY_ADD = 0,
+    MFK_BINARY_SUB = 1,
+    MFK_BINARY_MUL = 2,
+    MFK_BINARY_DIV = 3
+} mfk_binary_op;
+int mfk_binary_f32(int32_t op, const float* x, const float* y, float* out, int64_t n,
+                   void* stream);
+
+/* out[i] = alpha * x[i] over n contiguous elements: the OpId::Scal kernel (CPU adapter
+ * src/backends/cpu/backend.cpp:95-98 -> cpu::scal_f32, src/backends/cpu/ops/blas/blas.cpp:23),
+ * which the reference's gemm uses for beta * c (src/ops/blas.cpp:257) and which its CUDA backend
+ * lacked. Bit-identical to the CPU. out may be x. */
+int mfk_scal_f32(float alpha, const float* x, float* out, int64_t n, void* stream);
+
+/* *out = sum of x[i] * y[i] over n contiguous elements, the products summed in double and the sum
+ * rounded once to fp32, as cpu::dot_f32 does (src/backends/cpu/ops/blas/blas.cpp:14-21); replaces
+ * the reference's CUDA Dot kernel (cublasSdot, src/backends/cuda/backend.cpp:122-134). out is a
+ * device pointer to one float; n == 0 writes 0. The order of the double sum is fixed for a given
+ * n on a given GPU model, so repeated calls give the same bits. */
+int mfk_dot_f32(const float* x, const float* y, int64_t n, float* out, void* stream);
+
 /* Tensor::to(device) between two CUDA devices: `bytes` from src on src_device to dst on
  * dst_device, device to device over NVLink (a stream-ordered peer copy on `stream`), instead of
  * the reference's staging through a host std::vector (src/core/tensor.cpp:193-206). The same

@@ -6,12 +6,15 @@ mirrors the reference's op API over torch CUDA tensors, ``sharded`` splits a GEM
 from ._lib import MfkError, build  # noqa: F401
 from .ops import (  # noqa: F401
     PackedB,
+    add,
     attention,
     bias_add,
     bias_grad,
     contiguous,
     copy,
     device_status,
+    div,
+    dot,
     gelu,
     gemm,
     gemm_prepacked,
@@ -24,17 +27,20 @@ from .ops import (  # noqa: F401
     matmul,
     matmul_backward,
     matvec,
+    mul,
     pack_b,
     relu,
+    scal,
     set_default_precision,
     softmax,
+    sub,
     to,
     where,
 )
 
 __all__ = [
-    "MfkError", "PackedB", "build", "attention", "bias_add", "bias_grad", "contiguous",
-    "copy", "device_status",
+    "MfkError", "PackedB", "build", "add", "attention", "bias_add", "bias_grad", "contiguous",
+    "copy", "device_status", "div", "dot", "mul", "scal", "sub",
     "gelu", "gemm", "gemm_prepacked", "gemm_strided_batched", "gemv", "get_default_precision",
     "linear", "linear_backward", "log_softmax", "matmul", "matmul_backward", "matvec", "pack_b",
     "relu", "set_default_precision", "softmax", "to", "where",

@@ -26,6 +26,7 @@ IPC_HANDLE_BYTES = 64
 
 ACT_NONE, ACT_RELU, ACT_GELU, ACT_GELU_TANH = 0, 1, 2, 3
 PRECISION_DEFAULT, PRECISION_3XTF32, PRECISION_1XTF32 = -1, 0, 1
+BINARY_ADD, BINARY_SUB, BINARY_MUL, BINARY_DIV = 0, 1, 2, 3
 
 # Every symbol include/mfk.h declares.
 EXPORTED = (
@@ -50,6 +51,9 @@ EXPORTED = (
     "mfk_strided_copy_f32",
     "mfk_copy_f32",
     "mfk_copy_peer",
+    "mfk_binary_f32",
+    "mfk_scal_f32",
+    "mfk_dot_f32",
     "mfk_set_default_precision",
     "mfk_get_default_precision",
     "mfk_device_status",
@@ -143,6 +147,9 @@ def lib() -> ctypes.CDLL:
                                                 i32, vp, vp]
             so.mfk_copy_f32.argtypes = [vp, vp, i64, vp]
             so.mfk_copy_peer.argtypes = [vp, i32, vp, i32, i64, vp]
+            so.mfk_binary_f32.argtypes = [i32, vp, vp, vp, i64, vp]
+            so.mfk_scal_f32.argtypes = [f32, vp, vp, i64, vp]
+            so.mfk_dot_f32.argtypes = [vp, vp, i64, vp, vp]
             so.mfk_set_default_precision.argtypes = [i32]
             so.mfk_get_default_precision.restype = i32
             so.mfk_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]

@@ -12,10 +12,12 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "mfk.h"
 
+#include "blas1.cuh"
 #include "gemm_tc.cuh"
 #include "movement.cuh"
 #include "prep.cuh"
@@ -1286,6 +1288,92 @@ int mfk_copy_f32(const float* x, float* out, int64_t n, void* stream) {
     const int rc = current_device(&dev, &info);
     if (rc != MFK_OK) return rc;
     return launch_contig_copy(x, out, n, info, static_cast<cudaStream_t>(stream));
+}
+
+int mfk_binary_f32(int32_t op, const float* x, const float* y, float* out, int64_t n,
+                   void* stream_) {
+    if (op < MFK_BINARY_ADD || op > MFK_BINARY_DIV || n < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (n == 0) return MFK_OK;
+    if (x == nullptr || y == nullptr || out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const int64_t max_blocks = static_cast<int64_t>(info->sm_count) * 8;
+    const bool vec = aligned16(x) && aligned16(y) && aligned16(out) && n % 4 == 0;
+    const int64_t work = vec ? n / 4 : n;
+    const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((work + 255) / 256, max_blocks));
+    auto launch = [&](auto op_tag) {
+        constexpr int kOp = decltype(op_tag)::value;
+        if (vec) {
+            mfk::binary_vec4_kernel<kOp><<<blocks, 256, 0, stream>>>(
+                reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(y),
+                reinterpret_cast<float4*>(out), work);
+        } else {
+            mfk::binary_scalar_kernel<kOp><<<blocks, 256, 0, stream>>>(x, y, out, n);
+        }
+    };
+    switch (op) {
+    case MFK_BINARY_ADD: launch(std::integral_constant<int, mfk::kBinAdd>{}); break;
+    case MFK_BINARY_SUB: launch(std::integral_constant<int, mfk::kBinSub>{}); break;
+    case MFK_BINARY_MUL: launch(std::integral_constant<int, mfk::kBinMul>{}); break;
+    default: launch(std::integral_constant<int, mfk::kBinDiv>{}); break;
+    }
+    g_launches.fetch_add(1);
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+int mfk_scal_f32(float alpha, const float* x, float* out, int64_t n, void* stream_) {
+    if (n < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (n == 0) return MFK_OK;
+    if (x == nullptr || out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const int64_t max_blocks = static_cast<int64_t>(info->sm_count) * 8;
+    if (aligned16(x) && aligned16(out) && n % 4 == 0) {
+        const unsigned blocks =
+            static_cast<unsigned>(std::min<int64_t>((n / 4 + 255) / 256, max_blocks));
+        mfk::scal_vec4_kernel<<<blocks, 256, 0, stream>>>(
+            alpha, reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(out), n / 4);
+    } else {
+        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, max_blocks));
+        mfk::scal_scalar_kernel<<<blocks, 256, 0, stream>>>(alpha, x, out, n);
+    }
+    g_launches.fetch_add(1);
+    MFK_CUDA(cudaGetLastError());
+    return MFK_OK;
+}
+
+int mfk_dot_f32(const float* x, const float* y, int64_t n, float* out, void* stream_) {
+    if (n < 0 || out == nullptr) return MFK_ERR_INVALID_ARGUMENT;
+    if (n > 0 && (x == nullptr || y == nullptr)) return MFK_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    const int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (n == 0) {
+        MFK_CUDA(cudaMemsetAsync(out, 0, sizeof(float), stream));
+        return MFK_OK;
+    }
+    // two blocks of 256 threads per SM, each thread with eight float4 of each input at least
+    const int parts = static_cast<int>(std::max<int64_t>(
+        1, std::min<int64_t>((n + 8191) / 8192, static_cast<int64_t>(info->sm_count) * 2)));
+    double* partial = nullptr;
+    MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&partial), sizeof(double) * parts, stream));
+    const int vec = aligned16(x) && aligned16(y) ? 1 : 0;
+    mfk::dot_partial_kernel<<<parts, 256, 0, stream>>>(x, y, n, vec, partial);
+    mfk::dot_finish_kernel<<<1, 32, 0, stream>>>(partial, parts, out);
+    g_launches.fetch_add(2);
+    const cudaError_t launched = cudaGetLastError();
+    cudaFreeAsync(partial, stream);
+    if (launched != cudaSuccess) return cuda_fail(launched, "dot kernels");
+    return MFK_OK;
 }
 
 int mfk_copy_peer(void* dst, int32_t dst_device, const void* src, int32_t src_device,

@@ -8,11 +8,15 @@
 // and turn a non-zero status into the exceptions the reference uses (std::invalid_argument for
 // argument errors, std::runtime_error otherwise; src/backends/cuda/backend.cpp:22-34).
 //
-// Built only against the reference's headers (include/, src/); see INTEGRATION.md.
+// Built only against the reference's headers (include/, src/). With the op-layer patches of
+// host/patches applied to those sources (MENSURFLOW_HAS_OPID_GEMM), it also registers the
+// one-kernel gemm (OpId::Gemm, with bias and activation fused) and bias_add's bias gradient
+// (OpId::BiasGrad), and provides the device-to-device copy that Tensor::to() uses between GPUs.
 #include "backends/backend.hpp"
 #include "core/dispatcher.hpp"
 #include "core/registry.hpp"
 #include "core/tensor_access.hpp"
+#include "cuda_stream.hpp"
 #include "mfk.h"
 
 #include <cuda_runtime.h>
@@ -211,8 +215,12 @@ void gemm_batched_kernel(const OpArgs& args, Stream& stream) {
     check_mfk(mfk_gemm_strided_batched_f32(&d, &bd, s.raw()), "gemm_strided_batched");
 }
 
-// OpId::Gemm (the one-dispatch gemm of INTEGRATION.md's op-layer patch): inputs {a, b[, c]}
-// as op(a), op(b) views, out contiguous [m, n], alpha/beta in OpArgs.
+#ifdef MENSURFLOW_HAS_OPID_GEMM
+// OpId::Gemm, the whole of gemm in one kernel (patched src/ops/blas.cpp): inputs {op(a), op(b)}
+// as views with any strides, then c when beta != 0, then the bias when with_bias; out contiguous
+// [m, n]; alpha, beta and the activation in OpArgs. alpha * op(a) op(b), + beta * c, + bias and
+// the activation are rounded in the order gemm's composed ops and bias_add round them
+// (src/ops/blas.cpp:246-260, src/ops/elementwise.cpp:251-258).
 void gemm_kernel(const OpArgs& args, Stream& stream) {
     auto& s = cuda(stream);
     const Tensor& a = args.inputs[0];
@@ -231,16 +239,81 @@ void gemm_kernel(const OpArgs& args, Stream& stream) {
     d.n = out.size(1);
     d.k = a.size(1);
     d.alpha = args.alpha;
-    d.beta = args.inputs.size() > 2 ? args.beta : 0.0f;
-    if (args.inputs.size() > 2) {
+    const std::size_t with_c = args.inputs.size() - (args.with_bias ? 1 : 0) > 2 ? 1 : 0;
+    d.beta = with_c ? args.beta : 0.0f;
+    if (with_c) {
         const Tensor& c = args.inputs[2];
         d.c_in = TensorAccess::data<float>(c);
         d.c_in_rs = c.strides()[0];
         d.c_in_cs = c.strides()[1];
     }
-    d.activation = MFK_ACT_NONE;
+    if (args.with_bias) {
+        d.bias = TensorAccess::data<float>(args.inputs.back());
+    }
+    switch (args.activation) {
+    case 0:
+        d.activation = MFK_ACT_NONE;
+        break;
+    case 1:
+        d.activation = MFK_ACT_RELU;
+        break;
+    case 2:
+        d.activation = MFK_ACT_GELU;
+        break;
+    case 3:
+        d.activation = MFK_ACT_GELU_TANH;
+        break;
+    default:
+        throw std::invalid_argument("gemm: unknown activation");
+    }
     d.precision = MFK_PRECISION_DEFAULT;
     check_mfk(mfk_gemm_f32(&d, s.raw()), "gemm");
+}
+
+// OpId::BiasGrad (patched bias_add backward, src/ops/elementwise.cpp:263-283): the column sums
+// of a contiguous [rows, features] gradient in row order, the host loop's bits.
+void bias_grad_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& g = args.inputs[0];
+    const std::int64_t cols = g.dim() > 0 ? g.size(-1) : 1;
+    const std::int64_t rows = cols > 0 ? g.numel() / cols : 0;
+    check_mfk(mfk_bias_grad_f32(TensorAccess::data<float>(g), rows, cols, cols,
+                                TensorAccess::data<float>(args.outputs[0]), s.raw()),
+              "bias_grad");
+}
+#endif
+
+// OpId::Dot: contiguous 1-D x and y, a 0-d output on the device (src/ops/blas.cpp:41-68; the CPU
+// adapter, src/backends/cpu/backend.cpp:89-93, writes the same double-accumulated sum).
+void dot_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& x = args.inputs[0];
+    check_mfk(mfk_dot_f32(TensorAccess::data<float>(x), TensorAccess::data<float>(args.inputs[1]),
+                          x.numel(), TensorAccess::data<float>(args.outputs[0]), s.raw()),
+              "dot");
+}
+
+// OpId::Scal: out = alpha * x over a contiguous 1-D x (src/ops/blas.cpp:70-79; CPU adapter
+// src/backends/cpu/backend.cpp:95-98).
+void scal_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& out = args.outputs[0];
+    check_mfk(mfk_scal_f32(args.alpha, TensorAccess::data<float>(args.inputs[0]),
+                           TensorAccess::data<float>(out), out.numel(), s.raw()),
+              "scal");
+}
+
+// OpId::Add / Sub / Mul / Div: the op packs both inputs to the output's shape
+// (src/ops/elementwise.cpp:158-225), as the CPU adapter reads them (backend.cpp:595-598).
+template <int Op>
+void binary_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& out = args.outputs[0];
+    static const char* const names[] = {"add", "sub", "mul", "div"};
+    check_mfk(mfk_binary_f32(Op, TensorAccess::data<float>(args.inputs[0]),
+                             TensorAccess::data<float>(args.inputs[1]),
+                             TensorAccess::data<float>(out), out.numel(), s.raw()),
+              names[Op]);
 }
 
 // OpId::BiasAdd: contiguous x [batch, features], bias [features] (backend.cpp:762-767).
@@ -278,10 +351,10 @@ void gemv_kernel(const OpArgs& args, Stream& stream) {
 }
 
 // OpId::Copy: out = a packed copy of the input. The op hands over a contiguous input
-// (src/ops/blas.cpp:106-117); a strided input is gathered in the same launch, which is what
-// Tensor::contiguous() dispatches for a CUDA view once it routes through OpId::Copy instead of
-// the host (the patch in INTEGRATION.md; today src/core/tensor.cpp:224-229 stages through a host
-// vector). Same contract as the CPU adapter (src/backends/cpu/backend.cpp:110-113).
+// (src/ops/blas.cpp:106-117); a strided input is gathered in the same launch, which is what the
+// patched Tensor::contiguous() dispatches for a CUDA view instead of the unpatched host round
+// trip (src/core/tensor.cpp:224-229). Same contract as the CPU adapter
+// (src/backends/cpu/backend.cpp:110-113).
 void copy_kernel(const OpArgs& args, Stream& stream) {
     auto& s = cuda(stream);
     const Tensor& x = args.inputs[0];
@@ -383,10 +456,15 @@ class CudaBackend final : public Backend {
         dispatcher.register_kernel(key(OpId::LogSoftmax), softmax_kernel<1>);
         dispatcher.register_kernel(key(OpId::Where), where_kernel);
         dispatcher.register_kernel(key(OpId::Copy), copy_kernel);
+        dispatcher.register_kernel(key(OpId::Dot), dot_kernel);
+        dispatcher.register_kernel(key(OpId::Scal), scal_kernel);
+        dispatcher.register_kernel(key(OpId::Add), binary_kernel<MFK_BINARY_ADD>);
+        dispatcher.register_kernel(key(OpId::Sub), binary_kernel<MFK_BINARY_SUB>);
+        dispatcher.register_kernel(key(OpId::Mul), binary_kernel<MFK_BINARY_MUL>);
+        dispatcher.register_kernel(key(OpId::Div), binary_kernel<MFK_BINARY_DIV>);
 #ifdef MENSURFLOW_HAS_OPID_GEMM
         dispatcher.register_kernel(key(OpId::Gemm), gemm_kernel);
-#else
-        (void)gemm_kernel;
+        dispatcher.register_kernel(key(OpId::BiasGrad), bias_grad_kernel);
 #endif
     }
 
@@ -399,5 +477,24 @@ class CudaBackend final : public Backend {
 } // namespace
 
 void register_cuda_backend(Registry& registry) { registry.add(std::make_unique<CudaBackend>()); }
+
+void* cuda_stream_handle(Stream& stream) { return cuda(stream).raw(); }
+
+// Tensor::to() between CUDA devices (patched src/core/tensor.cpp): one stream-ordered copy on the
+// source device's stream, after the work that produced src, then a wait, as the host path's
+// copy_d2h + copy_h2d pair would have waited.
+bool cuda_device_copy(void* dst, int dst_index, const void* src, int src_index,
+                      std::size_t bytes) {
+    Backend* backend = Registry::instance().find(DeviceType::CUDA);
+    if (backend == nullptr) {
+        return false;
+    }
+    auto& s = cuda(backend->stream(src_index));
+    check_mfk(mfk_copy_peer(dst, dst_index, src, src_index, static_cast<std::int64_t>(bytes),
+                            s.raw()),
+              "Tensor::to");
+    s.synchronize();
+    return true;
+}
 
 } // namespace mensurflow::detail

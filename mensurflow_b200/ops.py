@@ -638,6 +638,78 @@ def gelu(x: torch.Tensor, approximate: bool = False) -> torch.Tensor:
     return _bias_act(x, None, _lib.ACT_GELU_TANH if approximate else _lib.ACT_GELU, "gelu")
 
 
+def _binary(a: torch.Tensor, b: torch.Tensor, code: int, op: str) -> torch.Tensor:
+    """Elementwise a op b with NumPy broadcasting, as the reference's binary_op
+    (src/ops/elementwise.cpp:158-225): broadcast inputs are expanded and packed to the result's
+    shape, then one kernel pass computes it."""
+    _require(a, op, "a")
+    _require(b, op, "b")
+    if a.dtype != b.dtype:
+        raise ValueError(f"{op}: dtypes differ ({a.dtype} and {b.dtype})")
+    _same(op, a, b)
+    try:
+        shape = tuple(torch.broadcast_shapes(tuple(a.shape), tuple(b.shape)))
+    except RuntimeError:
+        raise ValueError(f"{op}: shapes {tuple(a.shape)} and {tuple(b.shape)} do not broadcast")
+    _kernel_for(op, a)
+    x = contiguous(a.expand(shape))
+    y = contiguous(b.expand(shape))
+    out = torch.empty(shape, dtype=torch.float32, device=a.device)
+    check(_lib.lib().mfk_binary_f32(code, x.data_ptr(), y.data_ptr(), out.data_ptr(), out.numel(),
+                                    _stream()), op)
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a + b, as mensurflow::add (elementwise.hpp; src/ops/elementwise.cpp:227)."""
+    return _binary(a, b, _lib.BINARY_ADD, "add")
+
+
+def sub(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a - b, as mensurflow::sub (src/ops/elementwise.cpp:231)."""
+    return _binary(a, b, _lib.BINARY_SUB, "sub")
+
+
+def mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a * b, as mensurflow::mul (src/ops/elementwise.cpp:235)."""
+    return _binary(a, b, _lib.BINARY_MUL, "mul")
+
+
+def div(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a / b, as mensurflow::div (src/ops/elementwise.cpp:239)."""
+    return _binary(a, b, _lib.BINARY_DIV, "div")
+
+
+def scal(alpha: float, x: torch.Tensor) -> torch.Tensor:
+    """alpha * x for a 1-D x, as mensurflow::scal (src/ops/blas.cpp:70-79)."""
+    _require(x, "scal", "x", dims=1)
+    _same("scal", x)
+    _kernel_for("scal", x)
+    xx = contiguous(x)
+    out = torch.empty_like(xx)
+    check(_lib.lib().mfk_scal_f32(float(alpha), xx.data_ptr(), out.data_ptr(), xx.numel(),
+                                  _stream()), "scal")
+    return out
+
+
+def dot(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """sum(a * b) of two 1-D tensors as a 0-d tensor on their device, as mensurflow::dot
+    (src/ops/blas.cpp:41-68): products summed in double, rounded once."""
+    _require(a, "dot", "a", dims=1)
+    _require(b, "dot", "b", dims=1)
+    if a.dtype != b.dtype:
+        raise ValueError(f"dot: dtypes differ ({a.dtype} and {b.dtype})")
+    _same("dot", a, b)
+    if a.shape[0] != b.shape[0]:
+        raise ValueError(f"dot: lengths differ ({a.shape[0]} and {b.shape[0]})")
+    _kernel_for("dot", a)
+    x, y = contiguous(a), contiguous(b)
+    out = torch.empty((), dtype=torch.float32, device=a.device)
+    check(_lib.lib().mfk_dot_f32(x.data_ptr(), y.data_ptr(), x.numel(), out.data_ptr(),
+                                 _stream()), "dot")
+    return out
+
+
 def _softmax(x: torch.Tensor, axis: int, log: bool, op: str) -> torch.Tensor:
     _require(x, op, "input")
     if x.dtype != torch.float32:
