@@ -429,7 +429,7 @@ def c5_strong_scaling(args, world, rank, device, gen, barrier, max_over_ranks, s
 
         def fused_step():
             sharded.gemm_into_peer(A, B, 1.0, None, 0.0, False, peer.row_ptr(rank * m), n,
-                                   precision=args.precision)
+                                   precision=args.precision, peer_memory=rank != 0)
             dist.all_reduce(flag)
 
         def barrier_step():
@@ -545,7 +545,7 @@ def main():
                 def fused_step():
                     sharded.gemm_into_peer(A, B, alpha, C_in, beta, trans_b,
                                            peer.row_ptr(rank * m), n, bias=bias,
-                                           precision=args.precision)
+                                           precision=args.precision, peer_memory=rank != 0)
                     dist.all_reduce(flag)
 
                 def barrier_step():

@@ -134,6 +134,15 @@ int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream);
 #define MFK_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
 int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream);
 
+/* mfk_gemm_f32 with C in another GPU's memory: a peer allocation or a CUDA IPC mapping of one
+ * (mfk_ipc_open_handle), written over NVLink. The caller states it, rather than the library
+ * inferring it from the pointer's attributes (which for an IPC mapping need not name the owning
+ * GPU): the epilogue then writes C with plain stores of full 128-byte row segments, never
+ * through a tensor map, and ends with a system-scope fence, so work the other GPU orders after
+ * this kernel (an event wait, a collective) sees the rows. Also valid, only slower, on local
+ * memory. No counterpart in the reference (single device); the gather of the row-block split. */
+int mfk_gemm_peer_f32(const mfk_gemm_desc* desc, void* stream);
+
 /* A GEMM split by row blocks over several GPUs of this process, optionally gathered into one
  * device's buffer in the same kernels. Rank r (of nranks) computes its rows with per_rank[r] (every
  * pointer on devices[r]) on streams[r] (NULL: that device's default stream). With gather == 0

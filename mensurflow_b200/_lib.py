@@ -33,6 +33,7 @@ EXPORTED = (
     "mfk_gemm_f32",
     "mfk_gemm_f32_noalloc",
     "mfk_gemm_strided_batched_f32",
+    "mfk_gemm_peer_f32",
     "mfk_sharded_gemm_f32",
     "mfk_ipc_get_handle",
     "mfk_ipc_open_handle",
@@ -122,6 +123,7 @@ def lib() -> ctypes.CDLL:
             vp, i64, i32, f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
             so.mfk_gemm_f32.argtypes = [ctypes.POINTER(GemmDesc), vp]
             so.mfk_gemm_f32_noalloc.argtypes = [ctypes.POINTER(GemmDesc), vp]
+            so.mfk_gemm_peer_f32.argtypes = [ctypes.POINTER(GemmDesc), vp]
             so.mfk_gemm_strided_batched_f32.argtypes = [ctypes.POINTER(GemmDesc),
                                                         ctypes.POINTER(BatchDesc), vp]
             so.mfk_sharded_gemm_f32.argtypes = [ctypes.POINTER(GemmDesc), i32,

@@ -404,8 +404,15 @@ int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode
     return MFK_OK;
 }
 
+// Where C lies, as the caller states it: kCOutputInfer looks at the pointer's attributes (a
+// device pointer of another GPU is peer memory), kCOutputPeer is certain that C is another
+// GPU's memory (a peer buffer or a CUDA IPC mapping of one, whose reported device need not be the
+// owner): then no tensor map ever covers C, whatever its attributes say.
+enum COutput { kCOutputInfer = 0, kCOutputPeer = 1 };
+
 int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream,
-             const FixedScratch* fixed, const mfk_packed_b* pb = nullptr);
+             const FixedScratch* fixed, const mfk_packed_b* pb = nullptr,
+             COutput c_where = kCOutputInfer);
 
 // Known answer: 1xTF32 reads A in place; a = 1 + 3*2^-12 holds 0.75 ulp of tf32 beyond 1, so
 // a * 1 is 1 when the tensor cores truncate fp32 operands and 1 + 2^-10 when they round. Runs
@@ -477,7 +484,7 @@ int check_desc(const mfk_gemm_desc* d) {
 }
 
 int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stream,
-             const FixedScratch* fixed, const mfk_packed_b* pb) {
+             const FixedScratch* fixed, const mfk_packed_b* pb, COutput c_where) {
     int rc = check_desc(d);
     if (rc != MFK_OK) return rc;
     const int64_t batch = bd ? bd->batch : 1;
@@ -694,8 +701,8 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     // C through TMA stores when its layout allows (16-byte aligned rows and matrices) and it lies
     // in this GPU's memory. C on another GPU (the gather target of a sharded product, reached over
     // NVLink) is written with plain stores from the epilogue: no tensor map covers peer memory.
-    bool c_local = true;
-    {
+    bool c_local = c_where != kCOutputPeer;
+    if (c_local) {
         cudaPointerAttributes pa{};
         if (cudaPointerGetAttributes(&pa, d->c) == cudaSuccess) {
             c_local = pa.type != cudaMemoryTypeDevice || pa.device == dev;
@@ -738,6 +745,11 @@ extern "C" {
 
 int mfk_gemm_f32(const mfk_gemm_desc* desc, void* stream) {
     return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int mfk_gemm_peer_f32(const mfk_gemm_desc* desc, void* stream) {
+    return run_gemm(desc, nullptr, static_cast<cudaStream_t>(stream), nullptr, nullptr,
+                    kCOutputPeer);
 }
 
 int mfk_gemm_f32_noalloc(const mfk_gemm_desc* desc, void* stream) {
@@ -826,7 +838,9 @@ int mfk_sharded_gemm_f32(const mfk_gemm_desc* per_rank, int32_t nranks, const in
                 }
             }
         }
-        const int rc = run_gemm(&d, nullptr, static_cast<cudaStream_t>(streams[r]), nullptr);
+        const bool peer = gather && devices[r] != root_dev;
+        const int rc = run_gemm(&d, nullptr, static_cast<cudaStream_t>(streams[r]), nullptr,
+                                nullptr, peer ? kCOutputPeer : kCOutputInfer);
         if (rc != MFK_OK) return rc;
         row0 += d.m;
     }

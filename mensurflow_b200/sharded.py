@@ -192,7 +192,8 @@ def sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, m_total: int, alpha: fl
         flag = torch.zeros(1, device=a_local.device)
         dist.all_reduce(flag, group=group)
         gemm_into_peer(a_local, b, alpha, c_local, beta, transpose_b, peer.row_ptr(start),
-                       peer.cols, bias=bias, activation=activation, precision=precision)
+                       peer.cols, bias=bias, activation=activation, precision=precision,
+                       peer_memory=peer.rank != peer.root)
         # every rank's rows have landed once every rank's GEMM has finished
         dist.all_reduce(flag, group=group)
         return peer.buffer if rank == peer.root else None
@@ -208,9 +209,12 @@ def sharded_gemm(a_local: torch.Tensor, b: torch.Tensor, m_total: int, alpha: fl
 def gemm_into_peer(a: torch.Tensor, b: torch.Tensor, alpha: float, c: Optional[torch.Tensor],
                    beta: float, transpose_b: bool, out_ptr: int, ldc: int, *,
                    bias: Optional[torch.Tensor] = None, activation: Optional[str] = None,
-                   precision: Optional[str] = None) -> None:
+                   precision: Optional[str] = None, peer_memory: bool = True) -> None:
     """The GEMM with its output rows at a raw device address (a peer GPU's buffer mapped on this
-    GPU): row i of C at out_ptr + 4 * i * ldc. Queued on the current stream."""
+    GPU): row i of C at out_ptr + 4 * i * ldc. Queued on the current stream. With `peer_memory`
+    (the default) the output is declared another GPU's memory (mfk_gemm_peer_f32: plain stores
+    and a system-scope fence, no tensor map over it); the root, writing into its own buffer,
+    passes peer_memory=False."""
     from . import _lib
     from .ops import _gemm_desc, _kernel_for, _stream
 
@@ -224,7 +228,8 @@ def gemm_into_peer(a: torch.Tensor, b: torch.Tensor, alpha: float, c: Optional[t
     d.m = a.shape[0]
     d.c = out_ptr
     d.ldc = ldc
-    _lib.check(_lib.lib().mfk_gemm_f32(ctypes.byref(d), _stream()), "gemm")
+    fn = _lib.lib().mfk_gemm_peer_f32 if peer_memory else _lib.lib().mfk_gemm_f32
+    _lib.check(fn(ctypes.byref(d), _stream()), "gemm")
 
 
 def sharded_gemm_batched(a_local: torch.Tensor, b_local: torch.Tensor, batch_total: int,

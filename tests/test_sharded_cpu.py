@@ -166,6 +166,7 @@ class _SharedRows:
     def __init__(self, buffer, root, rank):
         self.rows, self.cols = buffer.shape
         self.root = root
+        self.rank = rank
         self.shared = buffer
         self.buffer = buffer if rank == root else None
 
@@ -186,7 +187,9 @@ def _reuse_worker(rank, world, port, buffer, q):
         peer = _SharedRows(buffer, 0, rank)
 
         def rows_into_shared(a, b, alpha, c, beta, transpose_b, row0, ldc, *, bias=None,
-                             activation=None, precision=None):
+                             activation=None, precision=None, peer_memory=None):
+            # the root writes its own buffer; every other rank declares the buffer peer memory
+            assert peer_memory == (rank != 0)
             peer.shared[row0:row0 + a.shape[0]] = oracle_gemm(a, b, alpha, c, beta, False,
                                                               transpose_b)
 

@@ -58,6 +58,27 @@ def test_row_blocks_gathered_on_one_gpu_equal_the_single_product(cuda, precision
     assert mf.device_status() == 0
 
 
+@pytest.mark.parametrize("precision", ["3xtf32", "1xtf32"])
+def test_declared_peer_output_equals_the_tma_store_path(cuda, precision):
+    """mfk_gemm_peer_f32 (C declared another GPU's memory: plain 128-byte row stores and a
+    system-scope fence, never a tensor map) writes the same bits as mfk_gemm_f32 (TMA stores) —
+    only the store path differs. On one GPU the "peer" buffer is local memory, where the
+    declared path is valid too; rows and columns not multiples of the tile, and a row stride
+    wider than N, check the edges."""
+    m, n, k = 333, 300, 257
+    a, b, c, bias = _operands(m, n, k, cuda, seed=11)
+    want = mf.gemm(a, b, 0.5, c, 1.0, False, True, bias=bias, activation="relu",
+                   precision=precision)
+    ld = n + 12
+    buf = torch.full((m, ld), float("nan"), device=cuda)
+    sharded.gemm_into_peer(a, b, 0.5, c, 1.0, True, buf.data_ptr(), ld, bias=bias,
+                           activation="relu", precision=precision, peer_memory=True)
+    torch.cuda.synchronize()
+    assert torch.equal(buf[:, :n], want)
+    assert bool(torch.isnan(buf[:, n:]).all()), "the declared path wrote past N"
+    assert mf.device_status() == 0
+
+
 def test_row_blocks_argument_errors(cuda):
     a = torch.zeros(4, 8, device=cuda)
     with pytest.raises(ValueError):
