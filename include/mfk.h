@@ -239,6 +239,21 @@ int mfk_bias_grad_f32(const float* grad, int64_t rows, int64_t cols, int64_t ld,
 int mfk_softmax_f32(const float* x, float* out, int64_t outer, int64_t length, int64_t inner,
                     int32_t log, void* stream);
 
+/* Scaled-dot-product attention in one kernel: out = softmax(scale * q k^T) v per head, over the
+ * keys, with causal != 0 masking every key after the query (key > query). q, k, v and out are
+ * contiguous [heads, len, head_dim] fp32 (queries = keys = len), 16-byte aligned; head_dim must be
+ * 128 (MFK_ERR_UNSUPPORTED otherwise). For these shapes it computes what the reference's
+ * attention(q, k, v, nullptr, causal, scale) composes from gemm_strided_batched, where and softmax
+ * (src/ops/attention.cpp:48-98), in 3xTF32 throughout, without writing the [len, len] scores,
+ * and with the causal mask it skips the key tiles above the diagonal. The softmax is evaluated
+ * online (running row maximum and sum, the output rescaled as the maximum grows), so the result
+ * agrees with the composed path within the reference's attention tolerance (1e-4 relative), not
+ * bit for bit. Non-finite inputs are not supported (results are unspecified); callers that may
+ * hold them use the composed path. K and V are first split into tf32 (hi, lo) panels (V
+ * transposed) in a workspace from the stream-ordered allocator: 16 x heads x len x 128 bytes. */
+int mfk_attention_f32(const float* q, const float* k, const float* v, float* out, int64_t heads,
+                      int64_t len, int64_t head_dim, int32_t causal, float scale, void* stream);
+
 /* The softmax between attention's GEMMs with its masking fused in: for a contiguous
  * [batch, rows, cols] score tensor, entry (b, i, j) counts as -inf unless (keep == NULL or
  * keep[b*keep_bs + i*keep_rs + j] != 0) and (causal == 0 or j <= i); then softmax along cols.

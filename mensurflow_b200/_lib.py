@@ -47,6 +47,7 @@ EXPORTED = (
     "mfk_bias_act_f32",
     "mfk_bias_grad_f32",
     "mfk_softmax_f32",
+    "mfk_attention_f32",
     "mfk_masked_softmax_f32",
     "mfk_where_f32",
     "mfk_strided_copy_f32",
@@ -144,6 +145,7 @@ def lib() -> ctypes.CDLL:
             so.mfk_bias_grad_f32.argtypes = [vp, i64, i64, i64, vp, vp]
             so.mfk_softmax_f32.argtypes = [vp, vp, i64, i64, i64, i32, vp]
             so.mfk_masked_softmax_f32.argtypes = [vp, vp, i64, i64, i32, vp, i64, i64, i64, vp]
+            so.mfk_attention_f32.argtypes = [vp, vp, vp, vp, i64, i64, i64, i32, f32, vp]
             so.mfk_where_f32.argtypes = [vp, vp, vp, vp, i64, vp]
             so.mfk_strided_copy_f32.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64),
                                                 i32, vp, vp]

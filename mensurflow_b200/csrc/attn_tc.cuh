@@ -1,0 +1,508 @@
+// Fused scaled-dot-product attention on tcgen05 for fp32 data (3xTF32 throughout):
+//   O = softmax(scale * Q K^T, over keys; causal: key <= query) V
+// per head, with Q, K, V, O [heads, L, 128] (head dimension 128). One kernel: the scores never
+// leave the SM, and with the causal mask the key tiles above the diagonal are never visited.
+//
+// Replaces, for the causal / unmasked case with head dimension 128, the reference's composition
+// (src/ops/attention.cpp:48-98: gemm_strided_batched for S, where(-inf) for the mask, softmax,
+// gemm_strided_batched for P V), which writes and re-reads the whole [L, L] score matrix of every
+// head. Softmax follows the reference's numerics where it matters (scores are fl(scale * QK), the
+// row's exponentials are normalised by their sum; src/backends/cpu/ops/softmax/softmax.cpp:11-80)
+// but is evaluated online: running row maximum m and sum l per key tile, O rescaled when m grows
+// (only when it grows by more than 8, so the rescaling is rare and every exponential stays below
+// e^8), O / l at the end.
+//
+// Design (sm_100a), one CTA pair (cta_group::2) per work unit = (head, block of 256 queries):
+//  * Q of the unit (each CTA its 128 rows) is loaded raw by TMA into shared memory and split in
+//    place into tf32 (hi, lo) by two converter warps; it stays there for all of the unit's key
+//    tiles (the A operand of S = Q K^T);
+//  * K and V arrive pre-split into (hi, lo) panels (the GEMM path's packing passes: K as it is,
+//    V transposed so that keys are the contraction dimension), streamed through a ring of
+//    shared-memory stages by TMA, 32-wide chunks of the contraction per stage: four K chunks for
+//    S_j, four V chunks for the product with P_j;
+//  * tensor memory (512 columns): O [0, 128), two S buffers [128, 256) and [256, 384), P lo
+//    [384, 512). The softmax warps overwrite S_j with P_j's hi part and write its lo part beside
+//    it; the MMA then reads P from tensor memory as its A operand;
+//  * the MMA issuer (one thread) runs S_0, S_1, PV_0, S_2, PV_1, ...: while the softmax warps
+//    work on S_j the tensor cores compute S_{j+1} and PV_{j-1};
+//  * eight softmax warps per CTA, two per query row (one per half of the columns), two passes
+//    over each S tile (row maximum, then exponentials, their sum and the split, the row's scores
+//    held in registers between them), the epilogue O / l written straight from registers, each
+//    lane 128 contiguous bytes of its row per store group.
+#pragma once
+
+#include "mfk_ptx.cuh"
+
+namespace mfk {
+
+constexpr int kAttnD = 128;        // head dimension
+constexpr int kAttnRows = 128;     // query rows per CTA (TMEM lanes)
+constexpr int kAttnUnitRows = 256; // query rows per CTA pair
+constexpr int kAttnKeys = 128;     // keys per key tile
+constexpr int kAttnChunk = 32;     // contraction per ring stage (one 128-byte swizzle row)
+constexpr int kAttnStages = 5;
+constexpr int kAttnThreads = 384;  // warp 0 TMA, 1 MMA, 2-3 split Q, 4-11 softmax + epilogue
+constexpr int kAttnCvtWarp0 = 2;
+constexpr int kAttnSoftWarp0 = 4;
+constexpr float kAttnRescaleAbove = 8.0f;  // raise the running max only past m + 8
+
+// Shared memory per CTA (offsets from the 1024-aligned base).
+constexpr int kAttnQChunkBytes = kAttnRows * kAttnChunk * 4;            // 16 KB
+constexpr int kAttnQBytes = kAttnQChunkBytes * (kAttnD / kAttnChunk);   // 64 KB (hi or lo)
+constexpr int kAttnHalfBytes = (kAttnKeys / 2) * kAttnChunk * 4;        // 8 KB: 64 rows
+constexpr int kAttnStageBytes = 2 * kAttnHalfBytes;                     // hi | lo
+constexpr int kAttnOffQLo = kAttnQBytes;
+constexpr int kAttnOffRing = 2 * kAttnQBytes;
+constexpr int kAttnOffLPart = kAttnOffRing + kAttnStages * kAttnStageBytes;
+constexpr int kAttnOffBars = kAttnOffLPart + 2 * 8 * 32 * 4;           // [2][8 warps][32] float
+constexpr int kAttnSmemBytes = 1024 + kAttnOffBars + 256;
+static_assert(kAttnSmemBytes <= 232448, "attention: shared memory per CTA exceeded");
+
+// tensor memory columns
+constexpr uint32_t kAttnColO = 0;
+constexpr uint32_t kAttnColS = 128;  // buffer b at 128 + 128 b
+constexpr uint32_t kAttnColPLo = 384;
+
+enum : unsigned int {
+    kErrAttnProducer = 1u << 0,
+    kErrAttnMma = 1u << 1,
+    kErrAttnSoftmax = 1u << 2,
+    kErrAttnConvert = 1u << 3,
+};
+
+struct AttnArgs {
+    int heads;      // matrices (batch x heads)
+    int len;        // L: queries = keys
+    int num_qb;     // ceil(L / 256)
+    int causal;
+    float scale;
+    long long num_units;  // heads * num_qb
+};
+
+// Work unit u -> (head, query block): the longest units (last query blocks under the causal
+// mask) first, so the persistent pairs finish together.
+__device__ __forceinline__ void attn_unit(const AttnArgs& a, long long u, int& head, int& qb) {
+    qb = a.num_qb - 1 - static_cast<int>(u / a.heads);
+    head = static_cast<int>(u % a.heads);
+}
+
+// Key tiles a query block needs: up to its last query (causal) or all of them.
+__device__ __forceinline__ int attn_tiles(const AttnArgs& a, int qb) {
+    const int keys = a.causal ? min(a.len, (qb + 1) * kAttnUnitRows) : a.len;
+    return (keys + kAttnKeys - 1) / kAttnKeys;
+}
+
+// ---- producer: Q per unit, then K_0, K_1, V_0, K_2, V_1, ..., V_J through the ring ----------
+__device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorMap* tmQ,
+                                              const CUtensorMap* tmKh, const CUtensorMap* tmKl,
+                                              const CUtensorMap* tmVh, const CUtensorMap* tmVl,
+                                              uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                              uint64_t* q_full, uint64_t* q_free, uint32_t rank) {
+    const uint64_t keep = l2_policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    long long n = 0;  // units of this pair so far
+    auto load_stage = [&](const CUtensorMap* mh, const CUtensorMap* ml, int x, int y, int z) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, kErrAttnProducer)) return false;
+        uint8_t* s = smem + kAttnOffRing + stage * kAttnStageBytes;
+        if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kAttnStageBytes);
+        const uint32_t bar = mapa_shared(&full[stage], 0);
+        tma_load_3d_cg2(s, mh, bar, x, y, z, keep);
+        tma_load_3d_cg2(s + kAttnHalfBytes, ml, bar, x, y, z, keep);
+        if (++stage == kAttnStages) {
+            stage = 0;
+            phase ^= 1u;
+        }
+        return true;
+    };
+    for (long long u = blockIdx.x / 2; u < a.num_units; u += gridDim.x / 2, ++n) {
+        int head, qb;
+        attn_unit(a, u, head, qb);
+        const int tiles = attn_tiles(a, qb);
+        // Q: after the previous unit's S products have read it
+        if (n > 0 && !mbar_wait(q_free, static_cast<uint32_t>((n - 1) & 1), kErrAttnProducer))
+            return;
+        mbar_arrive_expect_tx(q_full, kAttnQBytes);
+        const int qrow = qb * kAttnUnitRows + static_cast<int>(rank) * kAttnRows;
+        for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc)
+            tma_load_3d(smem + kc * kAttnQChunkBytes, tmQ, q_full, kc * kAttnChunk, qrow, head,
+                        keep);
+        const int krow = static_cast<int>(rank) * (kAttnKeys / 2);
+        for (int j = 0; j <= tiles; ++j) {
+            if (j < tiles) {  // K_j: 64 keys of the tile per CTA, four chunks of the head dim
+                for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc)
+                    if (!load_stage(tmKh, tmKl, kc * kAttnChunk, j * kAttnKeys + krow, head))
+                        return;
+            }
+            if (j >= 1) {  // V_{j-1} transposed: 64 head dims per CTA, four chunks of keys
+                for (int kc = 0; kc < kAttnKeys / kAttnChunk; ++kc)
+                    if (!load_stage(tmVh, tmVl, (j - 1) * kAttnKeys + kc * kAttnChunk, krow, head))
+                        return;
+            }
+        }
+    }
+}
+
+// ---- converters: Q raw -> (hi, lo) in shared memory, in place ---------------------------------
+__device__ __forceinline__ void attn_convert(const AttnArgs& a, uint8_t* smem, uint64_t* q_full,
+                                            uint64_t* q_ready) {
+    const int ct = threadIdx.x - kAttnCvtWarp0 * 32;
+    const int lane = threadIdx.x % 32;
+    float4* hi = reinterpret_cast<float4*>(smem);
+    float4* lo = reinterpret_cast<float4*>(smem + kAttnOffQLo);
+    long long n = 0;
+    for (long long u = blockIdx.x / 2; u < a.num_units; u += gridDim.x / 2, ++n) {
+        if (!mbar_wait(q_full, static_cast<uint32_t>(n & 1), kErrAttnConvert)) return;
+#pragma unroll 4
+        for (int i = ct; i < kAttnQBytes / 16; i += 64) {
+            const float4 x = hi[i];
+            float4 h, l;
+            split_tf32(x.x, h.x, l.x);
+            split_tf32(x.y, h.y, l.y);
+            split_tf32(x.z, h.z, l.z);
+            split_tf32(x.w, h.w, l.w);
+            hi[i] = h;
+            lo[i] = l;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(q_ready, 0));
+    }
+}
+
+// ---- MMA issuer (one thread of the pair's first CTA) -----------------------------------------
+__device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8_t* smem,
+                                         uint64_t* full, uint64_t* empty, uint64_t* q_ready,
+                                         uint64_t* q_free, uint64_t* s_full, uint64_t* p_full,
+                                         uint64_t* pv_done) {
+    constexpr uint32_t idesc = idesc_tf32(kAttnUnitRows, 128, false, false);
+    constexpr uint16_t kPair = 3;
+    const uint32_t q_hi = smem_u32(smem);
+    const uint32_t q_lo = q_hi + kAttnOffQLo;
+    const uint32_t ring = q_hi + kAttnOffRing;
+    int stage = 0;
+    uint32_t phase = 0;
+    long long t = 0;  // key tiles of this pair so far (S buffer t & 1)
+    long long n = 0;
+    auto next_stage = [&]() {
+        if (++stage == kAttnStages) {
+            stage = 0;
+            phase ^= 1u;
+        }
+    };
+    // S_t = Q K_j^T into S buffer t & 1: four stages of K (hi, lo), 3 products per k-step
+    auto s_product = [&](long long tt) {
+        const uint32_t d = tmem + kAttnColS + static_cast<uint32_t>((tt & 1) * 128);
+        for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc) {
+            if (!mbar_wait(&full[stage], phase, kErrAttnMma)) return false;
+            tc_fence_after();
+            const uint32_t bh = ring + stage * kAttnStageBytes;
+            const uint32_t bl = bh + kAttnHalfBytes;
+            const uint32_t ah = q_hi + kc * kAttnQChunkBytes;
+            const uint32_t al = q_lo + kc * kAttnQChunkBytes;
+#pragma unroll
+            for (int ks = 0; ks < kAttnChunk / 8; ++ks) {
+                const uint32_t koff = ks * 32;
+                const uint64_t dah = smem_desc(ah + koff, 16, 1024, kSwizzle128B);
+                const uint64_t dal = smem_desc(al + koff, 16, 1024, kSwizzle128B);
+                const uint64_t dbh = smem_desc(bh + koff, 16, 1024, kSwizzle128B);
+                const uint64_t dbl = smem_desc(bl + koff, 16, 1024, kSwizzle128B);
+                mma_tf32_cg2(d, dal, dbh, idesc, (kc > 0 || ks > 0) ? 1u : 0u);
+                mma_tf32_cg2(d, dah, dbl, idesc, 1u);
+                mma_tf32_cg2(d, dah, dbh, idesc, 1u);
+            }
+            mma_commit_cg2_mc(&empty[stage], kPair);
+            next_stage();
+        }
+        mma_commit_cg2_mc(&s_full[tt & 1], kPair);
+        return true;
+    };
+    // O (+)= P_t V_j: P (hi in S buffer t & 1, lo in the P lo columns) from tensor memory
+    auto pv_product = [&](long long tt, bool first) {
+        if (!mbar_wait(&p_full[tt & 1], static_cast<uint32_t>((tt >> 1) & 1), kErrAttnMma))
+            return false;
+        tc_fence_after();
+        const uint32_t ph = tmem + kAttnColS + static_cast<uint32_t>((tt & 1) * 128);
+        const uint32_t pl = tmem + kAttnColPLo;
+        for (int kc = 0; kc < kAttnKeys / kAttnChunk; ++kc) {
+            if (!mbar_wait(&full[stage], phase, kErrAttnMma)) return false;
+            tc_fence_after();
+            const uint32_t bh = ring + stage * kAttnStageBytes;
+            const uint32_t bl = bh + kAttnHalfBytes;
+#pragma unroll
+            for (int ks = 0; ks < kAttnChunk / 8; ++ks) {
+                const uint32_t koff = ks * 32;
+                const uint32_t col = static_cast<uint32_t>(kc * kAttnChunk + ks * 8);
+                const uint64_t dbh = smem_desc(bh + koff, 16, 1024, kSwizzle128B);
+                const uint64_t dbl = smem_desc(bl + koff, 16, 1024, kSwizzle128B);
+                const uint32_t acc = (!first || kc > 0 || ks > 0) ? 1u : 0u;
+                mma_tf32_ts_cg2(tmem + kAttnColO, pl + col, dbh, idesc, acc);
+                mma_tf32_ts_cg2(tmem + kAttnColO, ph + col, dbl, idesc, 1u);
+                mma_tf32_ts_cg2(tmem + kAttnColO, ph + col, dbh, idesc, 1u);
+            }
+            mma_commit_cg2_mc(&empty[stage], kPair);
+            next_stage();
+        }
+        mma_commit_cg2_mc(pv_done, kPair);
+        return true;
+    };
+    for (long long u = blockIdx.x / 2; u < a.num_units; u += gridDim.x / 2, ++n) {
+        int head, qb;
+        attn_unit(a, u, head, qb);
+        const int tiles = attn_tiles(a, qb);
+        if (!mbar_wait(q_ready, static_cast<uint32_t>(n & 1), kErrAttnMma)) return;
+        tc_fence_after();
+        const long long t0 = t;
+        for (int j = 0; j < tiles; ++j) {
+            if (!s_product(t0 + j)) return;
+            if (j == tiles - 1) mma_commit_cg2_mc(q_free, kPair);  // every S of the unit
+            if (j >= 1 && !pv_product(t0 + j - 1, j == 1)) return;
+        }
+        if (!pv_product(t0 + tiles - 1, tiles == 1)) return;
+        t = t0 + tiles;
+    }
+}
+
+// ---- softmax and epilogue (eight warps per CTA: two per TMEM lane quarter) -----------------
+// Warp w (4..11) owns query row 32 (w % 4) + lane of its CTA's block and half h = (w - 4) / 4 of
+// the tile's 128 columns (keys, and later output columns). Pass 1 reads the whole row of S_j
+// (its own half kept in registers, the other half for the maximum only, so the two warps of a
+// row agree on it without talking); pass 2 writes P_j's hi over its half of S_j and lo into the
+// P lo columns. The row sum is kept per half and the two halves are added once per unit,
+// through shared memory and a bounded barrier.
+__device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_t sb,
+                                                      uint32_t pl, int h, int nvalid, float& m,
+                                                      double& l, bool rescale_allowed,
+                                                      uint32_t olanes, uint64_t* pv_done,
+                                                      long long t, int j) {
+    const float ninf = __int_as_float(0xff800000);
+    const int own0 = h * 64, other0 = (1 - h) * 64;
+    // pass 1: the row's maximum over its valid keys (both halves), own half kept in registers
+    float mt = ninf;
+    {
+        uint32_t x[32], y[32];
+        tmem_ld_issue_32x32b_x32(sb + other0, x);
+        tmem_ld_issue_32x32b_x32(sb + other0 + 32, y);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (other0 + i < nvalid) mt = fmaxf(mt, __fmul_rn(a.scale, __uint_as_float(x[i])));
+            if (other0 + 32 + i < nvalid)
+                mt = fmaxf(mt, __fmul_rn(a.scale, __uint_as_float(y[i])));
+        }
+    }
+    uint32_t sr[2][32];
+    tmem_ld_issue_32x32b_x32(sb + own0, sr[0]);
+    tmem_ld_issue_32x32b_x32(sb + own0 + 32, sr[1]);
+    tmem_ld_wait();
+    float* s = reinterpret_cast<float*>(&sr[0][0]);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+        s[i] = __fmul_rn(a.scale, s[i]);
+        if (own0 + i < nvalid) mt = fmaxf(mt, s[i]);
+    }
+    float mn = m;
+    if (mt != ninf && (m == ninf || mt > m + kAttnRescaleAbove)) mn = fmaxf(m, mt);
+    // the previous tile's product has finished: P lo is free and O holds it
+    if (j >= 1) {
+        if (!mbar_wait(pv_done, static_cast<uint32_t>((t - 1) & 1), kErrAttnSoftmax)) return false;
+        tc_fence_after();
+    }
+    if (rescale_allowed && __any_sync(0xffffffffu, mn != m)) {
+        const float f = mn != m ? expf(m - mn) : 1.0f;
+#pragma unroll
+        for (int c = 0; c < 64; c += 16) {
+            uint32_t r[16];
+            tmem_ld_issue_32x32b_x16(olanes + own0 + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__fmul_rn(__uint_as_float(r[i]), f));
+            tmem_st_32x32b_x16(olanes + own0 + c, r);
+        }
+        l *= static_cast<double>(f);
+    }
+    m = mn;
+    // pass 2: P = exp(s - m) on valid keys (0 elsewhere), split into tf32 (hi, lo); P >= 0 is
+    // finite, so the split needs no special cases: hi = P with its 13 low bits cleared, lo =
+    // P - hi (exact) rounded to tf32
+    float lt = 0.0f;
+    uint32_t* hb = &sr[0][0];  // P's hi part replaces the scores it came from
+#pragma unroll
+    for (int c = 0; c < 64; c += 16) {
+        uint32_t lo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float p = (own0 + c + i < nvalid) ? expf(s[c + i] - m) : 0.0f;
+            lt += p;
+            const uint32_t hi = __float_as_uint(p) & 0xFFFFE000u;
+            lo[i] = tf32_round_bits(__float_as_uint(p - __uint_as_float(hi)));
+            hb[c + i] = hi;
+        }
+        tmem_st_32x32b_x16(sb + own0 + c, *reinterpret_cast<const uint32_t(*)[16]>(hb + c));
+        tmem_st_32x32b_x16(pl + own0 + c, lo);
+    }
+    l += static_cast<double>(lt);
+    return true;
+}
+
+__device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint32_t tmem,
+                                             uint64_t* s_full, uint64_t* p_full,
+                                             uint64_t* pv_done, uint64_t* l_bar, float* l_part,
+                                             uint32_t rank) {
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int q = warp % 4;                       // TMEM lane quarter
+    const int h = (warp - kAttnSoftWarp0) / 4;    // column half
+    const uint32_t lanes = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    long long t = 0;
+    long long n = 0;
+    bool ok = true;  // a bounded wait gave up: leave every loop
+    for (long long u = blockIdx.x / 2; ok && u < a.num_units; u += gridDim.x / 2, ++n) {
+        int head, qb;
+        attn_unit(a, u, head, qb);
+        const int tiles = attn_tiles(a, qb);
+        const int row0 = qb * kAttnUnitRows + static_cast<int>(rank) * kAttnRows + q * 32;
+        const int row = row0 + lane;
+        // keys valid for this row: key < L, and key <= row under the causal mask
+        const int kend = a.causal ? min(a.len, row + 1) : a.len;
+        float m = __int_as_float(0xff800000);
+        double l = 0.0;
+        for (int j = 0; j < tiles; ++j, ++t) {
+            const uint32_t sb = lanes + kAttnColS + static_cast<uint32_t>((t & 1) * 128);
+            const int nvalid = max(0, min(kAttnKeys, kend - j * kAttnKeys));
+            if (!mbar_wait(&s_full[t & 1], static_cast<uint32_t>((t >> 1) & 1), kErrAttnSoftmax)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            if (!attn_softmax_row_half(a, sb, lanes + kAttnColPLo, h, nvalid, m, l, j >= 1,
+                                       lanes + kAttnColO, pv_done, t, j)) {
+                ok = false;
+                break;
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(&p_full[t & 1], 0));
+        }
+        if (!ok) break;
+        // the row sum: this half's plus the other warp's (slot n & 1, so a slot is rewritten
+        // only after the partner has read it: it arrives for unit n + 1 after reading unit n)
+        float* slot = l_part + (n & 1) * (8 * 32);
+        slot[(warp - kAttnSoftWarp0) * 32 + lane] = static_cast<float>(l);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&l_bar[q]);
+        if (!mbar_wait(&l_bar[q], static_cast<uint32_t>(n & 1), kErrAttnSoftmax)) break;
+        l += static_cast<double>(slot[(warp - kAttnSoftWarp0 + (h ? -4 : 4)) * 32 + lane]);
+        // epilogue: O / l once the last product has finished
+        if (!mbar_wait(pv_done, static_cast<uint32_t>((t - 1) & 1), kErrAttnSoftmax)) break;
+        tc_fence_after();
+        const float inv = static_cast<float>(1.0 / l);
+        float* orow = out + (static_cast<long long>(head) * a.len + row) * kAttnD + h * 64;
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+            uint32_t r[32];
+            tmem_ld_issue_32x32b_x32(lanes + kAttnColO + h * 64 + c, r);
+            tmem_ld_wait();
+            if (row < a.len) {
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                    reinterpret_cast<float4*>(orow + c)[v] =
+                        make_float4(__fmul_rn(__uint_as_float(r[4 * v]), inv),
+                                    __fmul_rn(__uint_as_float(r[4 * v + 1]), inv),
+                                    __fmul_rn(__uint_as_float(r[4 * v + 2]), inv),
+                                    __fmul_rn(__uint_as_float(r[4 * v + 3]), inv));
+                }
+            }
+        }
+        // the epilogue's reads of O are done before the next unit's first product overwrites it:
+        // the next p_full arrival comes after them (tcgen05.wait::ld above)
+    }
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmKh,
+                   const __grid_constant__ CUtensorMap tmKl,
+                   const __grid_constant__ CUtensorMap tmVh,
+                   const __grid_constant__ CUtensorMap tmVl, float* out, const AttnArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAttnOffBars);
+    uint64_t* full = bars;
+    uint64_t* empty = full + kAttnStages;
+    uint64_t* q_full = empty + kAttnStages;
+    uint64_t* q_ready = q_full + 1;
+    uint64_t* q_free = q_ready + 1;
+    uint64_t* s_full = q_free + 1;   // [2]
+    uint64_t* p_full = s_full + 2;   // [2]
+    uint64_t* pv_done = p_full + 2;
+    uint64_t* drain = pv_done + 1;
+    uint64_t* l_bar = drain + 1;     // [4]: the two warps of a lane quarter
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(l_bar + 4);
+    float* l_part = reinterpret_cast<float*>(smem + kAttnOffLPart);
+    static_assert((2 * kAttnStages + 14) * 8 + 4 <= 256, "attention: barrier area too small");
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_ctarank();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kAttnStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(q_full, 1);
+        mbar_init(q_ready, 2 * 2);  // both converter warps of both CTAs
+        mbar_init(q_free, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&p_full[b], 8 * 2);  // the eight softmax warps of both CTAs
+        }
+        mbar_init(pv_done, 1);
+        mbar_init(drain, 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&l_bar[i], 2);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmKh);
+        tma_prefetch_desc(&tmKl);
+        tma_prefetch_desc(&tmVh);
+        tma_prefetch_desc(&tmVl);
+    }
+    if (warp == 1) tmem_alloc_cg2(tmem_holder, 512);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0)
+            attn_producer(a, &tmQ, &tmKh, &tmKl, &tmVh, &tmVl, smem, full, empty, q_full, q_free,
+                          rank);
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            attn_mma(a, tmem, smem, full, empty, q_ready, q_free, s_full, p_full, pv_done);
+            // every MMA issued must finish before tensor memory is released
+            mma_commit_cg2(drain);
+            mbar_wait(drain, 0, kErrAttnMma);
+        }
+        __syncwarp();
+    } else if (warp < kAttnSoftWarp0) {
+        attn_convert(a, smem, q_full, q_ready);
+    } else {
+        attn_softmax(a, out, tmem, s_full, p_full, pv_done, l_bar, l_part, rank);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_cg2(tmem, 512);
+    }
+}
+
+}  // namespace mfk

@@ -17,6 +17,7 @@
 
 #include "mfk.h"
 
+#include "attn_tc.cuh"
 #include "blas1.cuh"
 #include "gemm_tc.cuh"
 #include "movement.cuh"
@@ -1161,6 +1162,104 @@ int mfk_softmax_f32(const float* x, float* out, int64_t outer, int64_t length, i
     mfk::SoftmaxMask mk{nullptr, 0, 0, 0, 1};
     return launch_softmax(x, out, outer, length, inner, log != 0, mk,
                           static_cast<cudaStream_t>(stream));
+}
+
+int mfk_attention_f32(const float* q, const float* k, const float* v, float* out, int64_t heads,
+                      int64_t len, int64_t head_dim, int32_t causal, float scale,
+                      void* stream_) {
+    if (heads < 0 || len < 0 || head_dim < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (heads == 0 || len == 0) return MFK_OK;
+    if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+        return MFK_ERR_INVALID_ARGUMENT;
+    if (head_dim != mfk::kAttnD || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
+        !aligned16(out))
+        return MFK_ERR_UNSUPPORTED;
+    if (len > (int64_t(1) << 30) || heads > (int64_t(1) << 30)) return MFK_ERR_UNSUPPORTED;
+    int dev = 0;
+    DeviceInfo* info = nullptr;
+    int rc = current_device(&dev, &info);
+    if (rc != MFK_OK) return rc;
+    const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const int64_t d = head_dim;
+    const int64_t kp_v = (len + mfk::kBK - 1) / mfk::kBK * mfk::kBK;
+    // K split as it lies ([head][key][d], d the contraction of S = Q K^T); V split transposed
+    // ([head][d][key], keys the contraction of O = P V), both into (hi, lo) panels
+    const size_t k_elems = static_cast<size_t>(heads) * len * d;
+    const size_t v_elems = static_cast<size_t>(heads) * d * kp_v;
+    const size_t bytes = sizeof(float) * 2 * (k_elems + v_elems);
+    uint8_t* ws = nullptr;
+    MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream));
+    struct Free {
+        uint8_t* p;
+        cudaStream_t s;
+        ~Free() { cudaFreeAsync(p, s); }
+    } release{ws, stream};
+    Operand K{k, d, 1, len, BatchLayout{}};
+    K.bl.stride = len * d;
+    K.hi = reinterpret_cast<float*>(ws);
+    K.lo = K.hi + k_elems;
+    Operand V{v, 1, d, d, BatchLayout{}};  // row = head dim, depth = key
+    V.bl.stride = len * d;
+    V.hi = K.lo + k_elems;
+    V.lo = V.hi + v_elems;
+    if ((rc = launch_pack(K, d, d, heads, mfk::kPackSplit, info, stream)) != MFK_OK) return rc;
+    if ((rc = launch_pack(V, len, kp_v, heads, mfk::kPackSplit, info, stream)) != MFK_OK)
+        return rc;
+    CUtensorMap mq, mkh, mkl, mvh, mvl;
+    const bool maps =
+        make_kmajor_map(&mq, q, d, len, heads, d, len * d, mfk::kAttnRows) &&
+        make_kmajor_map(&mkh, K.hi, d, len, heads, d, len * d, mfk::kAttnKeys / 2) &&
+        make_kmajor_map(&mkl, K.lo, d, len, heads, d, len * d, mfk::kAttnKeys / 2) &&
+        make_kmajor_map(&mvh, V.hi, kp_v, d, heads, kp_v, d * kp_v, mfk::kAttnD / 2) &&
+        make_kmajor_map(&mvl, V.lo, kp_v, d, heads, kp_v, d * kp_v, mfk::kAttnD / 2);
+    if (!maps) {
+        t_cuda_error = "cuTensorMapEncodeTiled rejected an attention operand";
+        return MFK_ERR_UNSUPPORTED;
+    }
+    mfk::AttnArgs a{};
+    a.heads = static_cast<int>(heads);
+    a.len = static_cast<int>(len);
+    a.num_qb = static_cast<int>((len + mfk::kAttnUnitRows - 1) / mfk::kAttnUnitRows);
+    a.causal = causal != 0 ? 1 : 0;
+    a.scale = scale;
+    a.num_units = static_cast<long long>(a.heads) * a.num_qb;
+    auto kernel = mfk::attn_tc_kernel;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.blockDim = dim3(mfk::kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = mfk::kAttnSmemBytes;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    constexpr int kSlot = 15;  // this kernel's per-device set-up flags
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if (!info->smem_set[kSlot]) {
+            MFK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          mfk::kAttnSmemBytes));
+            int units = info->sm_count / 2;
+            cfg.gridDim = dim3(static_cast<unsigned>(info->sm_count / 2 * 2), 1, 1);
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess &&
+                clusters > 0)
+                units = clusters;
+            cudaGetLastError();
+            info->resident_units[kSlot] = units;
+            info->smem_set[kSlot] = true;
+        }
+    }
+    const long long pairs = std::min<long long>(a.num_units, info->resident_units[kSlot]);
+    cfg.gridDim = dim3(static_cast<unsigned>(pairs * 2), 1, 1);
+    {
+        TimedLaunch timed(stream);
+        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mkh, mkl, mvh, mvl, out, a));
+    }
+    g_launches.fetch_add(1);
+    return MFK_OK;
 }
 
 int mfk_masked_softmax_f32(const float* scores, const uint8_t* keep, int64_t keep_bs,

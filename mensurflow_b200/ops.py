@@ -767,7 +767,7 @@ def where(condition: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> torch.Te
     return out
 
 
-def _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks):
+def _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks, fused=None):
     """Execution::GPU on host-resident q, k, v (as gemm's host path): the batch is cut into
     chunks whose q, k, v stream in on one stream, are attended on the caller's stream and stream
     back on a third, so the copies overlap each other and the math. q, k and v must share their
@@ -810,7 +810,7 @@ def _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks):
         ready = torch.cuda.Event()
         ready.record(copy_in)
         compute.wait_event(ready)
-        o = attention(dq, dk, dv, d_mask, causal, scale, precision=precision)
+        o = attention(dq, dk, dv, d_mask, causal, scale, precision=precision, fused=fused)
         done = torch.cuda.Event()
         done.record(compute)
         copy_out.wait_event(done)
@@ -824,15 +824,56 @@ def _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks):
     return out
 
 
+FUSED_ATTENTION_HEAD_DIM = 128
+
+
+def _fused_attention_eligible(q, k, v, mask, precision) -> bool:
+    """The one-kernel path (mfk_attention_f32): no mask tensor, q, k and v of one shape
+    [..., L, 128] on a CUDA device, 3xTF32."""
+    if mask is not None or q.device.type != "cuda" or q.dim() < 2:
+        return False
+    if tuple(q.shape) != tuple(k.shape) or tuple(q.shape) != tuple(v.shape):
+        return False
+    if q.shape[-1] != FUSED_ATTENTION_HEAD_DIM or q.shape[-2] == 0:
+        return False
+    code = _PRECISIONS[precision]
+    if code == _lib.PRECISION_DEFAULT:
+        code = _lib.lib().mfk_get_default_precision()
+    return code == _lib.PRECISION_3XTF32
+
+
+def _fused_attention(q, k, v, causal, scale):
+    _kernel_for("attention", q)
+    qq, kk, vv = (contiguous(t) for t in (q, k, v))
+    if any(t.data_ptr() % 16 for t in (qq, kk, vv)):
+        qq, kk, vv = (t.clone() for t in (qq, kk, vv))
+    out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
+    length, depth = q.shape[-2], q.shape[-1]
+    heads = q.numel() // (length * depth)
+    check(_lib.lib().mfk_attention_f32(qq.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+                                       out.data_ptr(), heads, length, depth,
+                                       1 if causal else 0, float(scale), _stream()), "attention")
+    return out
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
               mask: Optional[torch.Tensor] = None, causal: bool = False, scale: float = 0.0, *,
               precision: Optional[str] = None, execution: str = "auto",
-              out: Optional[torch.Tensor] = None, chunks: int = 16) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, chunks: int = 16,
+              fused: Optional[bool] = None) -> torch.Tensor:
     """Scaled dot-product attention as mensurflow::attention (attention.hpp:21,
     src/ops/attention.cpp:48-98): scores = scale * q @ k^T (batched GEMM, scale in alpha), entries
     outside `mask` (Bool, broadcast to the scores) and, with `causal`, above the diagonal set to
-    -inf, softmax over the keys, then weights @ v. The masking is fused into the softmax pass
-    (one read and one write of the scores instead of the reference's where + softmax passes).
+    -inf, softmax over the keys, then weights @ v.
+
+    Two device paths. Without a mask tensor, with q, k and v of one shape [..., L, 128] and
+    3xTF32, one kernel computes the whole op (mfk_attention_f32: the scores stay on chip, the
+    causal mask skips the key tiles above the diagonal; the softmax is evaluated online, so the
+    result agrees with the composed path within the reference's 1e-4, not bit for bit; it is not
+    for non-finite inputs). Otherwise, or with fused=False, the composed path: the batched GEMM,
+    the masking fused into the softmax pass (one read and one write of the scores instead of the
+    reference's where + softmax passes), the second batched GEMM. fused=True insists on the one
+    kernel (ValueError when the inputs do not qualify).
 
     `execution` follows the reference's Execution: with host tensors "gpu" streams batch chunks
     through the current CUDA device and returns a host tensor (`out`, if given, receives it)."""
@@ -843,7 +884,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 t.dtype == torch.float32 and t.dim() >= 2 for t in (q, k, v))):
         if mask is not None and (not isinstance(mask, torch.Tensor) or mask.dtype != torch.bool):
             raise ValueError("attention: mask must be a defined Bool tensor")
-        return _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks)
+        return _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks,
+                                    fused)
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
         if t is None or not isinstance(t, torch.Tensor):
             raise ValueError(f"attention: undefined {name}")
@@ -863,6 +905,12 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                          "number of keys")
     if scale == 0.0:
         scale = float(np.float32(1.0 / np.sqrt(depth))) if depth > 0 else 1.0
+    eligible = _fused_attention_eligible(q, k, v, mask, precision)
+    if fused and not eligible:
+        raise ValueError("attention: the fused kernel needs no mask tensor, q, k and v of one "
+                         "shape [..., L, 128] on a CUDA device, and 3xTF32")
+    if eligible and fused is not False:
+        return _fused_attention(q, k, v, causal, scale)
     scores = gemm_strided_batched(q, k, scale, None, 0.0, False, True, precision=precision)
     keep = None
     if mask is not None:

@@ -141,3 +141,71 @@ def test_attention_on_host_tensors_argument_errors(cuda):
         mf.attention(q, q, q, torch.ones(2, 4, 4, dtype=torch.bool), execution="gpu")
     with pytest.raises(ValueError):
         mf.attention(q, q, q, execution="tpu")
+
+
+# ---- the fused kernel (mfk_attention_f32) --------------------------------------------------
+
+def _qkv(heads, length, seed, std=1.0 / np.sqrt(128)):
+    rng = np.random.default_rng(seed)
+    return tuple((rng.standard_normal((heads, length, 128)) * std).astype(np.float32)
+                 for _ in range(3))
+
+
+@pytest.mark.parametrize("heads,length,causal", [
+    (3, 256, True), (2, 384, True), (2, 200, True), (1, 77, False), (2, 128, False),
+    (4, 512, True), (1, 640, False), (2, 1, True)])
+def test_fused_attention_matches_reference(cuda, heads, length, causal):
+    """The one-kernel path against the reference's own attention (composed gemm / where / softmax
+    / gemm on the CPU) within its test tolerance (softmax_loss_test.cpp: 1e-4, 1e-6), at lengths
+    that are and are not multiples of the kernel's 128-key tiles and 256-query blocks."""
+    q, k, v = _qkv(heads, length, 10 * heads + length)
+    got = mf.attention(dev(q, cuda), dev(k, cuda), dev(v, cuda), causal=causal,
+                       fused=True).cpu().numpy()
+    want = O.ref_attention(q, k, v, causal=causal)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-6)
+    composed = mf.attention(dev(q, cuda), dev(k, cuda), dev(v, cuda), causal=causal,
+                            fused=False).cpu().numpy()
+    np.testing.assert_allclose(got, composed, rtol=1e-4, atol=1e-6)
+    assert mf.device_status() == 0
+
+
+def test_fused_attention_running_max_rescales(cuda):
+    """Scores that grow along the keys by ~30 over the sequence: the running row maximum is raised
+    several times (each time by more than the kernel's slack of 8), so the output accumulator is
+    rescaled in tensor memory between key tiles; an explicit scale as well."""
+    heads, length = 2, 768
+    rng = np.random.default_rng(7)
+    u = rng.standard_normal(128).astype(np.float32)
+    u /= np.linalg.norm(u)
+    q = (rng.standard_normal((heads, length, 128)) * 0.05 + u).astype(np.float32)
+    ramp = (np.arange(length, dtype=np.float32) / length * 30.0)[None, :, None]
+    k = (rng.standard_normal((heads, length, 128)) * 0.05 + ramp * u).astype(np.float32)
+    v = (rng.standard_normal((heads, length, 128)) / np.sqrt(128)).astype(np.float32)
+    for causal in (True, False):
+        got = mf.attention(dev(q, cuda), dev(k, cuda), dev(v, cuda), causal=causal, scale=1.0,
+                           fused=True).cpu().numpy()
+        want = O.ref_attention(q, k, v, causal=causal, scale=1.0)
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-6, err_msg=f"causal={causal}")
+    assert mf.device_status() == 0
+
+
+def test_fused_attention_routing(cuda):
+    """Eligible calls take the one kernel by default; a mask, a head dimension other than 128,
+    shared k/v or 1xTF32 take the composed path, and fused=True refuses them."""
+    q, k, v = _qkv(2, 128, 3)
+    tq, tk, tv = dev(q, cuda), dev(k, cuda), dev(v, cuda)
+    np.testing.assert_array_equal(mf.attention(tq, tk, tv, causal=True).cpu().numpy(),
+                                  mf.attention(tq, tk, tv, causal=True, fused=True).cpu().numpy())
+    mask = torch.ones(128, 128, dtype=torch.bool, device=cuda)
+    with pytest.raises(ValueError):
+        mf.attention(tq, tk, tv, mask=mask, fused=True)
+    with pytest.raises(ValueError):
+        mf.attention(tq[..., :64], tk[..., :64], tv[..., :64], fused=True)
+    with pytest.raises(ValueError):
+        mf.attention(tq, tk[:1], tv[:1], fused=True)
+    with pytest.raises(ValueError):
+        mf.attention(tq, tk, tv, precision="1xtf32", fused=True)
+    # the composed path still serves them
+    got = mf.attention(tq, tk, tv, mask=mask, causal=True).cpu().numpy()
+    np.testing.assert_allclose(got, O.ref_attention(q, k, v, causal=True), rtol=1e-4, atol=1e-6)
+    assert mf.device_status() == 0
