@@ -26,9 +26,9 @@
 //  * the MMA issuer (one thread) runs S_0, S_1, PV_0, S_2, PV_1, ...: while the softmax warps
 //    work on S_j the tensor cores compute S_{j+1} and PV_{j-1};
 //  * eight softmax warps per CTA, two per query row (one per half of the columns), two passes
-//    over each S tile (row maximum, then exponentials, their sum and the split, the row's scores
-//    held in registers between them), the epilogue O / l written straight from registers, each
-//    lane 128 contiguous bytes of its row per store group.
+//    over each S tile (row maximum, swapped with the other half's through shared memory, then
+//    exponentials, their sum and the split, the scores held in registers between them), the
+//    epilogue O / l written straight from registers.
 #pragma once
 
 #include "mfk_ptx.cuh"
@@ -53,8 +53,8 @@ constexpr int kAttnHalfBytes = (kAttnKeys / 2) * kAttnChunk * 4;        // 8 KB:
 constexpr int kAttnStageBytes = 2 * kAttnHalfBytes;                     // hi | lo
 constexpr int kAttnOffQLo = kAttnQBytes;
 constexpr int kAttnOffRing = 2 * kAttnQBytes;
-constexpr int kAttnOffLPart = kAttnOffRing + kAttnStages * kAttnStageBytes;
-constexpr int kAttnOffBars = kAttnOffLPart + 2 * 8 * 32 * 4;           // [2][8 warps][32] float
+constexpr int kAttnOffSwap = kAttnOffRing + kAttnStages * kAttnStageBytes;
+constexpr int kAttnOffBars = kAttnOffSwap + 2 * 8 * 32 * 4;           // swap slots [2][8][32]
 constexpr int kAttnSmemBytes = 1024 + kAttnOffBars + 256;
 static_assert(kAttnSmemBytes <= 232448, "attention: shared memory per CTA exceeded");
 
@@ -265,32 +265,41 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
 
 // ---- softmax and epilogue (eight warps per CTA: two per TMEM lane quarter) -----------------
 // Warp w (4..11) owns query row 32 (w % 4) + lane of its CTA's block and half h = (w - 4) / 4 of
-// the tile's 128 columns (keys, and later output columns). Pass 1 reads the whole row of S_j
-// (its own half kept in registers, the other half for the maximum only, so the two warps of a
-// row agree on it without talking); pass 2 writes P_j's hi over its half of S_j and lo into the
-// P lo columns. The row sum is kept per half and the two halves are added once per unit,
-// through shared memory and a bounded barrier.
+// the tile's 128 columns (keys, and later output columns); the other warp of its lane quarter
+// owns the other half. A warp reads and writes only its own columns of S_j / P_j: the two halves'
+// row maxima (per tile) and row sums (per unit) are swapped through shared memory.
+
+// The two warps of a lane quarter swap one float per lane: event e writes slot e & 1 and waits
+// for phase e of the quarter's barrier (both warps arrive). A slot is rewritten two events later,
+// only after the partner has arrived for the event in between, i.e. after it read the value.
+struct AttnSwap {
+    float* xch;     // [2 slots][8 warps][32 lanes]
+    uint64_t* bar;  // the lane quarter's barrier, two arrivals per event
+    int me, partner, lane;
+    long long e;
+    __device__ __forceinline__ bool swap(float v, float& other) {
+        float* slot = xch + (e & 1) * (8 * 32);
+        slot[me * 32 + lane] = v;
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar);
+        if (!mbar_wait(bar, static_cast<uint32_t>(e & 1), kErrAttnSoftmax)) return false;
+        other = slot[partner * 32 + lane];
+        ++e;
+        return true;
+    }
+};
+
 __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_t sb,
                                                       uint32_t pl, int h, int nvalid, float& m,
                                                       double& l, bool rescale_allowed,
                                                       uint32_t olanes, uint64_t* pv_done,
-                                                      long long t, int j) {
+                                                      long long t, int j, AttnSwap& sw) {
     const float ninf = __int_as_float(0xff800000);
-    const int own0 = h * 64, other0 = (1 - h) * 64;
-    // pass 1: the row's maximum over its valid keys (both halves), own half kept in registers
+    const int own0 = h * 64;
+    // pass 1: the maximum over this half's valid keys, the scores kept in registers; then the
+    // row's maximum with the other half's
     float mt = ninf;
-    {
-        uint32_t x[32], y[32];
-        tmem_ld_issue_32x32b_x32(sb + other0, x);
-        tmem_ld_issue_32x32b_x32(sb + other0 + 32, y);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            if (other0 + i < nvalid) mt = fmaxf(mt, __fmul_rn(a.scale, __uint_as_float(x[i])));
-            if (other0 + 32 + i < nvalid)
-                mt = fmaxf(mt, __fmul_rn(a.scale, __uint_as_float(y[i])));
-        }
-    }
     uint32_t sr[2][32];
     tmem_ld_issue_32x32b_x32(sb + own0, sr[0]);
     tmem_ld_issue_32x32b_x32(sb + own0 + 32, sr[1]);
@@ -301,6 +310,9 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
         s[i] = __fmul_rn(a.scale, s[i]);
         if (own0 + i < nvalid) mt = fmaxf(mt, s[i]);
     }
+    float mo;
+    if (!sw.swap(mt, mo)) return false;
+    mt = fmaxf(mt, mo);
     float mn = m;
     if (mt != ninf && (m == ninf || mt > m + kAttnRescaleAbove)) mn = fmaxf(m, mt);
     // the previous tile's product has finished: P lo is free and O holds it
@@ -347,13 +359,15 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
 
 __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint32_t tmem,
                                              uint64_t* s_full, uint64_t* p_full,
-                                             uint64_t* pv_done, uint64_t* l_bar, float* l_part,
+                                             uint64_t* pv_done, uint64_t* x_bar, float* xch,
                                              uint32_t rank) {
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const int q = warp % 4;                       // TMEM lane quarter
     const int h = (warp - kAttnSoftWarp0) / 4;    // column half
     const uint32_t lanes = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    AttnSwap sw{xch, &x_bar[q], warp - kAttnSoftWarp0, warp - kAttnSoftWarp0 + (h ? -4 : 4),
+                lane, 0};
     long long t = 0;
     long long n = 0;
     bool ok = true;  // a bounded wait gave up: leave every loop
@@ -376,7 +390,7 @@ __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint
             }
             tc_fence_after();
             if (!attn_softmax_row_half(a, sb, lanes + kAttnColPLo, h, nvalid, m, l, j >= 1,
-                                       lanes + kAttnColO, pv_done, t, j)) {
+                                       lanes + kAttnColO, pv_done, t, j, sw)) {
                 ok = false;
                 break;
             }
@@ -386,14 +400,10 @@ __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint
             if (lane == 0) mbar_arrive_cluster(mapa_shared(&p_full[t & 1], 0));
         }
         if (!ok) break;
-        // the row sum: this half's plus the other warp's (slot n & 1, so a slot is rewritten
-        // only after the partner has read it: it arrives for unit n + 1 after reading unit n)
-        float* slot = l_part + (n & 1) * (8 * 32);
-        slot[(warp - kAttnSoftWarp0) * 32 + lane] = static_cast<float>(l);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&l_bar[q]);
-        if (!mbar_wait(&l_bar[q], static_cast<uint32_t>(n & 1), kErrAttnSoftmax)) break;
-        l += static_cast<double>(slot[(warp - kAttnSoftWarp0 + (h ? -4 : 4)) * 32 + lane]);
+        // the row sum: this half's plus the other warp's
+        float lo_half;
+        if (!sw.swap(static_cast<float>(l), lo_half)) break;
+        l += static_cast<double>(lo_half);
         // epilogue: O / l once the last product has finished
         if (!mbar_wait(pv_done, static_cast<uint32_t>((t - 1) & 1), kErrAttnSoftmax)) break;
         tc_fence_after();
@@ -439,9 +449,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* p_full = s_full + 2;   // [2]
     uint64_t* pv_done = p_full + 2;
     uint64_t* drain = pv_done + 1;
-    uint64_t* l_bar = drain + 1;     // [4]: the two warps of a lane quarter
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(l_bar + 4);
-    float* l_part = reinterpret_cast<float*>(smem + kAttnOffLPart);
+    uint64_t* x_bar = drain + 1;     // [4]: the two warps of a lane quarter
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(x_bar + 4);
+    float* xch = reinterpret_cast<float*>(smem + kAttnOffSwap);
     static_assert((2 * kAttnStages + 14) * 8 + 4 <= 256, "attention: barrier area too small");
 
     const int warp = threadIdx.x / 32;
@@ -461,7 +471,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         mbar_init(pv_done, 1);
         mbar_init(drain, 1);
-        for (int i = 0; i < 4; ++i) mbar_init(&l_bar[i], 2);
+        for (int i = 0; i < 4; ++i) mbar_init(&x_bar[i], 2);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -493,7 +503,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (warp < kAttnSoftWarp0) {
         attn_convert(a, smem, q_full, q_ready);
     } else {
-        attn_softmax(a, out, tmem, s_full, p_full, pv_done, l_bar, l_part, rank);
+        attn_softmax(a, out, tmem, s_full, p_full, pv_done, x_bar, xch, rank);
     }
 
     tc_fence_before();
