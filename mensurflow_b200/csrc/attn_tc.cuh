@@ -336,15 +336,20 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
     m = mn;
     // pass 2: P = exp(s - m) on valid keys (0 elsewhere), split into tf32 (hi, lo); P >= 0 is
     // finite, so the split needs no special cases: hi = P with its 13 low bits cleared, lo =
-    // P - hi (exact) rounded to tf32
+    // P - hi (exact) rounded to tf32. exp(s - m) = 2^(s log2 e - m log2 e), the exponent from one
+    // FMA (an absolute error of about |s - m| 2^-24 in it, a relative one of 0.7 times that in
+    // P: below 1e-6 for every term within e^-14 of the row's largest)
     float lt = 0.0f;
     uint32_t* hb = &sr[0][0];  // P's hi part replaces the scores it came from
+    const float ml = m * 1.44269504088896340736f;
+    const bool full = __all_sync(0xffffffffu, nvalid >= own0 + 64);  // no masked key in this half
 #pragma unroll
     for (int c = 0; c < 64; c += 16) {
         uint32_t lo[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const float p = (own0 + c + i < nvalid) ? expf(s[c + i] - m) : 0.0f;
+            const float e = exp2f(fmaf(s[c + i], 1.44269504088896340736f, -ml));
+            const float p = (full || own0 + c + i < nvalid) ? e : 0.0f;
             lt += p;
             const uint32_t hi = __float_as_uint(p) & 0xFFFFE000u;
             lo[i] = tf32_round_bits(__float_as_uint(p - __uint_as_float(hi)));
