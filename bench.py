@@ -875,7 +875,9 @@ def main():
         peak_sustained = peaks["bf16_sustained"] / 2.0 / per_product
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak, "frac_of_sustained_peak": achieved / peak_sustained,
-                    "traffic": profiled_traffic(args.workload, args.precision),
+                    "traffic": profiled_traffic("c4unfused" if args.workload == "c4" and
+                                                args.c4_unfused else args.workload,
+                                                args.precision),
                     "peak_source": (f"{peaks['source']} bf16 burst {peaks['bf16_burst']} "
                                     f"TFLOP/s / 2 (TF32) / {int(per_product)} "
                                     f"({args.precision})"),
