@@ -11,7 +11,8 @@
 // Built only against the reference's headers (include/, src/). With the op-layer patches of
 // host/patches applied to those sources (MENSURFLOW_HAS_OPID_GEMM), it also registers the
 // one-kernel gemm (OpId::Gemm, with bias and activation fused) and bias_add's bias gradient
-// (OpId::BiasGrad), and provides the device-to-device copy that Tensor::to() uses between GPUs.
+// (OpId::BiasGrad) and attention in one kernel (OpId::Attention), and provides the
+// device-to-device copy that Tensor::to() uses between GPUs.
 #include "backends/backend.hpp"
 #include "core/dispatcher.hpp"
 #include "core/registry.hpp"
@@ -270,6 +271,23 @@ void gemm_kernel(const OpArgs& args, Stream& stream) {
     check_mfk(mfk_gemm_f32(&d, s.raw()), "gemm");
 }
 
+// OpId::Attention (patched src/ops/attention.cpp): q, k, v of one contiguous shape
+// [..., L, 128], out of that shape, alpha the scale, `causal` the mask. One kernel in 3xTF32
+// (whatever the process-wide precision: the op promises the reference's fp32 results).
+void attention_kernel(const OpArgs& args, Stream& stream) {
+    auto& s = cuda(stream);
+    const Tensor& q = args.inputs[0];
+    const Tensor& out = args.outputs[0];
+    const std::int64_t len = q.size(-2), depth = q.size(-1);
+    const std::int64_t heads = len * depth > 0 ? q.numel() / (len * depth) : 0;
+    check_mfk(mfk_attention_f32(TensorAccess::data<float>(q),
+                                TensorAccess::data<float>(args.inputs[1]),
+                                TensorAccess::data<float>(args.inputs[2]),
+                                TensorAccess::data<float>(out), heads, len, depth,
+                                args.causal ? 1 : 0, args.alpha, s.raw()),
+              "attention");
+}
+
 // OpId::BiasGrad (patched bias_add backward, src/ops/elementwise.cpp:263-283): the column sums
 // of a contiguous [rows, features] gradient in row order, the host loop's bits.
 void bias_grad_kernel(const OpArgs& args, Stream& stream) {
@@ -465,6 +483,7 @@ class CudaBackend final : public Backend {
 #ifdef MENSURFLOW_HAS_OPID_GEMM
         dispatcher.register_kernel(key(OpId::Gemm), gemm_kernel);
         dispatcher.register_kernel(key(OpId::BiasGrad), bias_grad_kernel);
+        dispatcher.register_kernel(key(OpId::Attention), attention_kernel);
 #endif
     }
 

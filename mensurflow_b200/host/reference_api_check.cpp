@@ -139,6 +139,27 @@ void check_attention(Device gpu) {
                                      Execution::GPU);
         require_close(got, want, 1e-4, 1e-6, std::string("attention ") + c.name);
     }
+    // head dim 128 without a mask: the patched attention dispatches the one-kernel path
+    {
+        const Tensor q3 = input({2, 4, 384, 128}, 34, 0.088f), k3 = input({2, 4, 384, 128}, 35, 0.088f),
+                     v3 = input({2, 4, 384, 128}, 36, 0.088f);
+        for (bool causal : {true, false}) {
+            const std::int64_t launches = mfk_launch_count();
+            const Tensor got = attention(q3.to(gpu), k3.to(gpu), v3.to(gpu), nullptr, causal, 0.0f,
+                                         Execution::GPU);
+            const std::int64_t ran = mfk_launch_count() - launches;
+            // the K and V packing passes and the attention kernel (plus, on a device's first
+            // call, the one-time tf32 truncation check); the composed path would run two
+            // batched GEMMs with their packing passes, where and softmax
+            if (ran < 3 || ran > 4) {
+                throw std::runtime_error("attention with head dim 128 ran " + std::to_string(ran) +
+                                         " kernels, not the fused path's 3");
+            }
+            require_close(got, attention(q3, k3, v3, nullptr, causal, 0.0f, Execution::CPU), 1e-4,
+                          1e-6, causal ? "attention in one kernel, causal 2x4x384x128"
+                                       : "attention in one kernel 2x4x384x128");
+        }
+    }
     const Tensor q2 = input({4, 256, 64}, 31, 0.125f), k2 = input({4, 256, 64}, 32, 0.125f),
                  v2 = input({4, 256, 64}, 33, 0.125f);
     require_close(attention(q2.to(gpu), k2.to(gpu), v2.to(gpu), nullptr, true, 0.0f,

@@ -60,5 +60,6 @@ def test_reference_program_passes_on_b200(cuda, name):
                      "dot n=1048583", "div, row broadcast (bit-exact)",
                      "bias_add bias gradient on the device (bit-exact)",
                      "matmul dB on the device",
-                     "Tensor::contiguous() of a CUDA view: stepped slices"):
+                     "Tensor::contiguous() of a CUDA view: stepped slices",
+                     "attention in one kernel, causal 2x4x384x128"):
             assert line in out, (line, out[-3000:])
