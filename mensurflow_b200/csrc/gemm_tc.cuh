@@ -818,7 +818,37 @@ __device__ __forceinline__ void nonfinite_fixup_tmem(const GemmArgs& g, uint32_t
 struct EpiRow {
     const float* cin_row;
     bool has_cin, has_bias, vec_cin;
+    // The bias of the warp's columns of the tile, spread over the lanes: lane l holds columns
+    // 4l .. 4l+3 of the warp's part (loaded once per tile, before the accumulator is ready), and
+    // a chunk's values are broadcast from there with shuffles instead of 16 dependent loads.
+    float4 bias4;
+    int chunk;  // the chunk being computed: its 16 columns sit in lanes 4 chunk .. 4 chunk + 3
 };
+
+// Bias of column j (0..15) of the current chunk, from the lane that holds it. Warp-uniform.
+__device__ __forceinline__ float chunk_bias(const EpiRow& e, int j) {
+    const float b = (j & 3) == 0 ? e.bias4.x : (j & 3) == 1 ? e.bias4.y
+                  : (j & 3) == 2 ? e.bias4.z : e.bias4.w;
+    return __shfl_sync(0xffffffffu, b, e.chunk * 4 + (j >> 2));
+}
+
+// The warp's bias values for columns [col_base, col_base + cols) of the tile (cols <= 128), lane
+// l taking columns 4l .. 4l+3; columns at or past n read as 0 (never used).
+__device__ __forceinline__ float4 load_tile_bias(const GemmArgs& g, int col_base, int cols,
+                                                 int lane) {
+    float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int c = col_base + 4 * lane;
+    if (g.bias == nullptr || 4 * lane >= cols || c >= g.n) return b;
+    if (c + 4 <= g.n && (reinterpret_cast<uintptr_t>(g.bias + c) & 15) == 0) {
+        b = __ldg(reinterpret_cast<const float4*>(g.bias + c));
+    } else {
+        b.x = __ldg(g.bias + c);
+        if (c + 1 < g.n) b.y = __ldg(g.bias + c + 1);
+        if (c + 2 < g.n) b.z = __ldg(g.bias + c + 2);
+        if (c + 3 < g.n) b.w = __ldg(g.bias + c + 3);
+    }
+    return b;
+}
 
 __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow& e, int col0,
                                                  const uint32_t (&r)[kEpiCols],
@@ -834,7 +864,7 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
                 float x = __uint_as_float(r[j + q]);
                 if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
                 if (e.has_cin) x = __fadd_rn(x, __fmul_rn(g.beta, c4[q]));
-                if (e.has_bias) x = __fadd_rn(x, g.bias[col0 + j + q]);
+                if (e.has_bias) x = __fadd_rn(x, chunk_bias(e, j + q));
                 v[j + q] = x;
             }
         }
@@ -846,7 +876,7 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
             if (g.alpha != 1.0f) x = __fmul_rn(g.alpha, x);
             if (col < g.n) {
                 if (e.has_cin) x = __fadd_rn(x, __fmul_rn(g.beta, e.cin_row[static_cast<long long>(col) * g.c_in_cs]));
-                if (e.has_bias) x = __fadd_rn(x, g.bias[col]);
+                if (e.has_bias) x = __fadd_rn(x, chunk_bias(e, j));
             }
             v[j] = x;
         }
@@ -901,9 +931,12 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
         for (int i = 0; i < 2; ++i)
             inf_packed |= g.ra != nullptr && g.nf_word[i] != nullptr && *g.nf_word[i] == g.nf_tag[i];
     }
+    static_assert(kHalf <= 128, "a warp's bias columns must fit four per lane");
     WorkIter<CG> wi(g);
     for (Work w; wi.next(g, w);) {
         const TileCoord tc = tile_coord(g, w.tile);
+        // the bias of this warp's columns, in flight while the accumulator is finished
+        if (e.has_bias) e.bias4 = load_tile_bias(g, tc.tn * BN + half * kHalf, kHalf, lane);
         if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) break;
         tc_fence_after();
         const int row0 = tc.tm * C::kTileM + static_cast<int>(rank) * kBM + ew * 32;
@@ -997,6 +1030,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                         v[j] = g.alpha == 1.0f ? x : __fmul_rn(g.alpha, x);
                     }
                 } else {
+                    e.chunk = ci;
                     epilogue_general(g, e, col0, r, v);
                 }
                 if (g.tma_store) {
