@@ -823,7 +823,26 @@ struct EpiRow {
     // a chunk's values are broadcast from there with shuffles instead of 16 dependent loads.
     float4 bias4;
     int chunk;  // the chunk being computed: its 16 columns sit in lanes 4 chunk .. 4 chunk + 3
+    // cin_pre: this chunk's C_in was copied ahead into the thread's row of a staging box, at
+    // shared address cin_smem (16-byte piece q at q ^ cin_swz), and is read from there.
+    bool cin_pre;
+    uint32_t cin_smem;
+    uint32_t cin_swz;
 };
+
+// Copies this lane's 64 bytes of C_in for the chunk at col0 into row `lane` of the staging box
+// at `buf`, in the box's swizzled layout, with cp.async: the loads are in flight without
+// holding registers. Commits one group per call (empty when the lane has no whole chunk there).
+__device__ __forceinline__ void cin_fetch(const EpiRow& e, uint32_t buf, int col0, int n,
+                                          int lane) {
+    if (e.has_cin && col0 + kEpiCols <= n) {
+        const float* src = e.cin_row + col0;
+#pragma unroll
+        for (int q = 0; q < kEpiCols / 4; ++q)
+            cp_async_16(buf + lane * (kEpiCols * 4) + ((q ^ ((lane >> 1) & 3)) << 4), src + 4 * q);
+    }
+    cp_async_commit();
+}
 
 // Bias of column j (0..15) of the current chunk, from the lane that holds it. Warp-uniform.
 __device__ __forceinline__ float chunk_bias(const EpiRow& e, int j) {
@@ -857,7 +876,11 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 4) {
             float4 cin4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e.has_cin) cin4 = *reinterpret_cast<const float4*>(e.cin_row + col0 + j);
+            if (e.has_cin) {
+                cin4 = e.cin_pre
+                           ? ld_shared_v4(e.cin_smem + (((j >> 2) ^ e.cin_swz) << 4))
+                           : *reinterpret_cast<const float4*>(e.cin_row + col0 + j);
+            }
             const float c4[4] = {cin4.x, cin4.y, cin4.z, cin4.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -896,7 +919,7 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
 // The epilogue warps (eight, or four in ATMEM kernels): warp w reads TMEM lane quarter (w % 4)
 // — the 32 rows it may access — and, with eight warps, the columns of its half of the tile, in
 // chunks of kEpiCols.
-template <int CG, int BN, bool SPLIT3, bool ATMEM>
+template <int CG, int BN, bool SPLIT3, bool ATMEM, bool CINA>
 __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap* tmC,
                                             uint8_t* epi_smem, uint32_t tmem_base,
                                             uint64_t* acc_full, uint64_t* acc_empty,
@@ -920,6 +943,14 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
                          (g.c_bs % 4 == 0);
     // This warp's two staging boxes: 32 rows of 64 B, SWIZZLE_64B as the TMA store reads them.
     const uint32_t box0 = smem_u32(epi_smem + (warp - C::kEpiWarp0C) * 2 * C::kEpiBoxBytes);
+    // CINA (short K, where the epilogue bounds the kernel) and TMA stores: the boxes also carry
+    // C_in. Each chunk's C_in is copied into the box its result will be staged in, one chunk
+    // ahead (the tile's first chunk while the accumulator is still being computed), and the
+    // result overwrites it in place.
+    const bool pre_cin = CINA && e.vec_cin && g.tma_store;
+    e.cin_pre = false;
+    e.cin_smem = 0u;
+    e.cin_swz = static_cast<uint32_t>((lane >> 1) & 3);
     int box = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -935,10 +966,6 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     WorkIter<CG> wi(g);
     for (Work w; wi.next(g, w);) {
         const TileCoord tc = tile_coord(g, w.tile);
-        // the bias of this warp's columns, in flight while the accumulator is finished
-        if (e.has_bias) e.bias4 = load_tile_bias(g, tc.tn * BN + half * kHalf, kHalf, lane);
-        if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) break;
-        tc_fence_after();
         const int row0 = tc.tm * C::kTileM + static_cast<int>(rank) * kBM + ew * 32;
         const int row = row0 + lane;
         const bool row_ok = row < g.m;
@@ -947,6 +974,20 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
         e.cin_row = e.has_cin ? g.c_in + static_cast<long long>(tc.b) * g.c_in_bs +
                                     static_cast<long long>(row) * g.c_in_rs
                               : nullptr;
+        const int col_w = tc.tn * BN + half * kHalf;  // this warp's first column of the tile
+        // the bias of this warp's columns, in flight while the accumulator is finished
+        if (e.has_bias) e.bias4 = load_tile_bias(g, col_w, kHalf, lane);
+        // and the first chunk's C_in, for a whole tile (a stream-K part fetches it only once it
+        // knows it sums the tile), into the box no store is reading any more
+        bool cin_ahead = false;
+        if (pre_cin && w.kb0 == 0 && w.kb1 == g.num_kb && row0 < g.m && col_w < g.n) {
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+            cin_fetch(e, box0 + box * C::kEpiBoxBytes, col_w, g.n, lane);
+            cin_ahead = true;
+        }
+        if (!mbar_wait(&acc_full[acc], acc_phase, kErrEpilogueWait)) break;
+        tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) +
                                static_cast<uint32_t>(acc * BN + half * kHalf);
         // 3xTF32: the k-blocks behind this accumulator may have met an infinity. The converters
@@ -1020,8 +1061,29 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
             uint32_t (&r)[kEpiCols] = h ? rb : ra;
             uint32_t (&rn)[kEpiCols] = h ? ra : rb;
             if (ci + 1 < kChunks) tmem_ld_issue_32x32b_x16(tbase + (ci + 1) * kEpiCols, rn);
-            const int col0 = tc.tn * BN + half * kHalf + ci * kEpiCols;
+            const int col0 = col_w + ci * kEpiCols;
             if (col0 < g.n && row0 < g.m) {
+                if (pre_cin) {
+                    // this chunk's C_in goes to `box` (unless fetched already), the next chunk's
+                    // to the other box once the store issued from it has read it
+                    if (!cin_ahead) {
+                        if (lane == 0) bulk_wait_read<0>();
+                        __syncwarp();
+                        cin_fetch(e, box0 + box * C::kEpiBoxBytes, col0, g.n, lane);
+                        cin_ahead = true;
+                    }
+                    if (ci + 1 < kChunks) {
+                        if (lane == 0) bulk_wait_read<0>();
+                        __syncwarp();
+                        cin_fetch(e, box0 + (box ^ 1) * C::kEpiBoxBytes, col0 + kEpiCols, g.n,
+                                  lane);
+                        cp_async_wait<1>();
+                    } else {
+                        cp_async_wait<0>();
+                    }
+                    e.cin_pre = true;
+                    e.cin_smem = box0 + box * C::kEpiBoxBytes + lane * (kEpiCols * 4);
+                }
                 float v[kEpiCols];
                 if (plain) {
 #pragma unroll
@@ -1132,7 +1194,7 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
     __syncwarp();
 }
 
-template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM = false>
+template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM = false, bool CINA = false>
 __global__ void __launch_bounds__(TcConfig<CG, BN, SPLIT3, ATMEM>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0,
                    const __grid_constant__ CUtensorMap tmA1,
@@ -1238,7 +1300,7 @@ __global__ void __launch_bounds__(TcConfig<CG, BN, SPLIT3, ATMEM>::kThreads, 1)
     } else if (!ATMEM && ASPLIT && warp >= kCvtWarp0 && warp < kCvtWarp0 + kCvtThreads / 32) {
         tc_convert<CG, BN, SPLIT3>(g, stages, a_full, converted, inf_seen);
     } else if (warp >= C::kEpiWarp0C && warp < C::kEpiWarp0C + C::kEpiWarpsC) {
-        tc_epilogue<CG, BN, SPLIT3, ATMEM>(g, &tmC, epi_smem, tmem_base, acc_full, acc_empty,
+        tc_epilogue<CG, BN, SPLIT3, ATMEM, CINA>(g, &tmC, epi_smem, tmem_base, acc_full, acc_empty,
                                            rank, inf_seen);
     }
 

@@ -263,17 +263,21 @@ bool tma_readable(const Operand& o, int64_t k) {
 // in the kernel whenever TMA can read it where it lies; B, and an A it cannot read, are packed.
 constexpr int64_t kInKernelSplitMaxN = INT64_MAX;
 
+// The C_in-ahead epilogue (see run_gemm) for K up to this many k-blocks, counted three times in
+// 3xTF32: K <= 256 in 3xTF32, K <= 768 in 1xTF32.
+constexpr int kCinAheadMaxKBlocks = 24;
 
 
-// One kernel instantiation per (CG, BN, SPLIT3, ASPLIT, ATMEM); `slot` indexes its per-device
-// set-up flags.
-template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM = false>
+
+// One kernel instantiation per (CG, BN, SPLIT3, ASPLIT, ATMEM, CINA); `slot` indexes its
+// per-device set-up flags.
+template <int CG, int BN, bool SPLIT3, bool ASPLIT, bool ATMEM = false, bool CINA = false>
 int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
               const CUtensorMap& b1, const CUtensorMap& cmap, const GemmArgs& g_in,
               DeviceInfo* info, int slot, cudaStream_t stream, bool allow_sk) {
     GemmArgs g = g_in;
     using C = mfk::TcConfig<CG, BN, SPLIT3, ATMEM>;
-    auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3, ASPLIT, ATMEM>;
+    auto kernel = mfk::gemm_tc_kernel<CG, BN, SPLIT3, ASPLIT, ATMEM, CINA>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.blockDim = dim3(C::kThreads, 1, 1);
@@ -721,8 +725,20 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
     // 3xTF32 with A read in place: the kernel splits A in shared memory.
     const bool asplit = split3 && A.direct;
     g.raw_hi = raw_hi ? 1 : 0;
+    // Short K with C_in: the epilogue, not the MMAs, bounds the kernel, and the variant that
+    // copies C_in into the staging boxes a chunk ahead pays (8192 x 8192 x 128, beta 1, bias:
+    // 215 -> 189 us). Where the MMAs of a tile outlast its epilogue it does not (K = 1024:
+    // 521 -> 538 us), so only short K takes it.
+    const bool cin_ahead = g.c_in != nullptr && g.tma_store &&
+                           g.num_kb * (split3 ? 3 : 1) <= kCinAheadMaxKBlocks;
     if (cg == 2 && BN == 256) {
-        if (asplit) return launch_tc<2, 256, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 6, stream, fixed == nullptr);
+        if (asplit) {
+            return cin_ahead
+                ? launch_tc<2, 256, true, true, false, true>(ma0, ma1, mb0, mb1, mc, g, info, 11, stream, fixed == nullptr)
+                : launch_tc<2, 256, true, true>(ma0, ma1, mb0, mb1, mc, g, info, 6, stream, fixed == nullptr);
+        }
+        if (!split3 && cin_ahead)
+            return launch_tc<2, 256, false, false, false, true>(ma0, ma1, mb0, mb1, mc, g, info, 12, stream, fixed == nullptr);
         return split3 ? launch_tc<2, 256, true, false>(ma0, ma1, mb0, mb1, mc, g, info, 0, stream, fixed == nullptr)
                       : launch_tc<2, 256, false, false>(ma0, ma1, mb0, mb1, mc, g, info, 1, stream, fixed == nullptr);
     }

@@ -443,6 +443,23 @@ __device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
     return v;
 }
 
+// ---- per-thread asynchronous copies, global -> shared (16 bytes, cached in L2 only) ----------
+// The copies complete in the issuing thread's groups: cp_async_wait<N> returns once at most N of
+// its committed groups are still pending, and their data is then visible to that thread.
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -316,13 +316,6 @@ constexpr int kBgThreads = 256;
 __device__ __forceinline__ void cp_async_4(uint32_t dst, const float* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 __global__ void __launch_bounds__(kBgThreads) bias_grad_kernel(const float* __restrict__ g,
                                                                long long rows, long long cols,

@@ -476,6 +476,45 @@ def test_stream_k_tail(cuda, shape, precision):
     no_fault()
 
 
+# Short K with C_in (K <= 256 in 3xTF32, K <= 768 in 1xTF32; N > 128, C TMA-writable) takes the
+# epilogue variant that copies C_in into the staging boxes a chunk ahead: ragged rows and
+# columns (a partial 16-column chunk), a single k-block, a stream-K tail (124 tiles on 74
+# units, 3xTF32), a batch; (m, n, k, batch).
+CIN_AHEAD_SHAPES = [(1000, 1000, 100, 1), (520, 260, 16, 1), (1024, 7936, 256, 1),
+                    (300, 516, 64, 3)]
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("shape", CIN_AHEAD_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_short_k_with_c_in(cuda, shape, precision):
+    """The oracle's result within the path's bound; the same bits with C_in updated in place
+    (C_in is C) and with C_in as a transposed view (read element by element); batched."""
+    m, n, k, batch = shape
+    rng = np.random.default_rng(m + 3 * n + 5 * k + batch)
+    a = rng.standard_normal((batch, m, k)).astype(np.float32)
+    b = rng.standard_normal((batch, k, n)).astype(np.float32)
+    c = rng.standard_normal((batch, m, n)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    ta, tb, tc, tbias = dev(a, cuda), dev(b, cuda), dev(c, cuda), dev(bias, cuda)
+    got = mf.gemm(ta[0], tb[0], 0.5, tc[0], 1.0, bias=tbias, precision=precision)
+    want = O.gemm(a[0], b[0], 0.5, c[0], 1.0, bias=bias)
+    mag = 0.5 * O.abs_product(a[0], b[0]) + np.abs(c[0]) + np.abs(bias)[None, :]
+    assert_close(host(got), want, mag, tol(precision), f"{shape} {precision}")
+    in_place = tc[0].clone()
+    mf.gemm(ta[0], tb[0], 0.5, in_place, 1.0, bias=tbias, precision=precision, out=in_place)
+    assert torch.equal(in_place, got), "C_in updated in place differs"
+    c_view = dev(np.ascontiguousarray(c[0].T), cuda).t()
+    got_view = mf.gemm(ta[0], tb[0], 0.5, c_view, 1.0, bias=tbias, precision=precision)
+    assert torch.equal(got_view, got), "C_in as a strided view differs"
+    if batch > 1:
+        out = mf.gemm_strided_batched(ta, tb, 0.5, tc, 1.0, precision=precision)
+        for i in range(batch):
+            want = O.gemm(a[i], b[i], 0.5, c[i], 1.0)
+            mag = 0.5 * O.abs_product(a[i], b[i]) + np.abs(c[i])
+            assert_close(host(out[i]), want, mag, tol(precision), f"{shape} batched [{i}]")
+    no_fault()
+
+
 # The shape tables of the reference's packed-GEMM test (tests/ops/gemm_packed_test.cpp): around
 # every micro-tile edge (:175-179), odd extras (:181-182), the threaded and large cases (:186,
 # :275), single rows (:380-381), narrow outputs (:400-403), and the strided-view shapes (:436-438).
