@@ -6,9 +6,9 @@
 // Replaces, for the causal / unmasked case with head dimension 128, the reference's composition
 // (src/ops/attention.cpp:48-98: gemm_strided_batched for S, where(-inf) for the mask, softmax,
 // gemm_strided_batched for P V), which writes and re-reads the whole [L, L] score matrix of every
-// head. Softmax follows the reference's numerics where it matters (scores are fl(scale * QK), the
-// row's exponentials are normalised by their sum; src/backends/cpu/ops/softmax/softmax.cpp:11-80)
-// but is evaluated online: running row maximum m and sum l per key tile, O rescaled when m grows
+// head. Softmax follows the reference's numerics where it matters (the row maximum is that of
+// fl(scale * QK), the row's exponentials are normalised by their sum;
+// src/backends/cpu/ops/softmax/softmax.cpp:11-80) but is evaluated online: running row maximum m and sum l per key tile, O rescaled when m grows
 // (only when it grows by more than 8, so the rescaling is rare and every exponential stays below
 // e^8), O / l at the end.
 //
@@ -77,6 +77,7 @@ struct AttnArgs {
     int causal;
     float scale;
     long long num_units;  // heads * num_qb
+    int q_raw_hi;         // the tensor cores truncate fp32 operands: raw Q serves as its hi part
 };
 
 // Work unit u -> (head, query block): the longest units (last query blocks under the causal
@@ -122,11 +123,12 @@ __device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorM
         // Q: after the previous unit's S products have read it
         if (n > 0 && !mbar_wait(q_free, static_cast<uint32_t>((n - 1) & 1), kErrAttnProducer))
             return;
-        mbar_arrive_expect_tx(q_full, kAttnQBytes);
         const int qrow = qb * kAttnUnitRows + static_cast<int>(rank) * kAttnRows;
-        for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc)
-            tma_load_3d(smem + kc * kAttnQChunkBytes, tmQ, q_full, kc * kAttnChunk, qrow, head,
-                        keep);
+        for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc) {  // one barrier per 32-column chunk
+            mbar_arrive_expect_tx(&q_full[kc], kAttnQChunkBytes);
+            tma_load_3d(smem + kc * kAttnQChunkBytes, tmQ, &q_full[kc], kc * kAttnChunk, qrow,
+                        head, keep);
+        }
         const int krow = static_cast<int>(rank) * (kAttnKeys / 2);
         for (int j = 0; j <= tiles; ++j) {
             if (j < tiles) {  // K_j: 64 keys of the tile per CTA, four chunks of the head dim
@@ -143,30 +145,49 @@ __device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorM
     }
 }
 
-// ---- converters: Q raw -> (hi, lo) in shared memory, in place ---------------------------------
+// ---- converters: Q raw -> (hi, lo) in shared memory, chunk by chunk --------------------------
+// Each 32-column chunk is released to the MMA issuer as soon as it is split, so the unit's first
+// S product starts after one chunk rather than all four. With q_raw_hi the raw values stay as
+// the hi part (the tensor cores truncate them to the same tf32 value) and only lo is written.
 __device__ __forceinline__ void attn_convert(const AttnArgs& a, uint8_t* smem, uint64_t* q_full,
                                             uint64_t* q_ready) {
     const int ct = threadIdx.x - kAttnCvtWarp0 * 32;
     const int lane = threadIdx.x % 32;
     float4* hi = reinterpret_cast<float4*>(smem);
     float4* lo = reinterpret_cast<float4*>(smem + kAttnOffQLo);
+    constexpr int kChunkVecs = kAttnQChunkBytes / 16;
     long long n = 0;
     for (long long u = blockIdx.x / 2; u < a.num_units; u += gridDim.x / 2, ++n) {
-        if (!mbar_wait(q_full, static_cast<uint32_t>(n & 1), kErrAttnConvert)) return;
+        for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc) {
+            if (!mbar_wait(&q_full[kc], static_cast<uint32_t>(n & 1), kErrAttnConvert)) return;
+            if (a.q_raw_hi) {
 #pragma unroll 4
-        for (int i = ct; i < kAttnQBytes / 16; i += 64) {
-            const float4 x = hi[i];
-            float4 h, l;
-            split_tf32(x.x, h.x, l.x);
-            split_tf32(x.y, h.y, l.y);
-            split_tf32(x.z, h.z, l.z);
-            split_tf32(x.w, h.w, l.w);
-            hi[i] = h;
-            lo[i] = l;
+                for (int i = kc * kChunkVecs + ct; i < (kc + 1) * kChunkVecs; i += 64) {
+                    const float4 x = hi[i];
+                    float4 h, l;  // h unused: the raw value is hi
+                    split_tf32(x.x, h.x, l.x);
+                    split_tf32(x.y, h.y, l.y);
+                    split_tf32(x.z, h.z, l.z);
+                    split_tf32(x.w, h.w, l.w);
+                    lo[i] = l;
+                }
+            } else {
+#pragma unroll 4
+                for (int i = kc * kChunkVecs + ct; i < (kc + 1) * kChunkVecs; i += 64) {
+                    const float4 x = hi[i];
+                    float4 h, l;
+                    split_tf32(x.x, h.x, l.x);
+                    split_tf32(x.y, h.y, l.y);
+                    split_tf32(x.z, h.z, l.z);
+                    split_tf32(x.w, h.w, l.w);
+                    hi[i] = h;
+                    lo[i] = l;
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(&q_ready[kc], 0));
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(q_ready, 0));
     }
 }
 
@@ -190,10 +211,12 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
             phase ^= 1u;
         }
     };
-    // S_t = Q K_j^T into S buffer t & 1: four stages of K (hi, lo), 3 products per k-step
-    auto s_product = [&](long long tt) {
+    // S_t = Q K_j^T into S buffer t & 1. On the unit's first tile each chunk of Q is waited for
+    // (q_ready[kc], phase `qphase`) just before its MMAs.
+    auto s_product = [&](long long tt, bool first, uint32_t qphase) {
         const uint32_t d = tmem + kAttnColS + static_cast<uint32_t>((tt & 1) * 128);
         for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc) {
+            if (first && !mbar_wait(&q_ready[kc], qphase, kErrAttnMma)) return false;
             if (!mbar_wait(&full[stage], phase, kErrAttnMma)) return false;
             tc_fence_after();
             const uint32_t bh = ring + stage * kAttnStageBytes;
@@ -207,9 +230,10 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
                 const uint64_t dal = smem_desc(al + koff, 16, 1024, kSwizzle128B);
                 const uint64_t dbh = smem_desc(bh + koff, 16, 1024, kSwizzle128B);
                 const uint64_t dbl = smem_desc(bl + koff, 16, 1024, kSwizzle128B);
-                mma_tf32_cg2(d, dal, dbh, idesc, (kc > 0 || ks > 0) ? 1u : 0u);
-                mma_tf32_cg2(d, dah, dbl, idesc, 1u);
-                mma_tf32_cg2(d, dah, dbh, idesc, 1u);
+                // Q hi read once for its two products (A collector)
+                mma_tf32_cg2_a_fill(d, dah, dbh, idesc, (kc > 0 || ks > 0) ? 1u : 0u);
+                mma_tf32_cg2_a_lastuse(d, dah, dbl, idesc, 1u);
+                mma_tf32_cg2(d, dal, dbh, idesc, 1u);
             }
             mma_commit_cg2_mc(&empty[stage], kPair);
             next_stage();
@@ -250,11 +274,9 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
         int head, qb;
         attn_unit(a, u, head, qb);
         const int tiles = attn_tiles(a, qb);
-        if (!mbar_wait(q_ready, static_cast<uint32_t>(n & 1), kErrAttnMma)) return;
-        tc_fence_after();
         const long long t0 = t;
         for (int j = 0; j < tiles; ++j) {
-            if (!s_product(t0 + j)) return;
+            if (!s_product(t0 + j, j == 0, static_cast<uint32_t>(n & 1))) return;
             if (j == tiles - 1) mma_commit_cg2_mc(q_free, kPair);  // every S of the unit
             if (j >= 1 && !pv_product(t0 + j - 1, j == 1)) return;
         }
@@ -297,19 +319,37 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
                                                       long long t, int j, AttnSwap& sw) {
     const float ninf = __int_as_float(0xff800000);
     const int own0 = h * 64;
-    // pass 1: the maximum over this half's valid keys, the scores kept in registers; then the
-    // row's maximum with the other half's
-    float mt = ninf;
+    // pass 1: the maximum of fl(scale * s) over this half's valid keys, the raw scores kept in
+    // registers; then the row's maximum with the other half's. Rounding is monotonic, so for
+    // scale >= 0 that maximum is fl(scale * max s), and for scale < 0 fl(scale * min s): one
+    // multiply per row instead of one per score. Four independent chains.
     uint32_t sr[2][32];
     tmem_ld_issue_32x32b_x32(sb + own0, sr[0]);
     tmem_ld_issue_32x32b_x32(sb + own0 + 32, sr[1]);
     tmem_ld_wait();
-    float* s = reinterpret_cast<float*>(&sr[0][0]);
+    const float* s = reinterpret_cast<const float*>(&sr[0][0]);
+    const bool full = __all_sync(0xffffffffu, nvalid >= own0 + 64);  // no masked key in this half
+    const bool neg = a.scale < 0.0f;
+    const float pinf = __int_as_float(0x7f800000);
+    float ext[4];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-        s[i] = __fmul_rn(a.scale, s[i]);
-        if (own0 + i < nvalid) mt = fmaxf(mt, s[i]);
+    for (int c = 0; c < 4; ++c) ext[c] = neg ? pinf : ninf;
+    if (full && !neg) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) ext[i & 3] = fmaxf(ext[i & 3], s[i]);
+    } else if (!neg) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+            if (own0 + i < nvalid) ext[i & 3] = fmaxf(ext[i & 3], s[i]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+            if (own0 + i < nvalid) ext[i & 3] = fminf(ext[i & 3], s[i]);
     }
+    const float e01 = neg ? fminf(ext[0], ext[1]) : fmaxf(ext[0], ext[1]);
+    const float e23 = neg ? fminf(ext[2], ext[3]) : fmaxf(ext[2], ext[3]);
+    const float ex = neg ? fminf(e01, e23) : fmaxf(e01, e23);
+    float mt = own0 < nvalid ? __fmul_rn(a.scale, ex) : ninf;
     float mo;
     if (!sw.swap(mt, mo)) return false;
     mt = fmaxf(mt, mo);
@@ -334,23 +374,24 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
         l *= static_cast<double>(f);
     }
     m = mn;
-    // pass 2: P = exp(s - m) on valid keys (0 elsewhere), split into tf32 (hi, lo); P >= 0 is
-    // finite, so the split needs no special cases: hi = P with its 13 low bits cleared, lo =
-    // P - hi (exact) rounded to tf32. exp(s - m) = 2^(s log2 e - m log2 e), the exponent from one
-    // FMA (an absolute error of about |s - m| 2^-24 in it, a relative one of 0.7 times that in
-    // P: below 1e-6 for every term within e^-14 of the row's largest)
-    float lt = 0.0f;
+    // pass 2: P = exp(scale s - m) on valid keys (0 elsewhere), split into tf32 (hi, lo); P >= 0
+    // is finite, so the split needs no special cases: hi = P with its 13 low bits cleared, lo =
+    // P - hi (exact) rounded to tf32. exp(scale s - m) = 2^(s fl(scale log2 e) - fl(m log2 e)),
+    // the exponent from one FMA of the raw score (an absolute error of about
+    // (|scale s| + |m|) 2^-23 in it, a relative one of 0.7 times that in P: below 1e-6 for
+    // scores up to ~10)
+    float lt[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     uint32_t* hb = &sr[0][0];  // P's hi part replaces the scores it came from
     const float ml = m * 1.44269504088896340736f;
-    const bool full = __all_sync(0xffffffffu, nvalid >= own0 + 64);  // no masked key in this half
+    const float sl = a.scale * 1.44269504088896340736f;  // exponent of fl(scale s) - m: s sl - ml
 #pragma unroll
     for (int c = 0; c < 64; c += 16) {
         uint32_t lo[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const float e = exp2f(fmaf(s[c + i], 1.44269504088896340736f, -ml));
+            const float e = exp2f(fmaf(s[c + i], sl, -ml));
             const float p = (full || own0 + c + i < nvalid) ? e : 0.0f;
-            lt += p;
+            lt[i & 3] += p;
             const uint32_t hi = __float_as_uint(p) & 0xFFFFE000u;
             lo[i] = tf32_round_bits(__float_as_uint(p - __uint_as_float(hi)));
             hb[c + i] = hi;
@@ -358,7 +399,7 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
         tmem_st_32x32b_x16(sb + own0 + c, *reinterpret_cast<const uint32_t(*)[16]>(hb + c));
         tmem_st_32x32b_x16(pl + own0 + c, lo);
     }
-    l += static_cast<double>(lt);
+    l += static_cast<double>((lt[0] + lt[1]) + (lt[2] + lt[3]));
     return true;
 }
 
@@ -447,9 +488,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAttnOffBars);
     uint64_t* full = bars;
     uint64_t* empty = full + kAttnStages;
-    uint64_t* q_full = empty + kAttnStages;
-    uint64_t* q_ready = q_full + 1;
-    uint64_t* q_free = q_ready + 1;
+    uint64_t* q_full = empty + kAttnStages;  // [4]: per 32-column chunk of Q
+    uint64_t* q_ready = q_full + 4;          // [4]
+    uint64_t* q_free = q_ready + 4;
     uint64_t* s_full = q_free + 1;   // [2]
     uint64_t* p_full = s_full + 2;   // [2]
     uint64_t* pv_done = p_full + 2;
@@ -457,7 +498,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* x_bar = drain + 1;     // [4]: the two warps of a lane quarter
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(x_bar + 4);
     float* xch = reinterpret_cast<float*>(smem + kAttnOffSwap);
-    static_assert((2 * kAttnStages + 14) * 8 + 4 <= 256, "attention: barrier area too small");
+    static_assert((2 * kAttnStages + 20) * 8 + 4 <= 256, "attention: barrier area too small");
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -467,8 +508,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(q_full, 1);
-        mbar_init(q_ready, 2 * 2);  // both converter warps of both CTAs
+        for (int c = 0; c < 4; ++c) {
+            mbar_init(&q_full[c], 1);
+            mbar_init(&q_ready[c], 2 * 2);  // both converter warps of both CTAs
+        }
         mbar_init(q_free, 1);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);

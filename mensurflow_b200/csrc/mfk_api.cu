@@ -1245,6 +1245,7 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
     a.causal = causal != 0 ? 1 : 0;
     a.scale = scale;
     a.num_units = static_cast<long long>(a.heads) * a.num_qb;
+    a.q_raw_hi = k_raw_hi ? 1 : 0;
     auto kernel = mfk::attn_tc_kernel;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];

@@ -335,6 +335,31 @@ __device__ __forceinline__ void mma_tf32_cg2(uint32_t d_tmem, uint64_t a_desc, u
         : "memory");
 }
 
+// The same MMA with the A collector: `fill` reads A from shared memory and keeps it in the
+// collector buffer, `lastuse` takes A from that buffer (filled by the previous MMA this thread
+// issued, with the same A descriptor) and releases it. A pair of them reads A once.
+__device__ __forceinline__ void mma_tf32_cg2_a_fill(uint32_t d_tmem, uint64_t a_desc,
+                                                    uint64_t b_desc, uint32_t idesc,
+                                                    uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32.collector::a::fill [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_cg2_a_lastuse(uint32_t d_tmem, uint64_t a_desc,
+                                                       uint64_t b_desc, uint32_t idesc,
+                                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32.collector::a::lastuse [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem of both CTAs] (+)= A[tmem: lanes = the CTA's 128 rows, one 32-bit column per k]
 // * B[smem desc, N/2 rows in each CTA]. A read from tensor memory must be K-major.
 __device__ __forceinline__ void mma_tf32_ts_cg2(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
