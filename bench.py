@@ -933,11 +933,45 @@ def main():
                 torch.cuda.synchronize()
                 best = max(best, hbuf.numel() * 4 / (l0.elapsed_time(l1) * 1e-3) / 1e9)
             link[f"{what}_gbs"] = best
-        del hbuf, dbuf
+        # both directions at once (each on its own stream): on these boxes each runs ~10 %
+        # slower than alone, which the simple bound below does not count
+        hbuf2 = torch.empty(64 << 20, pin_memory=True)
+        dbuf2 = torch.empty(64 << 20, device=device)
+        s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        duplex = {"h2d_gbs": 0.0, "d2h_gbs": 0.0}
+        for _ in range(3):
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            with torch.cuda.stream(s_h2d):
+                ev[0].record(s_h2d)
+                dbuf.copy_(hbuf, non_blocking=True)
+                ev[1].record(s_h2d)
+            with torch.cuda.stream(s_d2h):
+                ev[2].record(s_d2h)
+                hbuf2.copy_(dbuf2, non_blocking=True)
+                ev[3].record(s_d2h)
+            torch.cuda.synchronize()
+            duplex["h2d_gbs"] = max(duplex["h2d_gbs"],
+                                    hbuf.numel() * 4 / (ev[0].elapsed_time(ev[1]) * 1e-3) / 1e9)
+            duplex["d2h_gbs"] = max(duplex["d2h_gbs"],
+                                    hbuf.numel() * 4 / (ev[2].elapsed_time(ev[3]) * 1e-3) / 1e9)
+        link["both_directions"] = duplex
+        del hbuf, dbuf, hbuf2, dbuf2
         bound_ms = max(h2d_bytes / (link["h2d_gbs"] * 1e9), d2h_bytes / (link["d2h_gbs"] * 1e9)) * 1e3
+        # The same bound with the two directions slowing each other while both run: the smaller
+        # direction overlaps the larger one completely, at the rates measured with both running,
+        # and the rest of the larger one runs alone.
+        hb, db = h2d_bytes / 1e9, d2h_bytes / 1e9
+        if hb >= db:
+            both_s = db / duplex["d2h_gbs"]
+            duplex_ms = (both_s + max(0.0, hb - duplex["h2d_gbs"] * both_s) / link["h2d_gbs"]) * 1e3
+        else:
+            both_s = hb / duplex["h2d_gbs"]
+            duplex_ms = (both_s + max(0.0, db - duplex["d2h_gbs"] * both_s) / link["d2h_gbs"]) * 1e3
         e2e = {"value": e_val, "unit": unit, "h2d_bytes_per_step": h2d_bytes,
                "d2h_bytes_per_step": d2h_bytes, "ms_per_step": e_ms, "steps": e2e_steps,
                "host_link": link, "link_bound_ms_per_step": bound_ms,
+               "link_bound_both_directions_ms_per_step": duplex_ms,
                "path": E2E_PATHS.get(args.workload, E2E_PATHS["default"])}
 
     allgather = None

@@ -152,6 +152,39 @@ def _gemm_desc(a_op, b_op, out, alpha, c_in, beta, bias, act, precision) -> Gemm
     return d
 
 
+# Input bytes per block of the host-tensor pipelines' default schedules (gemm's row blocks,
+# attention's batch blocks).
+_GEMM_BLOCK_BYTES = 64 << 20
+_ATTENTION_BLOCK_BYTES = 192 << 20
+
+
+def _block_bounds(total: int, unit_bytes: int, align: int, chunks: Optional[int],
+                  block_bytes: int = _GEMM_BLOCK_BYTES) -> list:
+    """Boundaries of the blocks a host-tensor pipeline streams `total` units (rows, or batch
+    entries) in. `chunks` given: that many equal blocks (multiples of `align` but the last).
+    Default: blocks of about `block_bytes` of input each, and the last two blocks' worth cut into
+    halves down to `align` units, because the last block's product and its copy back are the part
+    of the step no transfer overlaps. Measured on B200 through the host link: C2 (8192^3, 0.8 GB
+    in, 0.27 GB out) 32 equal blocks 16.4-16.5 ms per step, 16 equal blocks 16.3, eight 64 MB
+    blocks without the tapered end 16.6-16.9, seven and then 512 + 256 + 128 + 128 rows
+    15.9-16.3; C4 attention (1.5 GB in, 0.5 GB out) 16 equal blocks 32.0 ms, tapered blocks of
+    64 / 128 / 192 / 256 MB 32.2 / 31.4 / 31.2 / 31.2. Copies of 8 MB move at ~43 GB/s beside
+    the other direction, 32-64 MB ones at ~50."""
+    if chunks is not None:
+        n = max(1, min(chunks, total))
+        return sorted(set([round(i * total / n) // align * align for i in range(n)] + [total]))
+    block = max(align, (block_bytes // max(1, unit_bytes)) // align * align)
+    bounds, pos = [0], 0
+    while total - pos > 2 * block:
+        pos += block
+        bounds.append(pos)
+    while pos < total:
+        rest = total - pos
+        pos += rest if rest <= align else max(align, (rest // 2) // align * align)
+        bounds.append(pos)
+    return bounds
+
+
 def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activation, precision,
                     out, chunks):
     """Execution::GPU on host-resident tensors, as the reference's run_on does for data that lives
@@ -176,8 +209,12 @@ def _gemm_from_host(a, b, alpha, c, beta, transpose_a, transpose_b, bias, activa
     right_d = d_b.t() if transpose_b else d_b
     d_out = torch.empty((m, n), dtype=torch.float32, device=dev)
     # row blocks of op(A) are contiguous host slices only when A is not transposed
-    nchunks = 1 if transpose_a or m < 512 else max(1, min(chunks, m // 256))
-    bounds = [round(i * m / nchunks) // 128 * 128 for i in range(nchunks)] + [m]
+    if transpose_a or m < 512:
+        bounds = [0, m]
+    else:
+        bounds = _block_bounds(m, 4 * (k + (n if c is not None else 0)), 128,
+                               None if chunks is None else min(chunks, m // 256))
+    nchunks = len(bounds) - 1
     # In 3xTF32 every product splits op(B) first; with several row blocks it is split once, as
     # soon as it has arrived, and shared (bit-identical to splitting it for each block).
     split_b = None
@@ -242,7 +279,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, alpha: float = 1.0, c: Optional[torch
          beta: float = 0.0, transpose_a: bool = False, transpose_b: bool = False, *,
          bias: Optional[torch.Tensor] = None, activation: Optional[str] = None,
          precision: Optional[str] = None, out: Optional[torch.Tensor] = None,
-         execution: str = "auto", chunks: int = 32) -> torch.Tensor:
+         execution: str = "auto", chunks: Optional[int] = None) -> torch.Tensor:
     """alpha * op(a) @ op(b) + beta * c, as mensurflow::gemm (blas.hpp:59, blas.cpp:234-262),
     in ONE kernel; `bias` and `activation` fuse the following bias_add/relu/gelu.
 
@@ -796,8 +833,10 @@ def _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks, f
     copy_in.wait_stream(compute)
     with torch.cuda.stream(copy_in):
         d_mask = mask.to(dev, non_blocking=True) if mask is not None else None
-    nchunks = max(1, min(chunks, batch))
-    bounds = [round(i * batch / nchunks) for i in range(nchunks + 1)]
+    entry_bytes = 4 * (q3.shape[1] * q3.shape[2] + k3.shape[1] * k3.shape[2] +
+                       v3.shape[1] * v3.shape[2])
+    bounds = _block_bounds(batch, entry_bytes, 1, chunks, _ATTENTION_BLOCK_BYTES)
+    nchunks = len(bounds) - 1
     alive = []
     for i in range(nchunks):
         b0, b1 = bounds[i], bounds[i + 1]
@@ -859,7 +898,7 @@ def _fused_attention(q, k, v, causal, scale):
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
               mask: Optional[torch.Tensor] = None, causal: bool = False, scale: float = 0.0, *,
               precision: Optional[str] = None, execution: str = "auto",
-              out: Optional[torch.Tensor] = None, chunks: int = 16,
+              out: Optional[torch.Tensor] = None, chunks: Optional[int] = None,
               fused: Optional[bool] = None) -> torch.Tensor:
     """Scaled dot-product attention as mensurflow::attention (attention.hpp:21,
     src/ops/attention.cpp:48-98): scores = scale * q @ k^T (batched GEMM, scale in alpha), entries

@@ -196,3 +196,25 @@ def test_sharded_argument_checks_without_a_device():
     # gather="peer" needs the mapped buffer of C
     with pytest.raises(ValueError):
         sharded.sharded_gemm(torch.zeros(4, 3), torch.zeros(3, 2), 4, gather="peer")
+
+
+@pytest.mark.parametrize("total,unit_bytes,align", [(8192, 4 * 16384, 128), (4096, 4 * 1024, 128),
+                                                    (1000, 400, 128), (512, 3 << 20, 1), (5, 3 << 20, 1),
+                                                    (130, 1, 128), (1, 8, 1), (0, 8, 1)])
+def test_host_pipeline_block_schedule(total, unit_bytes, align):
+    """The default row-block schedule of the host-tensor pipelines: blocks of about 64 MB of
+    input, the last two blocks' worth halved down to `align` units; every unit in exactly one
+    block, every boundary but the last a multiple of `align`, block sizes never growing at the
+    end. An explicit block count gives that many equal blocks."""
+    b = ops._block_bounds(total, unit_bytes, align, None)
+    assert b[0] == 0 and b[-1] == total
+    sizes = np.diff(b)
+    assert (sizes > 0).all()
+    assert all(x % align == 0 for x in b[:-1])
+    assert all(s <= max(align, ops._GEMM_BLOCK_BYTES // unit_bytes) for s in sizes)
+    assert list(sizes[-3:]) == sorted(sizes[-3:], reverse=True)
+    if total >= 4 * align:
+        assert sizes[-1] <= align  # the tail is one aligned unit block
+    fixed = ops._block_bounds(total, unit_bytes, align, 4)
+    assert fixed[0] == 0 and fixed[-1] == total and (np.diff(fixed) > 0).all()
+    assert len(fixed) - 1 <= 4

@@ -111,7 +111,7 @@ def test_fused_mask_equals_where_then_softmax(cuda):
     assert mf.device_status() == 0
 
 
-@pytest.mark.parametrize("chunks", [1, 4, 16])
+@pytest.mark.parametrize("chunks", [1, 4, 16, None])
 def test_attention_on_host_tensors(cuda, chunks):
     """Execution::GPU on host-resident q, k, v: batch chunks stream through the device and the
     result comes back as a host tensor; it equals the attention of the same tensors on the device

@@ -402,11 +402,13 @@ def test_tf32_conversion_of_raw_fp32_operands(cuda):
     no_fault()
 
 
+@pytest.mark.parametrize("chunks", [4, None])
 @pytest.mark.parametrize("trans", [(False, True), (True, False)])
-def test_host_tensors_with_gpu_execution(cuda, trans):
+def test_host_tensors_with_gpu_execution(cuda, trans, chunks):
     """Host inputs with execution="gpu": copied to the device, computed, copied back (the
-    reference's run_on for data that lives elsewhere), pipelined by row blocks — the same values
-    as the device-resident call."""
+    reference's run_on for data that lives elsewhere), pipelined by row blocks (four equal ones,
+    or the default schedule: 640, 256, 128, 128, 128 and 20 rows here) — the same values as the
+    device-resident call."""
     ta, tb = trans
     m, n, k = 1300, 700, 900
     rng = np.random.default_rng(11)
@@ -415,7 +417,7 @@ def test_host_tensors_with_gpu_execution(cuda, trans):
     c = rng.standard_normal((m, n)).astype(np.float32)
     bias = rng.uniform(-0.1, 0.1, n).astype(np.float32)
     ha, hb, hc, hbias = (torch.from_numpy(x).pin_memory() for x in (a, b, c, bias))
-    got = mf.gemm(ha, hb, 0.5, hc, 1.0, ta, tb, bias=hbias, execution="gpu", chunks=4)
+    got = mf.gemm(ha, hb, 0.5, hc, 1.0, ta, tb, bias=hbias, execution="gpu", chunks=chunks)
     assert got.device.type == "cpu" and tuple(got.shape) == (m, n)
     want = host(mf.gemm(dev(a, cuda), dev(b, cuda), 0.5, dev(c, cuda), 1.0, ta, tb,
                         bias=dev(bias, cuda)))
