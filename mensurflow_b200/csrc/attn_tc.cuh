@@ -8,9 +8,9 @@
 // gemm_strided_batched for P V), which writes and re-reads the whole [L, L] score matrix of every
 // head. Softmax follows the reference's numerics where it matters (the row maximum is that of
 // fl(scale * QK), the row's exponentials are normalised by their sum;
-// src/backends/cpu/ops/softmax/softmax.cpp:11-80) but is evaluated online: running row maximum m and sum l per key tile, O rescaled when m grows
-// (only when it grows by more than 8, so the rescaling is rare and every exponential stays below
-// e^8), O / l at the end.
+// src/backends/cpu/ops/softmax/softmax.cpp:11-80) but is evaluated online: running row maximum m
+// and sum l per key tile, O rescaled when m grows (only when it grows by more than 8, so the
+// rescaling is rare and every exponential stays below e^8), O / l at the end.
 //
 // Design (sm_100a), one CTA pair (cta_group::2) per work unit = (head, block of 256 queries):
 //  * Q of the unit (each CTA its 128 rows) is loaded raw by TMA into shared memory and split in

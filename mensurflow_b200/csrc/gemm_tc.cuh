@@ -1186,8 +1186,10 @@ __device__ __forceinline__ void tc_epilogue(const GemmArgs& g, const CUtensorMap
             acc_phase ^= 1u;
         }
     }
-    // Stores must have finished reading shared memory (and landed) before the CTA exits.
+    // Stores must have finished reading shared memory (and landed) before the CTA exits, and so
+    // must C_in copies still in flight (a loop left early, after a wait gave up).
     if (g.tma_store && lane == 0) bulk_wait<0>();
+    if constexpr (CINA) cp_async_wait<0>();
     // Stores into a peer GPU's memory are performed at system scope before the kernel ends, so
     // whatever the other GPU orders after this kernel (an event wait, a collective) sees them.
     if (g.c_peer) __threadfence_system();

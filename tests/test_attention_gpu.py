@@ -189,6 +189,22 @@ def test_fused_attention_running_max_rescales(cuda):
     assert mf.device_status() == 0
 
 
+@pytest.mark.parametrize("scale", [-0.3, -1e-3, 2.0])
+def test_fused_attention_any_scale(cuda, scale):
+    """The reference takes any nonzero scale (src/ops/attention.cpp:64-69: scale is the scores
+    GEMM's alpha). The kernel finds each row's maximum of fl(scale * s) as fl(scale * max s),
+    or fl(scale * min s) for a negative scale, and folds the scale into the exponent: a negative,
+    a tiny and a large scale against the reference, at a length off the tile grid."""
+    q, k, v = _qkv(2, 300, 31)
+    for causal in (True, False):
+        got = mf.attention(dev(q, cuda), dev(k, cuda), dev(v, cuda), causal=causal, scale=scale,
+                           fused=True).cpu().numpy()
+        want = O.ref_attention(q, k, v, causal=causal, scale=scale)
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-6,
+                                   err_msg=f"scale={scale} causal={causal}")
+    assert mf.device_status() == 0
+
+
 def test_fused_attention_routing(cuda):
     """Eligible calls take the one kernel by default; a mask, a head dimension other than 128,
     shared k/v or 1xTF32 take the composed path, and fused=True refuses them."""
