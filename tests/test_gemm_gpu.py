@@ -508,6 +508,12 @@ def test_short_k_with_c_in(cuda, shape, precision):
     c_view = dev(np.ascontiguousarray(c[0].T), cuda).t()
     got_view = mf.gemm(ta[0], tb[0], 0.5, c_view, 1.0, bias=tbias, precision=precision)
     assert torch.equal(got_view, got), "C_in as a strided view differs"
+    # C_in one row broadcast down the rows (row stride 0): every lane copies the same row
+    c_row = tc[0][m // 2]
+    got_bc = mf.gemm(ta[0], tb[0], 0.5, c_row.expand(m, n), 1.0, bias=tbias, precision=precision)
+    got_full = mf.gemm(ta[0], tb[0], 0.5, c_row.expand(m, n).contiguous(), 1.0, bias=tbias,
+                       precision=precision)
+    assert torch.equal(got_bc, got_full), "C_in as a broadcast row differs"
     if batch > 1:
         out = mf.gemm_strided_batched(ta, tb, 0.5, tc, 1.0, precision=precision)
         for i in range(batch):
