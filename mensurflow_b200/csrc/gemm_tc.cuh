@@ -226,9 +226,16 @@ __device__ __forceinline__ float gelu_tanh_f32(float v) {
 }
 
 // Out-of-line copies for the epilogue's unrolled loops: one body in the instruction stream
-// instead of 32.
-__device__ __noinline__ float gelu_exact_f32_call(float v) { return gelu_exact_f32(v); }
-__device__ __noinline__ float gelu_tanh_f32_call(float v) { return gelu_tanh_f32(v); }
+// instead of 32. Four values per call: each evaluation is a long dependent chain, and four
+// independent ones interleave (the same arithmetic per value as the scalar form).
+__device__ __noinline__ float4 gelu_exact_f32_x4(float4 v) {
+    return make_float4(gelu_exact_f32(v.x), gelu_exact_f32(v.y), gelu_exact_f32(v.z),
+                       gelu_exact_f32(v.w));
+}
+__device__ __noinline__ float4 gelu_tanh_f32_x4(float4 v) {
+    return make_float4(gelu_tanh_f32(v.x), gelu_tanh_f32(v.y), gelu_tanh_f32(v.z),
+                       gelu_tanh_f32(v.w));
+}
 
 __device__ __forceinline__ float apply_act(float v, int act) {
     switch (act) {
@@ -909,10 +916,22 @@ __device__ __forceinline__ void epilogue_general(const GemmArgs& g, const EpiRow
         for (int j = 0; j < kEpiCols; ++j) v[j] = v[j] < 0.0f ? 0.0f : v[j];
     } else if (g.act == kActGelu) {
 #pragma unroll
-        for (int j = 0; j < kEpiCols; ++j) v[j] = gelu_exact_f32_call(v[j]);
+        for (int j = 0; j < kEpiCols; j += 4) {
+            const float4 r = gelu_exact_f32_x4(make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+            v[j] = r.x;
+            v[j + 1] = r.y;
+            v[j + 2] = r.z;
+            v[j + 3] = r.w;
+        }
     } else if (g.act == kActGeluTanh) {
 #pragma unroll
-        for (int j = 0; j < kEpiCols; ++j) v[j] = gelu_tanh_f32_call(v[j]);
+        for (int j = 0; j < kEpiCols; j += 4) {
+            const float4 r = gelu_tanh_f32_x4(make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+            v[j] = r.x;
+            v[j + 1] = r.y;
+            v[j + 2] = r.z;
+            v[j + 3] = r.w;
+        }
     }
 }
 
