@@ -16,10 +16,11 @@
 //  * Q of the unit (each CTA its 128 rows) is loaded raw by TMA into shared memory and split in
 //    place into tf32 (hi, lo) by two converter warps; it stays there for all of the unit's key
 //    tiles (the A operand of S = Q K^T);
-//  * K and V arrive pre-split into (hi, lo) panels (the GEMM path's packing passes: K as it is,
-//    V transposed so that keys are the contraction dimension), streamed through a ring of
-//    shared-memory stages by TMA, 32-wide chunks of the contraction per stage: four K chunks for
-//    S_j, four V chunks for the product with P_j;
+//  * K and V stream through a ring of shared-memory stages by TMA, 32-wide chunks of the
+//    contraction per stage: four K chunks for S_j, four V chunks for the product with P_j. K
+//    arrives raw and the converter warps split each stage in place; V arrives pre-split into
+//    (hi, lo) panels by the GEMM path's packing pass, transposed so that keys are the
+//    contraction dimension;
 //  * tensor memory (512 columns): O [0, 128), two S buffers [128, 256) and [256, 384), P lo
 //    [384, 512). The softmax warps overwrite S_j with P_j's hi part and write its lo part beside
 //    it; the MMA then reads P from tensor memory as its A operand;
@@ -55,7 +56,8 @@ constexpr int kAttnOffQLo = kAttnQBytes;
 constexpr int kAttnOffRing = 2 * kAttnQBytes;
 constexpr int kAttnOffSwap = kAttnOffRing + kAttnStages * kAttnStageBytes;
 constexpr int kAttnOffBars = kAttnOffSwap + 2 * 8 * 32 * 4;           // swap slots [2][8][32]
-constexpr int kAttnSmemBytes = 1024 + kAttnOffBars + 256;
+constexpr int kAttnBarBytes = 320;
+constexpr int kAttnSmemBytes = 1024 + kAttnOffBars + kAttnBarBytes;
 static_assert(kAttnSmemBytes <= 232448, "attention: shared memory per CTA exceeded");
 
 // tensor memory columns
@@ -77,7 +79,7 @@ struct AttnArgs {
     int causal;
     float scale;
     long long num_units;  // heads * num_qb
-    int q_raw_hi;         // the tensor cores truncate fp32 operands: raw Q serves as its hi part
+    int raw_hi;           // the tensor cores truncate fp32 operands: raw Q and K serve as hi
 };
 
 // Work unit u -> (head, query block): the longest units (last query blocks under the causal
@@ -94,22 +96,25 @@ __device__ __forceinline__ int attn_tiles(const AttnArgs& a, int qb) {
 }
 
 // ---- producer: Q per unit, then K_0, K_1, V_0, K_2, V_1, ..., V_J through the ring ----------
+// Each CTA loads its own half of a stage and counts the bytes on its own `landed` barrier: raw K
+// into the stage's hi part (the converters write lo beside it), V's pre-split (hi, lo) panels
+// into both parts.
 __device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorMap* tmQ,
-                                              const CUtensorMap* tmKh, const CUtensorMap* tmKl,
-                                              const CUtensorMap* tmVh, const CUtensorMap* tmVl,
-                                              uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                              const CUtensorMap* tmK, const CUtensorMap* tmVh,
+                                              const CUtensorMap* tmVl, uint8_t* smem,
+                                              uint64_t* landed, uint64_t* empty,
                                               uint64_t* q_full, uint64_t* q_free, uint32_t rank) {
     const uint64_t keep = l2_policy_evict_last();
     int stage = 0;
     uint32_t phase = 0;
     long long n = 0;  // units of this pair so far
+    // mh into the stage's hi part and, when given, ml into its lo part
     auto load_stage = [&](const CUtensorMap* mh, const CUtensorMap* ml, int x, int y, int z) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, kErrAttnProducer)) return false;
         uint8_t* s = smem + kAttnOffRing + stage * kAttnStageBytes;
-        if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * kAttnStageBytes);
-        const uint32_t bar = mapa_shared(&full[stage], 0);
-        tma_load_3d_cg2(s, mh, bar, x, y, z, keep);
-        tma_load_3d_cg2(s + kAttnHalfBytes, ml, bar, x, y, z, keep);
+        mbar_arrive_expect_tx(&landed[stage], ml != nullptr ? kAttnStageBytes : kAttnHalfBytes);
+        tma_load_3d(s, mh, &landed[stage], x, y, z, keep);
+        if (ml != nullptr) tma_load_3d(s + kAttnHalfBytes, ml, &landed[stage], x, y, z, keep);
         if (++stage == kAttnStages) {
             stage = 0;
             phase ^= 1u;
@@ -131,9 +136,9 @@ __device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorM
         }
         const int krow = static_cast<int>(rank) * (kAttnKeys / 2);
         for (int j = 0; j <= tiles; ++j) {
-            if (j < tiles) {  // K_j: 64 keys of the tile per CTA, four chunks of the head dim
+            if (j < tiles) {  // K_j (raw): 64 keys of the tile per CTA, four chunks of the head dim
                 for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc)
-                    if (!load_stage(tmKh, tmKl, kc * kAttnChunk, j * kAttnKeys + krow, head))
+                    if (!load_stage(tmK, nullptr, kc * kAttnChunk, j * kAttnKeys + krow, head))
                         return;
             }
             if (j >= 1) {  // V_{j-1} transposed: 64 head dims per CTA, four chunks of keys
@@ -145,55 +150,98 @@ __device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorM
     }
 }
 
-// ---- converters: Q raw -> (hi, lo) in shared memory, chunk by chunk --------------------------
-// Each 32-column chunk is released to the MMA issuer as soon as it is split, so the unit's first
-// S product starts after one chunk rather than all four. With q_raw_hi the raw values stay as
-// the hi part (the tensor cores truncate them to the same tf32 value) and only lo is written.
+// ---- converters: Q and K raw -> (hi, lo) in shared memory; every ring stage released -------
+// The two converter warps walk the ring in the producer's order. A K stage is split in place
+// (lo written beside the raw values, which are the hi part where the tensor cores truncate fp32;
+// else hi is rewritten too); a V stage, already split, is passed on. Either way both warps of
+// both CTAs arrive on the stage's `ready` barrier in the first CTA, which the MMA issuer waits
+// on. Q is split chunk by chunk, each chunk just before the stage of K_0 with the same head
+// dimensions, so a unit's first S product can start after one chunk of each.
+__device__ __forceinline__ void attn_split_vecs(float4* hi, float4* lo, int begin, int end,
+                                                int ct, bool raw_hi) {
+    if (raw_hi) {
+#pragma unroll 4
+        for (int i = begin + ct; i < end; i += 64) {
+            const float4 x = hi[i];
+            float4 h, l;  // h unused: the raw value is hi
+            split_tf32(x.x, h.x, l.x);
+            split_tf32(x.y, h.y, l.y);
+            split_tf32(x.z, h.z, l.z);
+            split_tf32(x.w, h.w, l.w);
+            lo[i] = l;
+        }
+    } else {
+#pragma unroll 4
+        for (int i = begin + ct; i < end; i += 64) {
+            const float4 x = hi[i];
+            float4 h, l;
+            split_tf32(x.x, h.x, l.x);
+            split_tf32(x.y, h.y, l.y);
+            split_tf32(x.z, h.z, l.z);
+            split_tf32(x.w, h.w, l.w);
+            hi[i] = h;
+            lo[i] = l;
+        }
+    }
+}
+
 __device__ __forceinline__ void attn_convert(const AttnArgs& a, uint8_t* smem, uint64_t* q_full,
-                                            uint64_t* q_ready) {
+                                            uint64_t* q_ready, uint64_t* landed,
+                                            uint64_t* ready) {
     const int ct = threadIdx.x - kAttnCvtWarp0 * 32;
     const int lane = threadIdx.x % 32;
-    float4* hi = reinterpret_cast<float4*>(smem);
-    float4* lo = reinterpret_cast<float4*>(smem + kAttnOffQLo);
+    const bool raw_hi = a.raw_hi != 0;
     constexpr int kChunkVecs = kAttnQChunkBytes / 16;
+    constexpr int kHalfVecs = kAttnHalfBytes / 16;
+    int stage = 0;
+    uint32_t phase = 0;
+    // the next ring stage: split it when it holds K, then release it to the MMA issuer
+    auto pass_stage = [&](bool split) {
+        if (!mbar_wait(&landed[stage], phase, kErrAttnConvert)) return false;
+        if (split) {
+            uint8_t* st = smem + kAttnOffRing + stage * kAttnStageBytes;
+            attn_split_vecs(reinterpret_cast<float4*>(st),
+                            reinterpret_cast<float4*>(st + kAttnHalfBytes), 0, kHalfVecs, ct,
+                            raw_hi);
+            fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&ready[stage], 0));
+        if (++stage == kAttnStages) {
+            stage = 0;
+            phase ^= 1u;
+        }
+        return true;
+    };
     long long n = 0;
     for (long long u = blockIdx.x / 2; u < a.num_units; u += gridDim.x / 2, ++n) {
+        int head, qb;
+        attn_unit(a, u, head, qb);
+        const int tiles = attn_tiles(a, qb);
         for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc) {
             if (!mbar_wait(&q_full[kc], static_cast<uint32_t>(n & 1), kErrAttnConvert)) return;
-            if (a.q_raw_hi) {
-#pragma unroll 4
-                for (int i = kc * kChunkVecs + ct; i < (kc + 1) * kChunkVecs; i += 64) {
-                    const float4 x = hi[i];
-                    float4 h, l;  // h unused: the raw value is hi
-                    split_tf32(x.x, h.x, l.x);
-                    split_tf32(x.y, h.y, l.y);
-                    split_tf32(x.z, h.z, l.z);
-                    split_tf32(x.w, h.w, l.w);
-                    lo[i] = l;
-                }
-            } else {
-#pragma unroll 4
-                for (int i = kc * kChunkVecs + ct; i < (kc + 1) * kChunkVecs; i += 64) {
-                    const float4 x = hi[i];
-                    float4 h, l;
-                    split_tf32(x.x, h.x, l.x);
-                    split_tf32(x.y, h.y, l.y);
-                    split_tf32(x.z, h.z, l.z);
-                    split_tf32(x.w, h.w, l.w);
-                    hi[i] = h;
-                    lo[i] = l;
-                }
-            }
+            attn_split_vecs(reinterpret_cast<float4*>(smem),
+                            reinterpret_cast<float4*>(smem + kAttnOffQLo), kc * kChunkVecs,
+                            (kc + 1) * kChunkVecs, ct, raw_hi);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(&q_ready[kc], 0));
+            if (!pass_stage(true)) return;  // K_0, the same head dimensions
+        }
+        for (int j = 1; j <= tiles; ++j) {
+            if (j < tiles) {
+                for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc)
+                    if (!pass_stage(true)) return;  // K_j
+            }
+            for (int kc = 0; kc < kAttnKeys / kAttnChunk; ++kc)
+                if (!pass_stage(false)) return;  // V_{j-1}
         }
     }
 }
 
 // ---- MMA issuer (one thread of the pair's first CTA) -----------------------------------------
 __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8_t* smem,
-                                         uint64_t* full, uint64_t* empty, uint64_t* q_ready,
+                                         uint64_t* ready, uint64_t* empty, uint64_t* q_ready,
                                          uint64_t* q_free, uint64_t* s_full, uint64_t* p_full,
                                          uint64_t* pv_done) {
     constexpr uint32_t idesc = idesc_tf32(kAttnUnitRows, 128, false, false);
@@ -217,7 +265,7 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
         const uint32_t d = tmem + kAttnColS + static_cast<uint32_t>((tt & 1) * 128);
         for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc) {
             if (first && !mbar_wait(&q_ready[kc], qphase, kErrAttnMma)) return false;
-            if (!mbar_wait(&full[stage], phase, kErrAttnMma)) return false;
+            if (!mbar_wait(&ready[stage], phase, kErrAttnMma)) return false;
             tc_fence_after();
             const uint32_t bh = ring + stage * kAttnStageBytes;
             const uint32_t bl = bh + kAttnHalfBytes;
@@ -249,7 +297,7 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
         const uint32_t ph = tmem + kAttnColS + static_cast<uint32_t>((tt & 1) * 128);
         const uint32_t pl = tmem + kAttnColPLo;
         for (int kc = 0; kc < kAttnKeys / kAttnChunk; ++kc) {
-            if (!mbar_wait(&full[stage], phase, kErrAttnMma)) return false;
+            if (!mbar_wait(&ready[stage], phase, kErrAttnMma)) return false;
             tc_fence_after();
             const uint32_t bh = ring + stage * kAttnStageBytes;
             const uint32_t bl = bh + kAttnHalfBytes;
@@ -478,16 +526,16 @@ __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
-                   const __grid_constant__ CUtensorMap tmKh,
-                   const __grid_constant__ CUtensorMap tmKl,
+                   const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmVh,
                    const __grid_constant__ CUtensorMap tmVl, float* out, const AttnArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAttnOffBars);
-    uint64_t* full = bars;
-    uint64_t* empty = full + kAttnStages;
+    uint64_t* landed = bars;                  // [stages]: this CTA's half of the stage arrived
+    uint64_t* ready = landed + kAttnStages;   // [stages]: both halves split, for the MMA issuer
+    uint64_t* empty = ready + kAttnStages;
     uint64_t* q_full = empty + kAttnStages;  // [4]: per 32-column chunk of Q
     uint64_t* q_ready = q_full + 4;          // [4]
     uint64_t* q_free = q_ready + 4;
@@ -498,14 +546,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t* x_bar = drain + 1;     // [4]: the two warps of a lane quarter
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(x_bar + 4);
     float* xch = reinterpret_cast<float*>(smem + kAttnOffSwap);
-    static_assert((2 * kAttnStages + 20) * 8 + 4 <= 256, "attention: barrier area too small");
+    static_assert((3 * kAttnStages + 20) * 8 + 4 <= kAttnBarBytes,
+                  "attention: barrier area too small");
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const uint32_t rank = cluster_ctarank();
     if (threadIdx.x == 0) {
         for (int s = 0; s < kAttnStages; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&landed[s], 1);
+            mbar_init(&ready[s], 2 * 2);  // both converter warps of both CTAs
             mbar_init(&empty[s], 1);
         }
         for (int c = 0; c < 4; ++c) {
@@ -524,8 +574,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmKh);
-        tma_prefetch_desc(&tmKl);
+        tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmVh);
         tma_prefetch_desc(&tmVl);
     }
@@ -538,18 +587,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
     if (warp == 0) {
         if (lane == 0)
-            attn_producer(a, &tmQ, &tmKh, &tmKl, &tmVh, &tmVl, smem, full, empty, q_full, q_free,
-                          rank);
+            attn_producer(a, &tmQ, &tmK, &tmVh, &tmVl, smem, landed, empty, q_full, q_free, rank);
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            attn_mma(a, tmem, smem, full, empty, q_ready, q_free, s_full, p_full, pv_done);
+            attn_mma(a, tmem, smem, ready, empty, q_ready, q_free, s_full, p_full, pv_done);
             // every MMA issued must finish before tensor memory is released
             mma_commit_cg2(drain);
             mbar_wait(drain, 0, kErrAttnMma);
         }
         __syncwarp();
     } else if (warp < kAttnSoftWarp0) {
-        attn_convert(a, smem, q_full, q_ready);
+        attn_convert(a, smem, q_full, q_ready, landed, ready);
     } else {
         attn_softmax(a, out, tmem, s_full, p_full, pv_done, x_bar, xch, rank);
     }

@@ -1198,14 +1198,13 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
     const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     const int64_t d = head_dim;
     const int64_t kp_v = (len + mfk::kBK - 1) / mfk::kBK * mfk::kBK;
-    // K split as it lies ([head][key][d], d the contraction of S = Q K^T); V split transposed
-    // ([head][d][key], keys the contraction of O = P V), both into (hi, lo) panels. Where the
-    // tensor cores are known to truncate fp32 operands to tf32, K itself serves as its hi part
-    // (the split's hi is the truncation, bit for bit) and only K's lo is written.
-    const bool k_raw_hi = tf32_truncates(info, stream, true);
-    const size_t k_elems = static_cast<size_t>(heads) * len * d;
+    // Q and K are read as they lie and split inside the kernel (where the tensor cores are known
+    // to truncate fp32 operands to tf32 the raw values serve as the hi parts, bit for bit, and
+    // only lo is computed); V is split transposed ([head][d][key], keys the contraction of
+    // O = P V) into (hi, lo) panels by a packing pass.
+    const bool raw_hi = tf32_truncates(info, stream, true);
     const size_t v_elems = static_cast<size_t>(heads) * d * kp_v;
-    const size_t bytes = sizeof(float) * ((k_raw_hi ? 1 : 2) * k_elems + 2 * v_elems);
+    const size_t bytes = sizeof(float) * 2 * v_elems;
     uint8_t* ws = nullptr;
     MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream));
     struct Free {
@@ -1213,25 +1212,16 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
         cudaStream_t s;
         ~Free() { cudaFreeAsync(p, s); }
     } release{ws, stream};
-    Operand K{k, d, 1, len, BatchLayout{}};
-    K.bl.stride = len * d;
-    K.hi = reinterpret_cast<float*>(ws);
-    K.lo = k_raw_hi ? K.hi : K.hi + k_elems;  // raw K as hi: only lo has a panel
     Operand V{v, 1, d, d, BatchLayout{}};  // row = head dim, depth = key
     V.bl.stride = len * d;
-    V.hi = K.lo + k_elems;  // after K's panels
+    V.hi = reinterpret_cast<float*>(ws);
     V.lo = V.hi + v_elems;
-    if ((rc = launch_pack(K, d, d, heads, k_raw_hi ? mfk::kPackLo : mfk::kPackSplit, info,
-                          stream)) != MFK_OK)
-        return rc;
     if ((rc = launch_pack(V, len, kp_v, heads, mfk::kPackSplit, info, stream)) != MFK_OK)
         return rc;
-    CUtensorMap mq, mkh, mkl, mvh, mvl;
+    CUtensorMap mq, mk, mvh, mvl;
     const bool maps =
         make_kmajor_map(&mq, q, d, len, heads, d, len * d, mfk::kAttnRows) &&
-        make_kmajor_map(&mkh, k_raw_hi ? k : K.hi, d, len, heads, d, len * d,
-                        mfk::kAttnKeys / 2) &&
-        make_kmajor_map(&mkl, K.lo, d, len, heads, d, len * d, mfk::kAttnKeys / 2) &&
+        make_kmajor_map(&mk, k, d, len, heads, d, len * d, mfk::kAttnKeys / 2) &&
         make_kmajor_map(&mvh, V.hi, kp_v, d, heads, kp_v, d * kp_v, mfk::kAttnD / 2) &&
         make_kmajor_map(&mvl, V.lo, kp_v, d, heads, kp_v, d * kp_v, mfk::kAttnD / 2);
     if (!maps) {
@@ -1245,7 +1235,7 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
     a.causal = causal != 0 ? 1 : 0;
     a.scale = scale;
     a.num_units = static_cast<long long>(a.heads) * a.num_qb;
-    a.q_raw_hi = k_raw_hi ? 1 : 0;
+    a.raw_hi = raw_hi ? 1 : 0;
     auto kernel = mfk::attn_tc_kernel;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -1279,7 +1269,7 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
     cfg.gridDim = dim3(static_cast<unsigned>(pairs * 2), 1, 1);
     {
         TimedLaunch timed(stream);
-        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mkh, mkl, mvh, mvl, out, a));
+        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mk, mvh, mvl, out, a));
     }
     g_launches.fetch_add(1);
     return MFK_OK;

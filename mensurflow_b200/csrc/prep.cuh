@@ -16,7 +16,6 @@ enum PackMode : int {
     kPackCopy = 0,   // hi = x
     kPackRound = 1,  // hi = round_tf32(x)
     kPackSplit = 2,  // split_tf32: hi = x truncated to tf32, lo = tf32(x - hi)
-    kPackLo = 3,     // the split's lo only (hi is x itself where the tensor cores truncate)
 };
 
 // op(X) of matrix b: element (r, p) at x[off(b) + r*rs + p*cs], with off(b) = offsets[b] when
@@ -63,10 +62,6 @@ __global__ void __launch_bounds__(256) pack_kmajor_kernel(
                 hi[o] = v;
             } else if (mode == kPackRound) {
                 hi[o] = round_tf32(v);
-            } else if (mode == kPackLo) {
-                float h, l;
-                split_tf32(v, h, l);
-                lo[o] = l;
             } else {
                 float h, l;
                 split_tf32(v, h, l);
@@ -89,13 +84,6 @@ __device__ __forceinline__ void pack_store4(float* hi, float* lo, long long i, f
         *h4 = v;
     } else if (mode == kPackRound) {
         *h4 = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
-    } else if (mode == kPackLo) {
-        float4 h, l;
-        split_tf32(v.x, h.x, l.x);
-        split_tf32(v.y, h.y, l.y);
-        split_tf32(v.z, h.z, l.z);
-        split_tf32(v.w, h.w, l.w);
-        reinterpret_cast<float4*>(lo)[i] = l;
     } else {
         float4 h, l;
         split_tf32(v.x, h.x, l.x);
