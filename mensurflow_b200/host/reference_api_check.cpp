@@ -150,11 +150,12 @@ void check_attention(Device gpu) {
             const Tensor got = attention(q3.to(gpu), k3.to(gpu), v3.to(gpu), nullptr, causal, 0.0f,
                                          Execution::GPU);
             const std::int64_t ran = mfk_launch_count() - launches;
-            // the K and V packing passes and the attention kernel; the composed path would run
-            // two batched GEMMs with their packing passes, where and softmax
-            if (ran != 3) {
+            // V's packing pass and the attention kernel (Q and K are split inside it); the
+            // composed path would run two batched GEMMs with their packing passes, where and
+            // softmax
+            if (ran != 2) {
                 throw std::runtime_error("attention with head dim 128 ran " + std::to_string(ran) +
-                                         " kernels, not the fused path's 3");
+                                         " kernels, not the fused path's 2");
             }
             require_close(got, attention(q3, k3, v3, nullptr, causal, 0.0f, Execution::CPU), 1e-4,
                           1e-6, causal ? "attention in one kernel, causal 2x4x384x128"
