@@ -48,7 +48,11 @@ typedef enum mfk_activation {
 
 /* Tensor-core arithmetic for the fp32 GEMMs. 3xTF32 splits each operand into tf32 hi + lo and
  * accumulates three products in fp32 (fp32-faithful: |C - C_ref| <= 1e-5 * (|A||B|)_ij + 1e-6);
- * 1xTF32 is one tf32 product per term (<= 2e-3 * (|A||B|)_ij). */
+ * 1xTF32 is one tf32 product per term (<= 2e-3 * (|A||B|)_ij). The split's hi part is x with its
+ * 13 low mantissa bits cleared; where a one-time check finds that the tensor cores truncate fp32
+ * operands to tf32, operands split inside a kernel keep their raw values as hi (only lo is
+ * written). The environment variable MFK_EXPLICIT_SPLIT (set, and not "0") makes every split
+ * write hi explicitly, as on tensor cores that round; the results are the same bits. */
 typedef enum mfk_precision {
     MFK_PRECISION_DEFAULT = -1, /* the process-wide setting (mfk_set_default_precision) */
     MFK_PRECISION_3XTF32 = 0,

@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -424,9 +425,13 @@ int run_gemm(const mfk_gemm_desc* d, const mfk_batch_desc* bd, cudaStream_t stre
 // once per device, on a private stream, only where allocating is allowed and the caller's
 // stream is not being captured; any failure leaves the explicit (always valid) split in use.
 bool tf32_truncates(DeviceInfo* info, cudaStream_t caller, bool may_allocate) {
-#ifdef MFK_FORCE_EXPLICIT_SPLIT
-    return false;  // build option: always split hi explicitly
-#endif
+    // MFK_EXPLICIT_SPLIT set (and not "0"): always write the split's hi part explicitly, as on
+    // tensor cores that round, so that path can be checked on hardware that truncates.
+    static const bool explicit_split = [] {
+        const char* e = std::getenv("MFK_EXPLICIT_SPLIT");
+        return e != nullptr && e[0] != '\0' && !(e[0] == '0' && e[1] == '\0');
+    }();
+    if (explicit_split) return false;
     const int known = info->tf32_truncates.load();
     if (known >= 0) return known == 1;
     if (!may_allocate) return false;
