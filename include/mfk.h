@@ -259,6 +259,16 @@ int mfk_softmax_f32(const float* x, float* out, int64_t outer, int64_t length, i
 int mfk_attention_f32(const float* q, const float* k, const float* v, float* out, int64_t heads,
                       int64_t len, int64_t head_dim, int32_t causal, float scale, void* stream);
 
+/* The same with a Bool keep mask, as the reference's attention(q, k, v, &mask, causal, scale):
+ * key j may be seen by query i of matrix b when keep[b*keep_bs + i*keep_rs + j*keep_cs] != 0
+ * (device bytes, strides in bytes, 0 broadcasts; a [len, len] mask shared by every matrix has
+ * keep_bs = 0), together with the causal limit when causal != 0. A query whose keys are all
+ * masked out gets zeros, as the reference's softmax gives them. */
+int mfk_attention_masked_f32(const float* q, const float* k, const float* v, const uint8_t* keep,
+                             int64_t keep_bs, int64_t keep_rs, int64_t keep_cs, float* out,
+                             int64_t heads, int64_t len, int64_t head_dim, int32_t causal,
+                             float scale, void* stream);
+
 /* The softmax between attention's GEMMs with its masking fused in: for a contiguous
  * [batch, rows, cols] score tensor, entry (b, i, j) counts as -inf unless (keep == NULL or
  * keep[b*keep_bs + i*keep_rs + j] != 0) and (causal == 0 or j <= i); then softmax along cols.

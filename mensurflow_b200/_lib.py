@@ -48,6 +48,7 @@ EXPORTED = (
     "mfk_bias_grad_f32",
     "mfk_softmax_f32",
     "mfk_attention_f32",
+    "mfk_attention_masked_f32",
     "mfk_masked_softmax_f32",
     "mfk_where_f32",
     "mfk_strided_copy_f32",
@@ -146,6 +147,8 @@ def lib() -> ctypes.CDLL:
             so.mfk_softmax_f32.argtypes = [vp, vp, i64, i64, i64, i32, vp]
             so.mfk_masked_softmax_f32.argtypes = [vp, vp, i64, i64, i32, vp, i64, i64, i64, vp]
             so.mfk_attention_f32.argtypes = [vp, vp, vp, vp, i64, i64, i64, i32, f32, vp]
+            so.mfk_attention_masked_f32.argtypes = [vp, vp, vp, vp, i64, i64, i64, vp, i64, i64,
+                                                    i64, i32, f32, vp]
             so.mfk_where_f32.argtypes = [vp, vp, vp, vp, i64, vp]
             so.mfk_strided_copy_f32.argtypes = [vp, ctypes.POINTER(i64), ctypes.POINTER(i64),
                                                 i32, vp, vp]

@@ -80,7 +80,20 @@ struct AttnArgs {
     float scale;
     long long num_units;  // heads * num_qb
     int raw_hi;           // the tensor cores truncate fp32 operands: raw Q and K serve as hi
+    // MASK kernels: key k may be seen by query q of matrix b where keep[b*keep_bs + q*keep_rs +
+    // k*keep_cs] != 0 (strides in bytes; 0 broadcasts), as the reference's where(mask, s, -inf)
+    const uint8_t* keep;
+    long long keep_bs, keep_rs, keep_cs;
 };
+
+// The keep bits of 64 keys from 16-byte loads: bit i set where byte i is nonzero.
+__device__ __forceinline__ uint32_t attn_keep_bits16(uint4 x) {
+    auto nib = [](uint32_t w) {
+        const uint32_t m = __vcmpne4(w, 0u) & 0x01010101u;  // one bit per byte, at bit 8 i
+        return (m | (m >> 7) | (m >> 14) | (m >> 21)) & 0xFu;
+    };
+    return nib(x.x) | (nib(x.y) << 4) | (nib(x.z) << 8) | (nib(x.w) << 12);
+}
 
 // Work unit u -> (head, query block): the longest units (last query blocks under the causal
 // mask) first, so the persistent pairs finish together.
@@ -360,11 +373,15 @@ struct AttnSwap {
     }
 };
 
+// MASK: `kbits` has bit i set where key own0 + i of the tile is valid (in range, under the
+// causal limit, kept by the mask); otherwise the first `nvalid` keys of the tile are valid.
+template <bool MASK>
 __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_t sb,
-                                                      uint32_t pl, int h, int nvalid, float& m,
-                                                      double& l, bool rescale_allowed,
-                                                      uint32_t olanes, uint64_t* pv_done,
-                                                      long long t, int j, AttnSwap& sw) {
+                                                      uint32_t pl, int h, int nvalid,
+                                                      uint64_t kbits, float& m, double& l,
+                                                      bool rescale_allowed, uint32_t olanes,
+                                                      uint64_t* pv_done, long long t, int j,
+                                                      AttnSwap& sw) {
     const float ninf = __int_as_float(0xff800000);
     const int own0 = h * 64;
     // pass 1: the maximum of fl(scale * s) over this half's valid keys, the raw scores kept in
@@ -376,7 +393,11 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
     tmem_ld_issue_32x32b_x32(sb + own0 + 32, sr[1]);
     tmem_ld_wait();
     const float* s = reinterpret_cast<const float*>(&sr[0][0]);
-    const bool full = __all_sync(0xffffffffu, nvalid >= own0 + 64);  // no masked key in this half
+    // no masked key in this half
+    const bool full = __all_sync(0xffffffffu, MASK ? kbits == ~0ull : nvalid >= own0 + 64);
+    auto valid = [&](int i) {
+        return MASK ? ((kbits >> i) & 1ull) != 0ull : own0 + i < nvalid;
+    };
     const bool neg = a.scale < 0.0f;
     const float pinf = __int_as_float(0x7f800000);
     float ext[4];
@@ -388,16 +409,16 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
     } else if (!neg) {
 #pragma unroll
         for (int i = 0; i < 64; ++i)
-            if (own0 + i < nvalid) ext[i & 3] = fmaxf(ext[i & 3], s[i]);
+            if (valid(i)) ext[i & 3] = fmaxf(ext[i & 3], s[i]);
     } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i)
-            if (own0 + i < nvalid) ext[i & 3] = fminf(ext[i & 3], s[i]);
+            if (valid(i)) ext[i & 3] = fminf(ext[i & 3], s[i]);
     }
     const float e01 = neg ? fminf(ext[0], ext[1]) : fmaxf(ext[0], ext[1]);
     const float e23 = neg ? fminf(ext[2], ext[3]) : fmaxf(ext[2], ext[3]);
     const float ex = neg ? fminf(e01, e23) : fmaxf(e01, e23);
-    float mt = own0 < nvalid ? __fmul_rn(a.scale, ex) : ninf;
+    float mt = (MASK ? kbits != 0ull : own0 < nvalid) ? __fmul_rn(a.scale, ex) : ninf;
     float mo;
     if (!sw.swap(mt, mo)) return false;
     mt = fmaxf(mt, mo);
@@ -438,7 +459,7 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const float e = exp2f(fmaf(s[c + i], sl, -ml));
-            const float p = (full || own0 + c + i < nvalid) ? e : 0.0f;
+            const float p = (full || valid(c + i)) ? e : 0.0f;
             lt[i & 3] += p;
             const uint32_t hi = __float_as_uint(p) & 0xFFFFE000u;
             lo[i] = tf32_round_bits(__float_as_uint(p - __uint_as_float(hi)));
@@ -451,6 +472,7 @@ __device__ __forceinline__ bool attn_softmax_row_half(const AttnArgs& a, uint32_
     return true;
 }
 
+template <bool MASK>
 __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint32_t tmem,
                                              uint64_t* s_full, uint64_t* p_full,
                                              uint64_t* pv_done, uint64_t* x_bar, float* xch,
@@ -478,13 +500,38 @@ __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint
         for (int j = 0; j < tiles; ++j, ++t) {
             const uint32_t sb = lanes + kAttnColS + static_cast<uint32_t>((t & 1) * 128);
             const int nvalid = max(0, min(kAttnKeys, kend - j * kAttnKeys));
+            // MASK: this row's keep bits for the half's 64 keys in range, loaded before the
+            // scores are waited for
+            uint64_t kbits = 0ull;
+            if constexpr (MASK) {
+                const int key0 = j * kAttnKeys + h * 64;
+                const int nk = max(0, min(64, kend - key0));
+                if (row < a.len && nk > 0) {
+                    const uint8_t* mrow = a.keep + static_cast<long long>(head) * a.keep_bs +
+                                          static_cast<long long>(row) * a.keep_rs +
+                                          static_cast<long long>(key0) * a.keep_cs;
+                    if (nk == 64 && a.keep_cs == 1 &&
+                        (reinterpret_cast<uintptr_t>(mrow) & 15u) == 0u) {
+                        const uint4* p4 = reinterpret_cast<const uint4*>(mrow);
+#pragma unroll
+                        for (int w = 0; w < 4; ++w)
+                            kbits |= static_cast<uint64_t>(attn_keep_bits16(__ldg(p4 + w)))
+                                     << (16 * w);
+                    } else {
+                        for (int i = 0; i < nk; ++i)
+                            kbits |= static_cast<uint64_t>(
+                                         __ldg(mrow + static_cast<long long>(i) * a.keep_cs) != 0)
+                                     << i;
+                    }
+                }
+            }
             if (!mbar_wait(&s_full[t & 1], static_cast<uint32_t>((t >> 1) & 1), kErrAttnSoftmax)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            if (!attn_softmax_row_half(a, sb, lanes + kAttnColPLo, h, nvalid, m, l, j >= 1,
-                                       lanes + kAttnColO, pv_done, t, j, sw)) {
+            if (!attn_softmax_row_half<MASK>(a, sb, lanes + kAttnColPLo, h, nvalid, kbits, m, l,
+                                             j >= 1, lanes + kAttnColO, pv_done, t, j, sw)) {
                 ok = false;
                 break;
             }
@@ -501,7 +548,8 @@ __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint
         // epilogue: O / l once the last product has finished
         if (!mbar_wait(pv_done, static_cast<uint32_t>((t - 1) & 1), kErrAttnSoftmax)) break;
         tc_fence_after();
-        const float inv = static_cast<float>(1.0 / l);
+        // a row whose every key is masked out: zeros, as the reference's softmax gives
+        const float inv = (MASK && l == 0.0) ? 0.0f : static_cast<float>(1.0 / l);
         float* orow = out + (static_cast<long long>(head) * a.len + row) * kAttnD + h * 64;
 #pragma unroll
         for (int c = 0; c < 64; c += 32) {
@@ -524,6 +572,7 @@ __device__ __forceinline__ void attn_softmax(const AttnArgs& a, float* out, uint
     }
 }
 
+template <bool MASK>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmK,
@@ -599,7 +648,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (warp < kAttnSoftWarp0) {
         attn_convert(a, smem, q_full, q_ready, landed, ready);
     } else {
-        attn_softmax(a, out, tmem, s_full, p_full, pv_done, x_bar, xch, rank);
+        attn_softmax<MASK>(a, out, tmem, s_full, p_full, pv_done, x_bar, xch, rank);
     }
 
     tc_fence_before();

@@ -1185,10 +1185,18 @@ int mfk_softmax_f32(const float* x, float* out, int64_t outer, int64_t length, i
                           static_cast<cudaStream_t>(stream));
 }
 
-int mfk_attention_f32(const float* q, const float* k, const float* v, float* out, int64_t heads,
-                      int64_t len, int64_t head_dim, int32_t causal, float scale,
-                      void* stream_) {
+}  // extern "C"
+
+namespace {
+
+// The fused attention for both entry points: keep == nullptr runs the kernel without a mask.
+template <bool MASK>
+int run_attention(const float* q, const float* k, const float* v, const uint8_t* keep,
+                  int64_t keep_bs, int64_t keep_rs, int64_t keep_cs, float* out, int64_t heads,
+                  int64_t len, int64_t head_dim, int32_t causal, float scale, void* stream_) {
     if (heads < 0 || len < 0 || head_dim < 0) return MFK_ERR_INVALID_ARGUMENT;
+    if (MASK && (keep == nullptr || keep_bs < 0 || keep_rs < 0 || keep_cs < 0))
+        return MFK_ERR_INVALID_ARGUMENT;
     if (heads == 0 || len == 0) return MFK_OK;
     if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
         return MFK_ERR_INVALID_ARGUMENT;
@@ -1241,7 +1249,11 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
     a.scale = scale;
     a.num_units = static_cast<long long>(a.heads) * a.num_qb;
     a.raw_hi = raw_hi ? 1 : 0;
-    auto kernel = mfk::attn_tc_kernel;
+    a.keep = keep;
+    a.keep_bs = keep_bs;
+    a.keep_rs = keep_rs;
+    a.keep_cs = keep_cs;
+    auto kernel = mfk::attn_tc_kernel<MASK>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.blockDim = dim3(mfk::kAttnThreads, 1, 1);
@@ -1253,7 +1265,7 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    constexpr int kSlot = 15;  // this kernel's per-device set-up flags
+    constexpr int kSlot = MASK ? 14 : 15;  // this kernel's per-device set-up flags
     {
         std::lock_guard<std::mutex> lock(g_mutex);
         if (!info->smem_set[kSlot]) {
@@ -1278,6 +1290,24 @@ int mfk_attention_f32(const float* q, const float* k, const float* v, float* out
     }
     g_launches.fetch_add(1);
     return MFK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mfk_attention_f32(const float* q, const float* k, const float* v, float* out, int64_t heads,
+                      int64_t len, int64_t head_dim, int32_t causal, float scale, void* stream) {
+    return run_attention<false>(q, k, v, nullptr, 0, 0, 0, out, heads, len, head_dim, causal,
+                                scale, stream);
+}
+
+int mfk_attention_masked_f32(const float* q, const float* k, const float* v, const uint8_t* keep,
+                             int64_t keep_bs, int64_t keep_rs, int64_t keep_cs, float* out,
+                             int64_t heads, int64_t len, int64_t head_dim, int32_t causal,
+                             float scale, void* stream) {
+    return run_attention<true>(q, k, v, keep, keep_bs, keep_rs, keep_cs, out, heads, len,
+                               head_dim, causal, scale, stream);
 }
 
 int mfk_masked_softmax_f32(const float* scores, const uint8_t* keep, int64_t keep_bs,

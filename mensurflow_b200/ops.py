@@ -866,10 +866,34 @@ def _attention_from_host(q, k, v, mask, causal, scale, precision, out, chunks, f
 FUSED_ATTENTION_HEAD_DIM = 128
 
 
+def _mask_broadcasts(mask, scores_shape) -> bool:
+    try:
+        return tuple(torch.broadcast_shapes(tuple(mask.shape), tuple(scores_shape))) == \
+            tuple(scores_shape)
+    except RuntimeError:
+        return False
+
+
+def _keep_matrices(mask, scores_shape):
+    """The Bool mask broadcast to the scores [..., Lq, Lk] as matrices [batch, Lq, Lk] with unit
+    column stride: (tensor, batch stride in bytes (0 when one matrix serves all), row stride)."""
+    queries, keys = scores_shape[-2], scores_shape[-1]
+    batch = int(np.prod(scores_shape[:-2])) if len(scores_shape) > 2 else 1
+    keep = mask.expand(scores_shape)
+    flat = keep.reshape(batch, queries, keys) if keep.dim() > 2 else keep.reshape(1, queries, keys)
+    if flat.stride(-1) != 1:
+        flat = flat.contiguous()
+    return flat, (flat.stride(0) if flat.shape[0] > 1 else 0), flat.stride(1)
+
+
 def _fused_attention_eligible(q, k, v, mask, precision) -> bool:
-    """The one-kernel path (mfk_attention_f32): no mask tensor, q, k and v of one shape
-    [..., L, 128] on a CUDA device, 3xTF32."""
-    if mask is not None or q.device.type != "cuda" or q.dim() < 2:
+    """The one-kernel path (mfk_attention_f32, or mfk_attention_masked_f32 with a Bool mask that
+    broadcasts to the scores): q, k and v of one shape [..., L, 128] on a CUDA device, 3xTF32."""
+    if q.device.type != "cuda" or q.dim() < 2:
+        return False
+    if mask is not None and (not isinstance(mask, torch.Tensor) or mask.dtype != torch.bool or
+                             mask.device != q.device or
+                             not _mask_broadcasts(mask, tuple(q.shape[:-1]) + (q.shape[-2],))):
         return False
     if tuple(q.shape) != tuple(k.shape) or tuple(q.shape) != tuple(v.shape):
         return False
@@ -881,7 +905,7 @@ def _fused_attention_eligible(q, k, v, mask, precision) -> bool:
     return code == _lib.PRECISION_3XTF32
 
 
-def _fused_attention(q, k, v, causal, scale):
+def _fused_attention(q, k, v, causal, scale, mask=None):
     _kernel_for("attention", q)
     qq, kk, vv = (contiguous(t) for t in (q, k, v))
     if any(t.data_ptr() % 16 for t in (qq, kk, vv)):
@@ -889,9 +913,19 @@ def _fused_attention(q, k, v, causal, scale):
     out = torch.empty(tuple(q.shape), dtype=torch.float32, device=q.device)
     length, depth = q.shape[-2], q.shape[-1]
     heads = q.numel() // (length * depth)
-    check(_lib.lib().mfk_attention_f32(qq.data_ptr(), kk.data_ptr(), vv.data_ptr(),
-                                       out.data_ptr(), heads, length, depth,
-                                       1 if causal else 0, float(scale), _stream()), "attention")
+    if mask is None:
+        check(_lib.lib().mfk_attention_f32(qq.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+                                           out.data_ptr(), heads, length, depth,
+                                           1 if causal else 0, float(scale), _stream()),
+              "attention")
+    else:
+        keep, keep_bs, keep_rs = _keep_matrices(mask, tuple(q.shape[:-1]) + (length,))
+        check(_lib.lib().mfk_attention_masked_f32(qq.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+                                                  keep.data_ptr(), keep_bs, keep_rs, 1,
+                                                  out.data_ptr(), heads, length, depth,
+                                                  1 if causal else 0, float(scale), _stream()),
+              "attention")
+        keep.record_stream(torch.cuda.current_stream(q.device))
     return out
 
 
@@ -946,10 +980,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         scale = float(np.float32(1.0 / np.sqrt(depth))) if depth > 0 else 1.0
     eligible = _fused_attention_eligible(q, k, v, mask, precision)
     if fused and not eligible:
-        raise ValueError("attention: the fused kernel needs no mask tensor, q, k and v of one "
-                         "shape [..., L, 128] on a CUDA device, and 3xTF32")
+        raise ValueError("attention: the fused kernel needs q, k and v of one shape [..., L, 128] "
+                         "on a CUDA device, 3xTF32, and a mask (if any) that is a Bool tensor on "
+                         "their device broadcasting to the scores")
     if eligible and fused is not False:
-        return _fused_attention(q, k, v, causal, scale)
+        return _fused_attention(q, k, v, causal, scale, mask)
     scores = gemm_strided_batched(q, k, scale, None, 0.0, False, True, precision=precision)
     keep = None
     if mask is not None:
@@ -957,26 +992,16 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
             raise ValueError("attention: mask must be a defined Bool tensor")
         if mask.device != q.device:
             raise ValueError("attention: mask must be on the inputs' device")
-        try:
-            ok = tuple(torch.broadcast_shapes(tuple(mask.shape), tuple(scores.shape))) == \
-                tuple(scores.shape)
-        except RuntimeError:
-            ok = False
-        if not ok:
+        if not _mask_broadcasts(mask, scores.shape):
             raise ValueError(f"attention: mask {tuple(mask.shape)} does not broadcast to the "
                              f"scores {tuple(scores.shape)}")
-        keep = mask.expand(scores.shape)
     if scores.numel() == 0:
         return gemm_strided_batched(scores, v, precision=precision)
     batch = scores.numel() // (queries * keys)
     keep_ptr, keep_bs, keep_rs = None, 0, 0
-    if keep is not None:
-        flat = keep.reshape(batch, queries, keys) if keep.dim() > 2 else keep.reshape(1, queries, keys)
-        if flat.stride(-1) != 1:
-            flat = flat.contiguous()
-        bs = flat.stride(0) if flat.shape[0] > 1 else 0
-        keep_ptr, keep_bs, keep_rs = flat.data_ptr(), bs, flat.stride(1)
-        keep = flat  # keep alive
+    if mask is not None:
+        keep, keep_bs, keep_rs = _keep_matrices(mask, tuple(scores.shape))  # kept alive here
+        keep_ptr = keep.data_ptr()
     check(_lib.lib().mfk_masked_softmax_f32(scores.data_ptr(), keep_ptr, keep_bs, keep_rs,
                                             1 if causal else 0, scores.data_ptr(), batch, queries,
                                             keys, _stream()), "attention")

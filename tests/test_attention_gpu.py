@@ -189,6 +189,34 @@ def test_fused_attention_running_max_rescales(cuda):
     assert mf.device_status() == 0
 
 
+@pytest.mark.parametrize("heads,length,causal,kind", [
+    (2, 300, False, "shared"), (2, 300, True, "shared"), (3, 256, False, "per_head"),
+    (2, 77, True, "empty_rows"), (1, 640, False, "empty_rows"), (2, 128, True, "per_head"),
+    (2, 512, False, "columns")])
+def test_fused_attention_with_mask(cuda, heads, length, causal, kind):
+    """The one kernel with a Bool keep mask (mfk_attention_masked_f32) against the reference's
+    attention(q, k, v, &mask, causal) and the composed path: a mask shared by every head, one per
+    head, rows whose every key is masked out (zeros, as the reference's softmax gives them), and
+    whole key columns masked; causal and not, at lengths off the tile grid."""
+    q, k, v = _qkv(heads, length, 7 * heads + length)
+    rng = np.random.default_rng(length + heads)
+    if kind == "per_head":
+        mask = rng.random((heads, length, length)) > 0.5
+    else:
+        mask = rng.random((length, length)) > 0.3
+    if kind == "empty_rows":
+        mask[[0, length // 2, length - 1], :] = False
+    if kind == "columns":
+        mask[:, 100:300] = False
+    tq, tk, tv, tm = dev(q, cuda), dev(k, cuda), dev(v, cuda), dev(mask, cuda)
+    got = mf.attention(tq, tk, tv, tm, causal=causal, fused=True).cpu().numpy()
+    want = O.ref_attention(q, k, v, mask, causal=causal)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-6)
+    composed = mf.attention(tq, tk, tv, tm, causal=causal, fused=False).cpu().numpy()
+    np.testing.assert_allclose(got, composed, rtol=1e-4, atol=1e-6)
+    assert mf.device_status() == 0
+
+
 @pytest.mark.parametrize("scale", [-0.3, -1e-3, 2.0])
 def test_fused_attention_any_scale(cuda, scale):
     """The reference takes any nonzero scale (src/ops/attention.cpp:64-69: scale is the scores
@@ -206,22 +234,28 @@ def test_fused_attention_any_scale(cuda, scale):
 
 
 def test_fused_attention_routing(cuda):
-    """Eligible calls take the one kernel by default; a mask, a head dimension other than 128,
+    """Eligible calls take the one kernel by default, a Bool mask that broadcasts to the scores
+    included (mfk_attention_masked_f32); a mask on the host, a head dimension other than 128,
     shared k/v or 1xTF32 take the composed path, and fused=True refuses them."""
     q, k, v = _qkv(2, 128, 3)
     tq, tk, tv = dev(q, cuda), dev(k, cuda), dev(v, cuda)
     np.testing.assert_array_equal(mf.attention(tq, tk, tv, causal=True).cpu().numpy(),
                                   mf.attention(tq, tk, tv, causal=True, fused=True).cpu().numpy())
     mask = torch.ones(128, 128, dtype=torch.bool, device=cuda)
+    np.testing.assert_array_equal(
+        mf.attention(tq, tk, tv, mask=mask, causal=True).cpu().numpy(),
+        mf.attention(tq, tk, tv, mask=mask, causal=True, fused=True).cpu().numpy())
     with pytest.raises(ValueError):
-        mf.attention(tq, tk, tv, mask=mask, fused=True)
+        mf.attention(tq, tk, tv, mask=mask.cpu(), fused=True)
     with pytest.raises(ValueError):
         mf.attention(tq[..., :64], tk[..., :64], tv[..., :64], fused=True)
     with pytest.raises(ValueError):
         mf.attention(tq, tk[:1], tv[:1], fused=True)
     with pytest.raises(ValueError):
         mf.attention(tq, tk, tv, precision="1xtf32", fused=True)
-    # the composed path still serves them
-    got = mf.attention(tq, tk, tv, mask=mask, causal=True).cpu().numpy()
+    # the composed path still serves them, and an all-true mask changes nothing
+    got = mf.attention(tq, tk, tv, mask=mask, causal=True, fused=False).cpu().numpy()
     np.testing.assert_allclose(got, O.ref_attention(q, k, v, causal=True), rtol=1e-4, atol=1e-6)
+    fused = mf.attention(tq, tk, tv, mask=mask, causal=True).cpu().numpy()
+    np.testing.assert_allclose(fused, O.ref_attention(q, k, v, causal=True), rtol=1e-4, atol=1e-6)
     assert mf.device_status() == 0
