@@ -280,6 +280,21 @@ void attention_kernel(const OpArgs& args, Stream& stream) {
     const Tensor& out = args.outputs[0];
     const std::int64_t len = q.size(-2), depth = q.size(-1);
     const std::int64_t heads = len * depth > 0 ? q.numel() / (len * depth) : 0;
+    if (args.inputs.size() > 3) {
+        // the Bool keep mask, expanded to the scores [..., len, len] by the op with one stride
+        // over the batch dimensions (the innermost one's; 0 when all are broadcast)
+        const Tensor& keep = args.inputs[3];
+        const Strides& st = keep.strides();
+        const std::size_t nb = st.size() - 2;
+        check_mfk(mfk_attention_masked_f32(
+                      TensorAccess::data<float>(q), TensorAccess::data<float>(args.inputs[1]),
+                      TensorAccess::data<float>(args.inputs[2]),
+                      TensorAccess::data<std::uint8_t>(keep), nb > 0 ? st[nb - 1] : 0, st[nb],
+                      st[nb + 1], TensorAccess::data<float>(out), heads, len, depth,
+                      args.causal ? 1 : 0, args.alpha, s.raw()),
+                  "attention");
+        return;
+    }
     check_mfk(mfk_attention_f32(TensorAccess::data<float>(q),
                                 TensorAccess::data<float>(args.inputs[1]),
                                 TensorAccess::data<float>(args.inputs[2]),

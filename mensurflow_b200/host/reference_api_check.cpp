@@ -161,6 +161,29 @@ void check_attention(Device gpu) {
                           1e-6, causal ? "attention in one kernel, causal 2x4x384x128"
                                        : "attention in one kernel 2x4x384x128");
         }
+        // with a Bool mask shared by every head (one query masked out entirely, so its row is
+        // zeros): the one kernel's masked form, in the same two launches
+        std::vector<std::uint8_t> keep3(static_cast<std::size_t>(384 * 384));
+        for (std::int64_t i = 0; i < 384; ++i) {
+            for (std::int64_t j = 0; j < 384; ++j) {
+                keep3[static_cast<std::size_t>(i * 384 + j)] = i != 5 && (i * 7 + j) % 5 != 0;
+            }
+        }
+        const Tensor mask3 = Tensor::from_host(keep3.data(), {384, 384}, DType::Bool);
+        const Tensor mask3_g = mask3.to(gpu);
+        for (bool causal : {true, false}) {
+            const std::int64_t launches = mfk_launch_count();
+            const Tensor got = attention(q3.to(gpu), k3.to(gpu), v3.to(gpu), &mask3_g, causal,
+                                         0.0f, Execution::GPU);
+            const std::int64_t ran = mfk_launch_count() - launches;
+            if (ran != 2) {
+                throw std::runtime_error("attention with a mask and head dim 128 ran " +
+                                         std::to_string(ran) + " kernels, not the fused path's 2");
+            }
+            require_close(got, attention(q3, k3, v3, &mask3, causal, 0.0f, Execution::CPU), 1e-4,
+                          1e-6, causal ? "attention in one kernel with a mask, causal 2x4x384x128"
+                                       : "attention in one kernel with a mask 2x4x384x128");
+        }
     }
     const Tensor q2 = input({4, 256, 64}, 31, 0.125f), k2 = input({4, 256, 64}, 32, 0.125f),
                  v2 = input({4, 256, 64}, 33, 0.125f);

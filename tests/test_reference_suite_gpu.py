@@ -61,5 +61,6 @@ def test_reference_program_passes_on_b200(cuda, name):
                      "bias_add bias gradient on the device (bit-exact)",
                      "matmul dB on the device",
                      "Tensor::contiguous() of a CUDA view: stepped slices",
-                     "attention in one kernel, causal 2x4x384x128"):
+                     "attention in one kernel, causal 2x4x384x128",
+                     "attention in one kernel with a mask, causal 2x4x384x128"):
             assert line in out, (line, out[-3000:])
