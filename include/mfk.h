@@ -253,9 +253,8 @@ int mfk_softmax_f32(const float* x, float* out, int64_t outer, int64_t length, i
  * online (running row maximum and sum, the output rescaled as the maximum grows), so the result
  * agrees with the composed path within the reference's attention tolerance (1e-4 relative), not
  * bit for bit. Non-finite inputs are not supported (results are unspecified); callers that may
- * hold them use the composed path. Q and K are read as they lie and split into tf32 (hi, lo)
- * inside the kernel; V is first split into transposed (hi, lo) panels in a workspace from the
- * stream-ordered allocator: 8 x heads x ceil(len / 32) x 32 x 128 bytes. */
+ * hold them use the composed path. Q, K and V are read as they lie and split into tf32 (hi, lo)
+ * inside the kernel: one launch, no workspace, nothing allocated. */
 int mfk_attention_f32(const float* q, const float* k, const float* v, float* out, int64_t heads,
                       int64_t len, int64_t head_dim, int32_t causal, float scale, void* stream);
 

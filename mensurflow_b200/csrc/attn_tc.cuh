@@ -17,10 +17,11 @@
 //    place into tf32 (hi, lo) by two converter warps; it stays there for all of the unit's key
 //    tiles (the A operand of S = Q K^T);
 //  * K and V stream through a ring of shared-memory stages by TMA, 32-wide chunks of the
-//    contraction per stage: four K chunks for S_j, four V chunks for the product with P_j. K
-//    arrives raw and the converter warps split each stage in place; V arrives pre-split into
-//    (hi, lo) panels by the GEMM path's packing pass, transposed so that keys are the
-//    contraction dimension;
+//    contraction per stage: four K chunks (32 head dimensions of 64 keys per CTA) for S_j, four
+//    V chunks (32 keys of 64 head dimensions per CTA) for the product with P_j. Both arrive raw,
+//    as they lie in memory, and the converter warps split each stage in place. K is read
+//    K-major; V, whose rows are keys (the contraction of O = P V), is read MN-major in the
+//    128-byte swizzle on 32-byte atoms, so no pass transposes or splits it beforehand;
 //  * tensor memory (512 columns): O [0, 128), two S buffers [128, 256) and [256, 384), P lo
 //    [384, 512). The softmax warps overwrite S_j with P_j's hi part and write its lo part beside
 //    it; the MMA then reads P from tensor memory as its A operand;
@@ -42,7 +43,7 @@ constexpr int kAttnUnitRows = 256; // query rows per CTA pair
 constexpr int kAttnKeys = 128;     // keys per key tile
 constexpr int kAttnChunk = 32;     // contraction per ring stage (one 128-byte swizzle row)
 constexpr int kAttnStages = 5;
-constexpr int kAttnThreads = 384;  // warp 0 TMA, 1 MMA, 2-3 split Q, 4-11 softmax + epilogue
+constexpr int kAttnThreads = 384;  // warp 0 TMA, 1 MMA, 2-3 split Q K V, 4-11 softmax + epilogue
 constexpr int kAttnCvtWarp0 = 2;
 constexpr int kAttnSoftWarp0 = 4;
 constexpr float kAttnRescaleAbove = 8.0f;  // raise the running max only past m + 8
@@ -52,6 +53,12 @@ constexpr int kAttnQChunkBytes = kAttnRows * kAttnChunk * 4;            // 16 KB
 constexpr int kAttnQBytes = kAttnQChunkBytes * (kAttnD / kAttnChunk);   // 64 KB (hi or lo)
 constexpr int kAttnHalfBytes = (kAttnKeys / 2) * kAttnChunk * 4;        // 8 KB: 64 rows
 constexpr int kAttnStageBytes = 2 * kAttnHalfBytes;                     // hi | lo
+// A V stage's half: two MN-major blocks of 32 keys x 32 head dimensions (128-byte rows, one per
+// key); the MMA reads them with the blocks kAttnVBlockBytes apart along the head dimension and
+// the 4-key swizzle atoms 512 bytes apart along the keys.
+constexpr int kAttnVBlockBytes = kAttnChunk * 32 * 4;                  // 4 KB
+constexpr int kAttnVAtomBytes = 4 * 128;
+static_assert(2 * kAttnVBlockBytes == kAttnHalfBytes, "attention: V stage layout");
 constexpr int kAttnOffQLo = kAttnQBytes;
 constexpr int kAttnOffRing = 2 * kAttnQBytes;
 constexpr int kAttnOffSwap = kAttnOffRing + kAttnStages * kAttnStageBytes;
@@ -109,25 +116,24 @@ __device__ __forceinline__ int attn_tiles(const AttnArgs& a, int qb) {
 }
 
 // ---- producer: Q per unit, then K_0, K_1, V_0, K_2, V_1, ..., V_J through the ring ----------
-// Each CTA loads its own half of a stage and counts the bytes on its own `landed` barrier: raw K
-// into the stage's hi part (the converters write lo beside it), V's pre-split (hi, lo) panels
-// into both parts.
+// Each CTA loads its own half of a stage, raw, into the stage's hi part (the converters write lo
+// beside it) and counts the bytes on its own `landed` barrier: a K stage in one box of 64 keys x
+// 32 head dimensions, a V stage in two boxes of 32 keys x 32 head dimensions.
 __device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorMap* tmQ,
-                                              const CUtensorMap* tmK, const CUtensorMap* tmVh,
-                                              const CUtensorMap* tmVl, uint8_t* smem,
-                                              uint64_t* landed, uint64_t* empty,
+                                              const CUtensorMap* tmK, const CUtensorMap* tmV,
+                                              uint8_t* smem, uint64_t* landed, uint64_t* empty,
                                               uint64_t* q_full, uint64_t* q_free, uint32_t rank) {
     const uint64_t keep = l2_policy_evict_last();
     int stage = 0;
     uint32_t phase = 0;
     long long n = 0;  // units of this pair so far
-    // mh into the stage's hi part and, when given, ml into its lo part
-    auto load_stage = [&](const CUtensorMap* mh, const CUtensorMap* ml, int x, int y, int z) {
+    // one box of m at (x, y, z), or two (x and x + 32) for a V stage
+    auto load_stage = [&](const CUtensorMap* m, bool v, int x, int y, int z) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, kErrAttnProducer)) return false;
         uint8_t* s = smem + kAttnOffRing + stage * kAttnStageBytes;
-        mbar_arrive_expect_tx(&landed[stage], ml != nullptr ? kAttnStageBytes : kAttnHalfBytes);
-        tma_load_3d(s, mh, &landed[stage], x, y, z, keep);
-        if (ml != nullptr) tma_load_3d(s + kAttnHalfBytes, ml, &landed[stage], x, y, z, keep);
+        mbar_arrive_expect_tx(&landed[stage], kAttnHalfBytes);
+        tma_load_3d(s, m, &landed[stage], x, y, z, keep);
+        if (v) tma_load_3d(s + kAttnVBlockBytes, m, &landed[stage], x + 32, y, z, keep);
         if (++stage == kAttnStages) {
             stage = 0;
             phase ^= 1u;
@@ -147,28 +153,29 @@ __device__ __forceinline__ void attn_producer(const AttnArgs& a, const CUtensorM
             tma_load_3d(smem + kc * kAttnQChunkBytes, tmQ, &q_full[kc], kc * kAttnChunk, qrow,
                         head, keep);
         }
-        const int krow = static_cast<int>(rank) * (kAttnKeys / 2);
+        const int krow = static_cast<int>(rank) * (kAttnKeys / 2);  // this CTA's keys of K_j
+        const int vcol = static_cast<int>(rank) * (kAttnD / 2);     // its head dims of V_j
         for (int j = 0; j <= tiles; ++j) {
             if (j < tiles) {  // K_j (raw): 64 keys of the tile per CTA, four chunks of the head dim
                 for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc)
-                    if (!load_stage(tmK, nullptr, kc * kAttnChunk, j * kAttnKeys + krow, head))
+                    if (!load_stage(tmK, false, kc * kAttnChunk, j * kAttnKeys + krow, head))
                         return;
             }
-            if (j >= 1) {  // V_{j-1} transposed: 64 head dims per CTA, four chunks of keys
+            if (j >= 1) {  // V_{j-1}: 64 head dims per CTA, four chunks of keys
                 for (int kc = 0; kc < kAttnKeys / kAttnChunk; ++kc)
-                    if (!load_stage(tmVh, tmVl, (j - 1) * kAttnKeys + kc * kAttnChunk, krow, head))
+                    if (!load_stage(tmV, true, vcol, (j - 1) * kAttnKeys + kc * kAttnChunk, head))
                         return;
             }
         }
     }
 }
 
-// ---- converters: Q and K raw -> (hi, lo) in shared memory; every ring stage released -------
-// The two converter warps walk the ring in the producer's order. A K stage is split in place
-// (lo written beside the raw values, which are the hi part where the tensor cores truncate fp32;
-// else hi is rewritten too); a V stage, already split, is passed on. Either way both warps of
-// both CTAs arrive on the stage's `ready` barrier in the first CTA, which the MMA issuer waits
-// on. Q is split chunk by chunk, each chunk just before the stage of K_0 with the same head
+// ---- converters: Q, K and V raw -> (hi, lo) in shared memory, stage by stage --------------
+// The two converter warps walk the ring in the producer's order. Every stage is split in place,
+// element by element in whatever layout it landed in (lo written beside the raw values, at the
+// same offset in the stage's lo half, so it shares their swizzle; the raw values are the hi
+// part where the tensor cores truncate fp32, else hi is rewritten too); then both warps of both
+// CTAs arrive on the stage's `ready` barrier in the first CTA, which the MMA issuer waits on. Q is split chunk by chunk, each chunk just before the stage of K_0 with the same head
 // dimensions, so a unit's first S product can start after one chunk of each.
 __device__ __forceinline__ void attn_split_vecs(float4* hi, float4* lo, int begin, int end,
                                                 int ct, bool raw_hi) {
@@ -208,16 +215,13 @@ __device__ __forceinline__ void attn_convert(const AttnArgs& a, uint8_t* smem, u
     constexpr int kHalfVecs = kAttnHalfBytes / 16;
     int stage = 0;
     uint32_t phase = 0;
-    // the next ring stage: split it when it holds K, then release it to the MMA issuer
-    auto pass_stage = [&](bool split) {
+    // the next ring stage: split it, then release it to the MMA issuer
+    auto pass_stage = [&]() {
         if (!mbar_wait(&landed[stage], phase, kErrAttnConvert)) return false;
-        if (split) {
-            uint8_t* st = smem + kAttnOffRing + stage * kAttnStageBytes;
-            attn_split_vecs(reinterpret_cast<float4*>(st),
-                            reinterpret_cast<float4*>(st + kAttnHalfBytes), 0, kHalfVecs, ct,
-                            raw_hi);
-            fence_proxy_async_smem();
-        }
+        uint8_t* st = smem + kAttnOffRing + stage * kAttnStageBytes;
+        attn_split_vecs(reinterpret_cast<float4*>(st),
+                        reinterpret_cast<float4*>(st + kAttnHalfBytes), 0, kHalfVecs, ct, raw_hi);
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(&ready[stage], 0));
         if (++stage == kAttnStages) {
@@ -239,15 +243,15 @@ __device__ __forceinline__ void attn_convert(const AttnArgs& a, uint8_t* smem, u
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(&q_ready[kc], 0));
-            if (!pass_stage(true)) return;  // K_0, the same head dimensions
+            if (!pass_stage()) return;  // K_0, the same head dimensions
         }
         for (int j = 1; j <= tiles; ++j) {
             if (j < tiles) {
                 for (int kc = 0; kc < kAttnD / kAttnChunk; ++kc)
-                    if (!pass_stage(true)) return;  // K_j
+                    if (!pass_stage()) return;  // K_j
             }
             for (int kc = 0; kc < kAttnKeys / kAttnChunk; ++kc)
-                if (!pass_stage(false)) return;  // V_{j-1}
+                if (!pass_stage()) return;  // V_{j-1}
         }
     }
 }
@@ -258,6 +262,7 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
                                          uint64_t* q_free, uint64_t* s_full, uint64_t* p_full,
                                          uint64_t* pv_done) {
     constexpr uint32_t idesc = idesc_tf32(kAttnUnitRows, 128, false, false);
+    constexpr uint32_t idesc_pv = idesc_tf32(kAttnUnitRows, 128, false, true);  // V MN-major
     constexpr uint16_t kPair = 3;
     const uint32_t q_hi = smem_u32(smem);
     const uint32_t q_lo = q_hi + kAttnOffQLo;
@@ -302,7 +307,8 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
         mma_commit_cg2_mc(&s_full[tt & 1], kPair);
         return true;
     };
-    // O (+)= P_t V_j: P (hi in S buffer t & 1, lo in the P lo columns) from tensor memory
+    // O (+)= P_t V_j: P (hi in S buffer t & 1, lo in the P lo columns) from tensor memory, V
+    // from the stage's MN-major blocks (8 keys per MMA = two 4-key swizzle atoms)
     auto pv_product = [&](long long tt, bool first) {
         if (!mbar_wait(&p_full[tt & 1], static_cast<uint32_t>((tt >> 1) & 1), kErrAttnMma))
             return false;
@@ -316,14 +322,16 @@ __device__ __forceinline__ void attn_mma(const AttnArgs& a, uint32_t tmem, uint8
             const uint32_t bl = bh + kAttnHalfBytes;
 #pragma unroll
             for (int ks = 0; ks < kAttnChunk / 8; ++ks) {
-                const uint32_t koff = ks * 32;
+                const uint32_t koff = ks * 2 * kAttnVAtomBytes;
                 const uint32_t col = static_cast<uint32_t>(kc * kAttnChunk + ks * 8);
-                const uint64_t dbh = smem_desc(bh + koff, 16, 1024, kSwizzle128B);
-                const uint64_t dbl = smem_desc(bl + koff, 16, 1024, kSwizzle128B);
+                const uint64_t dbh = smem_desc(bh + koff, kAttnVBlockBytes, kAttnVAtomBytes,
+                                               kSwizzle128BBase32B);
+                const uint64_t dbl = smem_desc(bl + koff, kAttnVBlockBytes, kAttnVAtomBytes,
+                                               kSwizzle128BBase32B);
                 const uint32_t acc = (!first || kc > 0 || ks > 0) ? 1u : 0u;
-                mma_tf32_ts_cg2(tmem + kAttnColO, pl + col, dbh, idesc, acc);
-                mma_tf32_ts_cg2(tmem + kAttnColO, ph + col, dbl, idesc, 1u);
-                mma_tf32_ts_cg2(tmem + kAttnColO, ph + col, dbh, idesc, 1u);
+                mma_tf32_ts_cg2(tmem + kAttnColO, pl + col, dbh, idesc_pv, acc);
+                mma_tf32_ts_cg2(tmem + kAttnColO, ph + col, dbl, idesc_pv, 1u);
+                mma_tf32_ts_cg2(tmem + kAttnColO, ph + col, dbh, idesc_pv, 1u);
             }
             mma_commit_cg2_mc(&empty[stage], kPair);
             next_stage();
@@ -577,8 +585,7 @@ template <bool MASK>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmVh,
-                   const __grid_constant__ CUtensorMap tmVl, float* out, const AttnArgs a) {
+                   const __grid_constant__ CUtensorMap tmV, float* out, const AttnArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -625,8 +632,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmVh);
-        tma_prefetch_desc(&tmVl);
+        tma_prefetch_desc(&tmV);
     }
     if (warp == 1) tmem_alloc_cg2(tmem_holder, 512);
     tc_fence_before();
@@ -637,7 +643,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
     if (warp == 0) {
         if (lane == 0)
-            attn_producer(a, &tmQ, &tmK, &tmVh, &tmVl, smem, landed, empty, q_full, q_free, rank);
+            attn_producer(a, &tmQ, &tmK, &tmV, smem, landed, empty, q_full, q_free, rank);
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
             attn_mma(a, tmem, smem, ready, empty, q_ready, q_free, s_full, p_full, pv_done);

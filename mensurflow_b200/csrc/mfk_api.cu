@@ -167,7 +167,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // A K-major operand view for TMA: `rows` rows of `depth` fp32 values, row r of matrix z at
 // base + z*bstride + r*rstride (elements). Box: 32 values (128 B, SWIZZLE_128B) x box_rows.
 bool make_kmajor_map(CUtensorMap* map, const float* base, int64_t depth, int64_t rows,
-                     int64_t nmat, int64_t rstride, int64_t bstride, int box_rows) {
+                     int64_t nmat, int64_t rstride, int64_t bstride, int box_rows,
+                     CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto fn = encode_fn();
     if (fn == nullptr) return false;
     if (nmat == 1) bstride = rstride * std::max<int64_t>(rows, 1);
@@ -179,7 +180,7 @@ bool make_kmajor_map(CUtensorMap* map, const float* base, int64_t depth, int64_t
     cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
                           const_cast<float*>(base), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -1210,33 +1211,17 @@ int run_attention(const float* q, const float* k, const float* v, const uint8_t*
     if (rc != MFK_OK) return rc;
     const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     const int64_t d = head_dim;
-    const int64_t kp_v = (len + mfk::kBK - 1) / mfk::kBK * mfk::kBK;
-    // Q and K are read as they lie and split inside the kernel (where the tensor cores are known
-    // to truncate fp32 operands to tf32 the raw values serve as the hi parts, bit for bit, and
-    // only lo is computed); V is split transposed ([head][d][key], keys the contraction of
-    // O = P V) into (hi, lo) panels by a packing pass.
+    // Q, K and V are read as they lie and split inside the kernel (where the tensor cores are
+    // known to truncate fp32 operands to tf32 the raw values serve as the hi parts, bit for bit,
+    // and only lo is computed): no pass before the kernel and no workspace. V's boxes use the
+    // 128-byte swizzle on 32-byte atoms, the layout the kernel reads it MN-major in.
     const bool raw_hi = tf32_truncates(info, stream, true);
-    const size_t v_elems = static_cast<size_t>(heads) * d * kp_v;
-    const size_t bytes = sizeof(float) * 2 * v_elems;
-    uint8_t* ws = nullptr;
-    MFK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream));
-    struct Free {
-        uint8_t* p;
-        cudaStream_t s;
-        ~Free() { cudaFreeAsync(p, s); }
-    } release{ws, stream};
-    Operand V{v, 1, d, d, BatchLayout{}};  // row = head dim, depth = key
-    V.bl.stride = len * d;
-    V.hi = reinterpret_cast<float*>(ws);
-    V.lo = V.hi + v_elems;
-    if ((rc = launch_pack(V, len, kp_v, heads, mfk::kPackSplit, info, stream)) != MFK_OK)
-        return rc;
-    CUtensorMap mq, mk, mvh, mvl;
+    CUtensorMap mq, mk, mv;
     const bool maps =
         make_kmajor_map(&mq, q, d, len, heads, d, len * d, mfk::kAttnRows) &&
         make_kmajor_map(&mk, k, d, len, heads, d, len * d, mfk::kAttnKeys / 2) &&
-        make_kmajor_map(&mvh, V.hi, kp_v, d, heads, kp_v, d * kp_v, mfk::kAttnD / 2) &&
-        make_kmajor_map(&mvl, V.lo, kp_v, d, heads, kp_v, d * kp_v, mfk::kAttnD / 2);
+        make_kmajor_map(&mv, v, d, len, heads, d, len * d, mfk::kAttnChunk,
+                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (!maps) {
         t_cuda_error = "cuTensorMapEncodeTiled rejected an attention operand";
         return MFK_ERR_UNSUPPORTED;
@@ -1286,7 +1271,7 @@ int run_attention(const float* q, const float* k, const float* v, const uint8_t*
     cfg.gridDim = dim3(static_cast<unsigned>(pairs * 2), 1, 1);
     {
         TimedLaunch timed(stream);
-        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mk, mvh, mvl, out, a));
+        MFK_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, out, a));
     }
     g_launches.fetch_add(1);
     return MFK_OK;

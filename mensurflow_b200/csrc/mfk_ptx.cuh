@@ -244,10 +244,19 @@ __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Shared-memory descriptor layout types (bits 61-63). kSwizzle128BBase32B is the 128-byte
+// swizzle on 32-byte atoms (32-byte chunk index XOR row mod 4, period 512 bytes), the layout an
+// MN-major tf32 operand is read in.
+enum : uint32_t {
+    kSwizzleNone = 0,
+    kSwizzle128BBase32B = 1,
+    kSwizzle128B = 2,
+    kSwizzle64B = 4,
+    kSwizzle32B = 6
+};
+
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): start address, leading and
 // stride byte offsets (all >> 4), version 1 at bits 46-47, swizzle mode at bits 61-63.
-enum : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
-
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
                                               uint32_t sbo_bytes, uint32_t swizzle) {
     uint64_t d = 0;

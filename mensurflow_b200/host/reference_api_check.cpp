@@ -150,19 +150,18 @@ void check_attention(Device gpu) {
             const Tensor got = attention(q3.to(gpu), k3.to(gpu), v3.to(gpu), nullptr, causal, 0.0f,
                                          Execution::GPU);
             const std::int64_t ran = mfk_launch_count() - launches;
-            // V's packing pass and the attention kernel (Q and K are split inside it); the
-            // composed path would run two batched GEMMs with their packing passes, where and
-            // softmax
-            if (ran != 2) {
+            // the attention kernel alone (Q, K and V are split inside it); the composed path
+            // would run two batched GEMMs with their packing passes, where and softmax
+            if (ran != 1) {
                 throw std::runtime_error("attention with head dim 128 ran " + std::to_string(ran) +
-                                         " kernels, not the fused path's 2");
+                                         " kernels, not the fused path's 1");
             }
             require_close(got, attention(q3, k3, v3, nullptr, causal, 0.0f, Execution::CPU), 1e-4,
                           1e-6, causal ? "attention in one kernel, causal 2x4x384x128"
                                        : "attention in one kernel 2x4x384x128");
         }
         // with a Bool mask shared by every head (one query masked out entirely, so its row is
-        // zeros): the one kernel's masked form, in the same two launches
+        // zeros): the one kernel's masked form, in one launch as well
         std::vector<std::uint8_t> keep3(static_cast<std::size_t>(384 * 384));
         for (std::int64_t i = 0; i < 384; ++i) {
             for (std::int64_t j = 0; j < 384; ++j) {
@@ -176,9 +175,9 @@ void check_attention(Device gpu) {
             const Tensor got = attention(q3.to(gpu), k3.to(gpu), v3.to(gpu), &mask3_g, causal,
                                          0.0f, Execution::GPU);
             const std::int64_t ran = mfk_launch_count() - launches;
-            if (ran != 2) {
+            if (ran != 1) {
                 throw std::runtime_error("attention with a mask and head dim 128 ran " +
-                                         std::to_string(ran) + " kernels, not the fused path's 2");
+                                         std::to_string(ran) + " kernels, not the fused path's 1");
             }
             require_close(got, attention(q3, k3, v3, &mask3, causal, 0.0f, Execution::CPU), 1e-4,
                           1e-6, causal ? "attention in one kernel with a mask, causal 2x4x384x128"
