@@ -2,7 +2,7 @@
 kernels that split an operand themselves keep its raw values as the hi part; MFK_EXPLICIT_SPLIT
 makes them write hi explicitly, as they must on tensor cores that round. Both must give the same
 bits: the GEMM's A split in shared and in tensor memory, the short-K GEMM, and the fused
-attention's Q and K splits, computed in a child process with the variable set and here without."""
+attention's Q, K and V splits, computed in a child process with the variable set and here without."""
 import os
 import subprocess
 import sys
