@@ -1057,9 +1057,12 @@ int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_
         TimedLaunch timed(stream);
         g_launches.fetch_add(1);
         if (vec) {
-            const int64_t warps = (rows + mfk::kGemvRowsPerWarp - 1) / mfk::kGemvRowsPerWarp;
-            const int64_t blocks = (warps * 32 + mfk::kGemvThreads - 1) / mfk::kGemvThreads;
-            if (blocks > INT32_MAX) return MFK_ERR_UNSUPPORTED;
+            // warps walk the rows with a grid stride: enough blocks to fill every SM, never
+            // more warps than rows
+            const int64_t warps_per_block = mfk::kGemvThreads / 32;
+            const int64_t blocks = std::min<int64_t>(
+                (rows + warps_per_block - 1) / warps_per_block,
+                static_cast<int64_t>(info->sm_count) * mfk::kGemvBlocksPerSm);
             mfk::gemv_n_vec4_kernel<<<static_cast<unsigned>(blocks), mfk::kGemvThreads, 0,
                                       stream>>>(a, rows, cols, lda, x, alpha, beta, y0, y);
         } else {

@@ -330,6 +330,30 @@ def test_gemv(cuda):
     no_fault()
 
 
+@pytest.mark.parametrize("rows,cols,width", [
+    (1, 1024, 1024),       # one row: a single warp
+    (3, 1001, 1004),       # a column slice: lda 1004, one element past the last 16-byte chunk
+    (77, 1280, 1280),      # one full round of eight loads per lane, then single chunks
+    (9473, 515, 520),      # more rows than warps in flight; 3 elements past the chunks
+    (20000, 8195, 8200),   # long rows with a ragged end, rows revisited by the grid stride
+])
+def test_gemv_ragged_rows_and_widths(cuda, rows, cols, width):
+    """The streaming gemv on row counts around its grid of warps and on widths that end inside
+    a round of loads or past the last 16-byte chunk (row-strided views: lda > cols), against the
+    oracle's double accumulation (equal after rounding to float, 1 ulp allowed)."""
+    rng = np.random.default_rng(rows + cols)
+    full = rng.standard_normal((rows, width)).astype(np.float32)
+    a = full[:, :cols]
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = rng.standard_normal(rows).astype(np.float32)
+    da = dev(full, cuda)[:, :cols]
+    got = host(mf.gemv(da, dev(x, cuda), -0.5, dev(y, cuda), 2.0))
+    want = O.gemv(a, x, -0.5, y, 2.0)
+    assert np.max(np.abs(got.view(np.int32).astype(np.int64) -
+                         want.view(np.int32).astype(np.int64))) <= 1
+    no_fault()
+
+
 def test_bias_add_and_activations(cuda):
     s = seeded_inputs()
     g = golden("seeded_cases.npz")
