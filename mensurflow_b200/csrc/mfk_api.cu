@@ -379,10 +379,14 @@ int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode
             for (int64_t i = 0; i < batch && offs_aligned; ++i) offs_aligned = o.bl.offsets[i] % 4 == 0;
         }
         if (offs_aligned) {
-            const int64_t rows = o.rows * batch;  // one warp per row, eight per block
-            const int64_t blocks = std::min<int64_t>((rows + 7) / 8,
-                                                     static_cast<int64_t>(info->sm_count) * 8);
-            mfk::pack_kmajor_vec4_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            // one warp per row (the block scheduler balances them), a grid stride beyond 32
+            // blocks per SM
+            const int64_t rows = o.rows * batch;
+            const int64_t warps_per_block = mfk::kPackThreads / 32;
+            const int64_t blocks = std::min<int64_t>((rows + warps_per_block - 1) / warps_per_block,
+                                                     static_cast<int64_t>(info->sm_count) * 32);
+            mfk::pack_kmajor_vec4_kernel<<<static_cast<unsigned>(blocks), mfk::kPackThreads, 0,
+                                           stream>>>(
                 o.ptr, reinterpret_cast<const long long*>(o.dev_offsets), o.bl.stride, o.rs,
                 static_cast<int>(o.rows), static_cast<int>(k), static_cast<int>(Kp),
                 static_cast<int>(batch), o.hi, o.lo, mode, inf_word, inf_tag);
@@ -1057,8 +1061,8 @@ int mfk_gemv_f32(const float* a, int64_t rows, int64_t cols, int64_t lda, int32_
         TimedLaunch timed(stream);
         g_launches.fetch_add(1);
         if (vec) {
-            // warps walk the rows with a grid stride: enough blocks to fill every SM, never
-            // more warps than rows
+            // one warp per row (the block scheduler balances them), a grid stride beyond
+            // kGemvBlocksPerSm blocks per SM
             const int64_t warps_per_block = mfk::kGemvThreads / 32;
             const int64_t blocks = std::min<int64_t>(
                 (rows + warps_per_block - 1) / warps_per_block,

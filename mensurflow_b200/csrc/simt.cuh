@@ -15,7 +15,7 @@ namespace mfk {
 // so a warp reads 512 contiguous bytes per load instruction.
 
 constexpr int kGemvThreads = 256;
-constexpr int kGemvBlocksPerSm = 8;  // launched per SM (four resident at 64 registers)
+constexpr int kGemvBlocksPerSm = 32;  // at most, launched per SM (four resident at 64 registers)
 constexpr int kGemvLoads = 8;        // 16-byte loads of A in flight per lane
 
 __device__ __forceinline__ double warp_sum(double v) {
@@ -44,10 +44,11 @@ __device__ __forceinline__ double dot4_f64(float4 v, float4 w) {
     return (double)v.x * w.x + (double)v.y * w.y + (double)v.z * w.z + (double)v.w * w.w;
 }
 
-// Warps walk the rows with a grid stride (kGemvBlocksPerSm blocks per SM, so every warp streams
-// several rows back to back); a lane keeps kGemvLoads 16-byte loads of its row in flight and
-// sums their products on four double chains. Against one row per warp with four loads in flight
-// it measured 6.57 against 6.0-6.2 TB/s at 65536 x 8192 (event-timed, one B200).
+// One warp per row where the grid allows (the block scheduler then balances the rows; a grid
+// stride beyond kGemvBlocksPerSm blocks per SM); a lane keeps kGemvLoads 16-byte loads of its
+// row in flight and sums their products on four double chains. At 65536 x 8192 in a probe of
+// back-to-back launches on one B200: 6.87 TB/s, against 6.72 with 8 blocks per SM walking ~7
+// rows per warp and 5.3 for two rows per warp with four loads in flight.
 __global__ void __launch_bounds__(kGemvThreads, 4) gemv_n_vec4_kernel(
     const float* __restrict__ a, long long rows, long long cols, long long lda,
     const float* __restrict__ x, float alpha, float beta, const float* __restrict__ y0,
