@@ -1418,8 +1418,10 @@ int mfk_strided_copy_f32(const float* x, const int64_t* shape, const int64_t* st
     } else {
         bool vec4 = v.stride[n - 1] == 1 && L % 4 == 0 && aligned16(x) && aligned16(out);
         for (int d = 0; d + 1 < n; ++d) vec4 = vec4 && v.stride[d] % 4 == 0;
+        // one warp per piece where the grid allows: the block scheduler balances them
         const int64_t pieces = (L + mfk::kCopyPiece - 1) / mfk::kCopyPiece;
-        const int64_t blocks = std::min<int64_t>((rows * pieces * 32 + 255) / 256, max_blocks);
+        const int64_t blocks = std::min<int64_t>((rows * pieces * 32 + 255) / 256,
+                                                 int64_t(info->sm_count) * 32);
         if (vec4) {
             mfk::copy_rows_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
                 x, out, v, rows);

@@ -66,8 +66,10 @@ __device__ __forceinline__ long long row_offset(const CopyView& v, long long row
 // One warp per piece of an output row: a row of L = shape[ndim-1] elements is cut into pieces of
 // kCopyPiece elements, so a view that merged into a few long rows (a stepped slice of a whole
 // matrix is one evenly strided run) still spreads over every SM. VEC4: L % 4 == 0, input stride
-// 1, every row start 16-byte aligned on both sides.
+// 1, every row start 16-byte aligned on both sides. Launched with one piece per warp where the
+// grid allows (a grid stride beyond that), so the block scheduler balances the pieces.
 constexpr long long kCopyPiece = 4096;
+constexpr int kCopyLoads = 8;
 
 template <bool VEC4>
 __global__ void __launch_bounds__(256) copy_rows_kernel(const float* __restrict__ x,
@@ -86,22 +88,22 @@ __global__ void __launch_bounds__(256) copy_rows_kernel(const float* __restrict_
         const long long len = min(kCopyPiece, L - j0);
         const float* src = x + row_offset(v, row) + j0 * sl;
         float* dst = out + row * L + j0;
-        // four loads in flight per lane before their stores
         if (VEC4) {
+            // kCopyLoads 16-byte loads in flight per lane before their stores
             const float4* s4 = reinterpret_cast<const float4*>(src);
             float4* d4 = reinterpret_cast<float4*>(dst);
             const long long L4 = len / 4;
             long long j = lane;
-            for (; j + 96 < L4; j += 128) {
-                const float4 a = __ldcs(s4 + j), b = __ldcs(s4 + j + 32);
-                const float4 c = __ldcs(s4 + j + 64), d = __ldcs(s4 + j + 96);
-                __stcs(d4 + j, a);
-                __stcs(d4 + j + 32, b);
-                __stcs(d4 + j + 64, c);
-                __stcs(d4 + j + 96, d);
+            for (; j + 32 * (kCopyLoads - 1) < L4; j += 32 * kCopyLoads) {
+                float4 t[kCopyLoads];
+#pragma unroll
+                for (int u = 0; u < kCopyLoads; ++u) t[u] = __ldcs(s4 + j + 32 * u);
+#pragma unroll
+                for (int u = 0; u < kCopyLoads; ++u) __stcs(d4 + j + 32 * u, t[u]);
             }
             for (; j < L4; j += 32) __stcs(d4 + j, __ldcs(s4 + j));
         } else {
+            // four loads in flight per lane before their stores
             long long j = lane;
             for (; j + 96 < len; j += 128) {
                 const float a = src[j * sl], b = src[(j + 32) * sl];
