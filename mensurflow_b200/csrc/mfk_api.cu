@@ -396,6 +396,20 @@ int launch_pack(const Operand& o, int64_t k, int64_t Kp, int64_t batch, int mode
         }
     }
     const int p_contig = (o.cs == 1) || (o.rs != 1 && std::llabs(o.cs) <= std::llabs(o.rs));
+    if (!p_contig) {
+        // rows run along memory: 64 x 64 tiles turned through shared memory, one per block
+        // where the grid allows
+        const int64_t tiles = (o.rows + mfk::kPackTile - 1) / mfk::kPackTile *
+                              ((Kp + mfk::kPackTile - 1) / mfk::kPackTile) * batch;
+        const int64_t blocks = std::min<int64_t>(tiles, static_cast<int64_t>(info->sm_count) * 32);
+        mfk::pack_transpose_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            o.ptr, reinterpret_cast<const long long*>(o.dev_offsets), o.bl.stride, o.rs, o.cs,
+            static_cast<int>(o.rows), static_cast<int>(k), static_cast<int>(Kp),
+            static_cast<int>(batch), o.hi, o.lo, mode, inf_word, inf_tag);
+        g_launches.fetch_add(1);
+        MFK_CUDA(cudaGetLastError());
+        return MFK_OK;
+    }
     if (o.rows > 65535LL * 32) return MFK_ERR_UNSUPPORTED;
     for (int64_t z0 = 0; z0 < batch; z0 += 65535) {
         const int64_t nz = std::min<int64_t>(65535, batch - z0);

@@ -73,6 +73,79 @@ __global__ void __launch_bounds__(256) pack_kmajor_kernel(
     }
 }
 
+// The transposing pass for an operand whose rows run along memory (op(X)(r, p) with |rs| < |cs|,
+// e.g. B [K, N] row-major read as N rows of K): 64 x 64 tiles of (r, p), one per block where the
+// grid allows. Each thread issues its 16 loads of a tile (coalesced along r) before it stores
+// any, the tile is turned through shared memory, and the rows of hi / lo are written along p
+// (coalesced). Tiles are numbered over [batch][R / 64][Kp / 64]; the columns K..Kp-1 are written
+// as zeros. On the transposed 1024 x 4096 and 4096 x 1024 weights of C3 and the 8192 x 32768 B of
+// C5 this replaces 32 x 32 tiles with four loads per thread, which left a pass latency-bound.
+constexpr int kPackTile = 64;
+
+__global__ void __launch_bounds__(256) pack_transpose_kernel(
+    const float* __restrict__ x, const long long* __restrict__ offsets, long long bstride,
+    long long rs, long long cs, int R, int K, int Kp, int batch, float* __restrict__ hi,
+    float* __restrict__ lo, int mode, unsigned* inf_word, unsigned inf_tag) {
+    __shared__ float tile[kPackTile][kPackTile + 1];  // [p - p0][r - r0]
+    const long long tiles_r = (R + kPackTile - 1) / kPackTile;
+    const long long tiles_p = (Kp + kPackTile - 1) / kPackTile;
+    const long long per_batch = tiles_r * tiles_p;
+    const long long total = per_batch * batch;
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+    bool inf = false;  // this thread has met an infinity
+    for (long long t = blockIdx.x; t < total; t += gridDim.x) {
+        const long long b = t / per_batch;
+        const long long rem = t - b * per_batch;
+        const long long tr = rem / tiles_p;
+        const int r0 = static_cast<int>(tr * kPackTile);
+        const int p0 = static_cast<int>((rem - tr * tiles_p) * kPackTile);
+        const float* xb = x + (offsets ? offsets[b] : b * bstride);
+        float vals[8][2];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+            for (int ii = 0; ii < 2; ++ii) {
+                const int r = r0 + tx + 32 * ii, p = p0 + ty + 8 * jj;
+                vals[jj][ii] = (r < R && p < K)
+                                   ? __ldcs(xb + static_cast<long long>(r) * rs +
+                                            static_cast<long long>(p) * cs)
+                                   : 0.0f;
+            }
+        }
+        __syncthreads();  // the previous tile's reads of `tile` are done
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+            for (int ii = 0; ii < 2; ++ii) tile[ty + 8 * jj][tx + 32 * ii] = vals[jj][ii];
+        }
+        __syncthreads();
+        const long long out_base = b * R * static_cast<long long>(Kp);
+#pragma unroll
+        for (int ii = 0; ii < 8; ++ii) {
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                const int r = r0 + ty + 8 * ii, p = p0 + tx + 32 * jj;
+                if (r < R && p < Kp) {
+                    const float v = tile[tx + 32 * jj][ty + 8 * ii];
+                    const long long o = out_base + static_cast<long long>(r) * Kp + p;
+                    if (mode == kPackCopy) {
+                        hi[o] = v;
+                    } else if (mode == kPackRound) {
+                        hi[o] = round_tf32(v);
+                    } else {
+                        float h, l;
+                        split_tf32(v, h, l);
+                        hi[o] = h;
+                        lo[o] = l;
+                        inf |= fabsf(v) == __int_as_float(0x7f800000);
+                    }
+                }
+            }
+        }
+    }
+    if (inf && inf_word != nullptr) *inf_word = inf_tag;
+}
+
 // The same pass for an operand that is already K-major with 16-byte aligned rows and K % 4 == 0
 // (the common case: A row-major, or B read transposed): no transpose needed, so each float4 goes
 // straight through, coalesced on both sides. One warp per output row (grid-stride over the
