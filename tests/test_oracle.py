@@ -197,3 +197,18 @@ def test_restatement_matches_reference_on_infinite_operands(shape):
     assert (~np.isfinite(want)).any()
     np.testing.assert_array_equal(np.isnan(got), np.isnan(want))
     np.testing.assert_array_equal(got[~np.isnan(want)], want[~np.isnan(want)])
+
+
+@pytest.mark.skipif(O.reference() is None, reason="reference library not built here")
+@pytest.mark.parametrize("rows,cols", [(1, 1024), (3, 1001), (77, 1280), (513, 515), (64, 8195)])
+def test_gemv_restatement_matches_reference_on_ragged_widths(rows, cols):
+    """The gemv restatement against the reference's own gemv (double accumulation in row order,
+    src/backends/cpu/ops/blas/blas.cpp:55-80) on the widths the GPU gemv tests use: equal after
+    rounding to float, 1 ulp allowed for the summation order."""
+    rng = np.random.default_rng(rows * 31 + cols)
+    a = rng.standard_normal((rows, cols)).astype(np.float32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = rng.standard_normal(rows).astype(np.float32)
+    got = O.gemv(a, x, -0.5, y, 2.0)
+    want = O.ref_gemv(a, x, -0.5, y, 2.0)
+    assert np.max(ulp_diff(got, want)) <= 1
